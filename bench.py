@@ -1,0 +1,350 @@
+"""Benchmark of the MoE quantized-expert layer.
+
+Workload: one MoE layer at Qwen3-30B-A3B shape -- hidden 2048, 128 experts,
+top-8, moe_intermediate 768, SwiGLU, q4_0 experts from N(0, 0.02), f32
+router N(0, 0.02), x ~ N(0, 1) -- over a batch of M decode tokens per GPU
+(default M=64; --tokens). A step is one hale_moe_forward over the batch.
+Metric: decode tokens/s through the layer (BASELINE: "decode tok/s ...;
+q4_0 MoE GEMV achieved HBM GB/s").
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M]
+  python bench.py --impl reference ...   # the reference's CPU path (oracle port)
+
+Multi-GPU (torchrun): each rank runs its own batch against its own copy of
+the layer (per-GPU work fixed -> weak scaling); the step time is the max
+over ranks.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+SEED = 2026
+E, H, I, K_TOP = 128, 2048, 768, 8
+WORKLOAD = "moe_layer_qwen3_30b_a3b_q4_0"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--impl", default="hale", choices=["hale", "reference"])
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def config(m, n):
+    return {"workload": WORKLOAD, "hidden": H, "experts": E, "top_k": K_TOP,
+            "moe_intermediate": I, "expert_dtype": "q4_0", "router_dtype": "f32",
+            "tokens_per_gpu": m, "global_batch": m * n, "parallelism": f"dp{n} (experts replicated per GPU)",
+            "inputs": "seeded synthetic: weights N(0,0.02), x N(0,1)",
+            "l2": "flushed between timed steps (256 MiB write, untimed)"}
+
+
+# ---------------------------------------------------------------------------
+# host data
+# ---------------------------------------------------------------------------
+def make_layer(fmt):
+    return fmt.SyntheticLayer(SEED, E, H, I, fmt.Q4_0)
+
+
+def encode_all(ld):
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(min(16, os.cpu_count() or 4)) as ex:
+        return list(ex.map(ld.expert_encoded, range(E)))
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def oracle_tok_s(ld, encoded, m, budget_s=8.0):
+    """The oracle (C restatement of the reference CPU path, OpenMP over rows
+    like rayon) on a bounded sample of the same tokens -> tokens/s."""
+    from oracle import oracle as O
+    fmt = __import__("importlib").import_module("hale-token_b200.formats")
+    experts = [O.ExpertWeights(fmt.Q4_0, H, I, *encoded[e]) for e in range(E)]
+    renc = fmt.encode(fmt.F32, ld.router)
+    x = ld.tokens(m)
+    O.moe_forward(fmt.F32, renc, experts, K_TOP, True, x[:1], native=True)  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while True:
+        take = min(m, 8)
+        O.moe_forward(fmt.F32, renc, experts, K_TOP, True, x[:take], native=True)
+        done += take
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt, O.num_threads(native=True)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device, self.rows, self.proc = device, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        reasons = set()
+        sm = []
+        smax = None
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    fmt = __import__("importlib").import_module("hale-token_b200.formats")
+    ld = make_layer(fmt)
+    encoded = encode_all(ld)
+    m = args.tokens
+    vals = []
+    for _ in range(args.warmup):
+        oracle_tok_s(ld, encoded, m, budget_s=0.5)
+    for _ in range(args.steps):
+        v, done, dt, cores = oracle_tok_s(ld, encoded, m, budget_s=2.0)
+        vals.append(v)
+    v = float(np.median(vals))
+    ms = m / v * 1e3
+    line = {
+        "metric": "decode_tok_s_moe_layer", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights x i8 activations, f32 accumulate",
+        "data": "synthetic", "config": config(m, 1), "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"each step: >=2 s of the layer over up to 8 of the {m} tokens, repeated; "
+                                   f"oracle/hale_oracle.c -O2 -march=native, OpenMP {cores} threads on {cpu_model()}"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "Rust reference cannot be built here (no cargo); the C restatement of its CPU path stands in",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    hale = importlib.import_module("hale-token_b200")
+    fmt = importlib.import_module("hale-token_b200.formats")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ctx = hale.Context(local)
+    ld = make_layer(fmt)
+    encoded = encode_all(ld)
+    pool = hale.Pool(ctx, fmt.Q4_0, H, I, 1, E)
+    for e in range(E):
+        pool.upload(0, e, fmt.pack_record(*encoded[e]))
+    router = torch.from_numpy(fmt.encode(fmt.F32, ld.router)).cuda()
+    layer = hale.moe_layer(0, router, fmt.F32, E, K_TOP, True)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def measure(m, steps, warmup, with_profile=False):
+        x = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).cuda()
+        out = torch.empty((m, H), dtype=torch.float32, device="cuda")
+        idx = torch.empty((m, K_TOP), dtype=torch.int32, device="cuda")
+        for _ in range(warmup):
+            hale.moe_forward(ctx, pool, layer, x, out, idx)
+        ctx.check()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        launches0 = ctx.launches
+        barrier()
+        torch.cuda.synchronize()
+        if with_profile:
+            ctx.profile(True)
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            hale.moe_forward(ctx, pool, layer, x, out, idx)
+            b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        prof = {}
+        if with_profile:
+            ctx.profile(False)
+            for kname in ("router", "expert_gate_up", "expert_down"):
+                prof[kname] = ctx.profile_read(kname)
+        ctx.check()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+        distinct = int(np.unique(idx.cpu().numpy()).size)
+        return ms, prof, ctx.launches - launches0, distinct
+
+    m = args.tokens
+    # ---- headline ----------------------------------------------------------
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ms, prof, launches, distinct = measure(m, args.steps, max(args.warmup, 3), with_profile=True)
+    clk = clocks.stop()
+    ms_max = max_over_ranks(ms)
+    value = world * m / (ms_max / 1e3)
+
+    # ---- roofline of the dominant kernel (gate/up GEMV) --------------------
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak_gbs = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    q4_row = fmt.row_bytes(fmt.Q4_0, H)
+    gate_up_bytes = distinct * 2 * I * q4_row                 # weights of the touched experts
+    gate_up_bytes += m * H + m * (H // 32) * 8               # quantized activations read
+    n_gu, t_gu = prof.get("expert_gate_up", (0, 0.0))
+    gu_ms = t_gu / max(n_gu, 1)
+    achieved = gate_up_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else None
+    layer_bytes = distinct * fmt.row_bytes(fmt.Q4_0, H) * 2 * I + distinct * H * fmt.row_bytes(fmt.Q4_0, I)
+    layer_bytes += E * H * 4 + 2 * m * H * 4
+    roofline = {"bound": "hbm", "kernel": "expert_gate_up", "achieved": achieved, "peak": peak_gbs,
+                "unit": "GB/s", "frac": (achieved / peak_gbs) if achieved else None, "traffic": None,
+                "peak_source": peak_src, "algorithmic_bytes_per_launch": gate_up_bytes,
+                "avg_launch_ms": gu_ms, "distinct_experts": distinct,
+                "layer": {"algorithmic_bytes": layer_bytes, "ms": ms,
+                          "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
+                          "frac": layer_bytes / (ms / 1e3) / 1e9 / peak_gbs}}
+    kern = {k: {"launches": n, "avg_ms": (t / n if n else None)} for k, (n, t) in prof.items()}
+
+    # ---- end to end through the public host-buffer call ---------------------
+    xh = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).pin_memory()
+    oh = torch.empty((m, H), dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        hale.moe_forward_host(ctx, pool, layer, xh, oh)
+    barrier()
+    e2e_t = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        hale.moe_forward_host(ctx, pool, layer, xh, oh)   # H2D, layer, D2H, sync
+        e2e_t.append(time.perf_counter() - t0)
+    barrier()
+    e2e_s = max_over_ranks(float(np.mean(e2e_t)))
+    e2e = {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": m * H * 4,
+           "d2h_bytes_per_step": m * H * 4, "ms_per_step": e2e_s * 1e3,
+           "timing": "host wall clock around hale_moe_forward_host (pinned buffers), max over ranks"}
+
+    # ---- sweep of the other config-1 batch sizes ----------------------------
+    sweep = {}
+    if not args.no_sweep:
+        for mm in (1, 8, 64, 512):
+            s_ms, _, _, s_distinct = measure(mm, max(5, args.steps // 2), 3)
+            s_ms = max_over_ranks(s_ms)
+            lb = s_distinct * (2 * I * q4_row + H * fmt.row_bytes(fmt.Q4_0, I)) + E * H * 4 + 2 * mm * H * 4
+            sweep[str(mm)] = {"ms_per_step": s_ms, "tok_s": world * mm / (s_ms / 1e3),
+                              "distinct_experts": s_distinct,
+                              "layer_hbm_gbs": lb / (s_ms / 1e3) / 1e9}
+
+    # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, done, dt, cores = oracle_tok_s(ld, encoded, m, budget_s=10.0)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{done} tokens of the same layer in {dt:.1f} s (batches of 8); "
+                         f"oracle/hale_oracle.c -O2 -march=native, OpenMP {cores} threads, {cpu_model()}"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode_tok_s_moe_layer", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_0 weights x i8 activations, int32 block dots, f32 accumulate",
+            "data": "synthetic", "config": config(m, world), "roofline": roofline,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "kernels": kern,
+            "clocks": clk, "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

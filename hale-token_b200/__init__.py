@@ -1,0 +1,311 @@
+"""hale-token_b200: B200 (sm_100a) implementation of Hale-Token's MoE
+quantized-expert forward and sampling tail, behind a C ABI.
+
+The product is libhale_cuda.so (csrc/, declared in include/hale_cuda.h).
+This module is a thin ctypes binding of that ABI -- the same calls a Rust
+host would make through `extern "C"` -- plus helpers that pass torch device
+tensors as raw pointers. There is no CPU fallback: importing this package
+without the built library raises.
+
+Because the directory name contains a dash, import it with
+``importlib.import_module("hale-token_b200")``.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libhale_cuda.so")
+
+# status codes (include/hale_cuda.h)
+OK = 0
+E_INVALID_ARGUMENT = -1
+E_BAD_TENSOR = -2
+E_IO = -3
+E_CONTEXT_OVERFLOW = -4
+E_CUDA = -10
+E_NO_DEVICE = -11
+E_OUT_OF_MEMORY = -12
+E_TIMEOUT = -13
+E_DEVICE_CHECK = -14
+E_UNSUPPORTED = -15
+
+F32, F16, BF16, Q8_0, Q4_0 = 0, 1, 2, 3, 4
+
+# Every function the header declares, with its ctypes signature.
+P = C.c_void_p
+U32, I32, U64, I64, SZ = C.c_uint32, C.c_int32, C.c_uint64, C.c_int64, C.c_size_t
+
+
+class CacheStats(C.Structure):
+    _fields_ = [("pinned_hits", U64), ("lru_hits", U64), ("misses", U64), ("bytes_loaded", U64),
+                ("load_seconds", C.c_double), ("pinned_experts", U64), ("pinned_bytes", U64),
+                ("lru_experts", U64), ("lru_bytes", U64), ("lru_capacity_bytes", U64),
+                ("passthrough", I32)]
+
+
+class ExpertKey(C.Structure):
+    _fields_ = [("layer", U32), ("expert", U32)]
+
+
+class ExpertView(C.Structure):
+    _fields_ = [("gate", P), ("up", P), ("down", P)]
+
+
+class MoeLayer(C.Structure):
+    _fields_ = [("layer", U32), ("router", P), ("router_dtype", C.c_int), ("n_experts", U32),
+                ("top_k", U32), ("normalize_topk", I32)]
+
+
+class SamplingParams(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", U32),
+                ("repetition_penalty", C.c_float)]
+
+
+SIGNATURES = {
+    "hale_ctx_create": (I32, [C.c_int, C.POINTER(P)]),
+    "hale_ctx_destroy": (None, [P]),
+    "hale_last_error": (I32, [P, C.c_char_p, SZ]),
+    "hale_ctx_check": (I32, [P, P]),
+    "hale_ctx_launch_count": (U64, [P]),
+    "hale_ctx_profile": (I32, [P, C.c_int]),
+    "hale_ctx_profile_read": (I32, [P, C.c_char_p, C.POINTER(U64), C.POINTER(C.c_double)]),
+    "hale_row_bytes": (I64, [C.c_int, U64]),
+    "hale_matrix_create": (I32, [P, C.c_int, U32, U32, P, U64, C.c_int, C.POINTER(P)]),
+    "hale_matrix_destroy": (None, [P]),
+    "hale_matrix_matvec": (I32, [P, P, P, U32, P, P, P]),
+    "hale_matrix_matvec_q8": (I32, [P, P, P, P, U32, P, P, P]),
+    "hale_quantize_q8": (I32, [P, P, U32, U32, P, P, P]),
+    "hale_pool_create": (I32, [P, C.c_int, U32, U32, U32, U32, C.POINTER(P)]),
+    "hale_pool_destroy": (None, [P]),
+    "hale_pool_upload_expert": (I32, [P, U32, U32, P, U64, C.c_int, P]),
+    "hale_pool_fetch": (I32, [P, P, U64, P]),
+    "hale_pool_stats": (I32, [P, C.POINTER(CacheStats)]),
+    "hale_pool_routing_counts": (I32, [P, P, U64]),
+    "hale_pool_expert_bytes": (U64, [P]),
+    "hale_moe_forward": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
+    "hale_moe_forward_host": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
+    "hale_moe_route": (I32, [P, C.POINTER(MoeLayer), U32, P, U32, P, P, P, P]),
+    "hale_lm_head": (I32, [P, P, P, U32, P, P]),
+    "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
+    "hale_expf_host": (None, [P, P, U64]),
+}
+
+_lib = None
+
+
+def lib():
+    """Loads libhale_cuda.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run __graft_entry__.build() "
+                              "or `python hale-token_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+class HaleError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"[{status}] {message}")
+        self.status = status
+
+
+def _check(status, ctx=None):
+    if status != OK:
+        buf = C.create_string_buffer(512)
+        lib().hale_last_error(ctx, buf, 512)
+        raise HaleError(status, buf.value.decode(errors="replace"))
+
+
+def ptr(t):
+    """Raw device/host address of a torch tensor or numpy array (or None)."""
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return C.c_void_p(t.data_ptr())
+    return C.c_void_p(t.ctypes.data)
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if isinstance(stream, int):
+        return C.c_void_p(stream)
+    return C.c_void_p(stream.cuda_stream)
+
+
+class Context:
+    """hale_ctx: one GPU and its workspace."""
+
+    def __init__(self, device=0):
+        h = P()
+        _check(lib().hale_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            lib().hale_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, stream=None):
+        _check(lib().hale_ctx_check(self.h, _stream(stream)), self.h)
+
+    @property
+    def launches(self):
+        return lib().hale_ctx_launch_count(self.h)
+
+    def profile(self, enable=True):
+        """Per-kernel CUDA-event timing of this library's launches."""
+        self.call("hale_ctx_profile", self.h, int(enable))
+
+    def profile_read(self, kernel):
+        """(launches, total device ms) for a kernel family since the last read."""
+        n, ms = U64(), C.c_double()
+        self.call("hale_ctx_profile_read", self.h, kernel.encode(), C.byref(n), C.byref(ms))
+        return n.value, ms.value
+
+    def call(self, fn, *args):
+        _check(getattr(lib(), fn)(*args), self.h)
+
+
+class Matrix:
+    """hale_matrix: WeightMatrix::new over reference-encoded rows."""
+
+    def __init__(self, ctx, dtype, rows, cols, encoded):
+        """`encoded`: numpy uint8 [rows, row_bytes] (host) or torch uint8 tensor (device)."""
+        h = P()
+        on_dev = hasattr(encoded, "is_cuda") and encoded.is_cuda
+        nbytes = encoded.numel() if hasattr(encoded, "numel") else encoded.nbytes
+        ctx.call("hale_matrix_create", ctx.h, dtype, rows, cols, ptr(encoded), nbytes, int(on_dev),
+                 C.byref(h))
+        self.ctx, self.h, self.dtype, self.rows, self.cols = ctx, h, dtype, rows, cols
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().hale_matrix_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    def matvec(self, x, out, block_sums=None, stream=None):
+        self.ctx.call("hale_matrix_matvec", self.ctx.h, self.h, ptr(x), x.shape[0], ptr(out),
+                      ptr(block_sums), _stream(stream))
+
+    def matvec_q8(self, scales, quants, out, block_sums=None, stream=None):
+        self.ctx.call("hale_matrix_matvec_q8", self.ctx.h, self.h, ptr(scales), ptr(quants),
+                      quants.shape[0], ptr(out), ptr(block_sums), _stream(stream))
+
+    def lm_head(self, hidden, logits, stream=None):
+        self.ctx.call("hale_lm_head", self.ctx.h, self.h, ptr(hidden), hidden.shape[0],
+                      ptr(logits), _stream(stream))
+
+
+class Pool:
+    """hale_pool: HBM-resident ExpertProvider."""
+
+    def __init__(self, ctx, dtype, hidden, inter, n_layers, n_experts):
+        h = P()
+        ctx.call("hale_pool_create", ctx.h, dtype, hidden, inter, n_layers, n_experts, C.byref(h))
+        self.ctx, self.h = ctx, h
+        self.dtype, self.hidden, self.inter, self.n_layers, self.n_experts = (
+            dtype, hidden, inter, n_layers, n_experts)
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().hale_pool_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    @property
+    def expert_bytes(self):
+        return lib().hale_pool_expert_bytes(self.h)
+
+    def upload(self, layer, expert, record, stream=None):
+        on_dev = hasattr(record, "is_cuda") and record.is_cuda
+        nbytes = record.numel() if hasattr(record, "numel") else record.nbytes
+        self.ctx.call("hale_pool_upload_expert", self.h, layer, expert, ptr(record), nbytes,
+                      int(on_dev), _stream(stream))
+
+    def fetch(self, keys):
+        arr = (ExpertKey * len(keys))(*[ExpertKey(l, e) for l, e in keys])
+        out = (ExpertView * len(keys))()
+        self.ctx.call("hale_pool_fetch", self.h, C.cast(arr, P), len(keys), C.cast(out, P))
+        return [(v.gate, v.up, v.down) for v in out]
+
+    def stats(self):
+        s = CacheStats()
+        self.ctx.call("hale_pool_stats", self.h, C.byref(s))
+        return s
+
+    def routing_counts(self):
+        import numpy as np
+        n = self.n_layers * self.n_experts
+        out = np.zeros(n, dtype=np.uint64)
+        self.ctx.call("hale_pool_routing_counts", self.h, ptr(out), n)
+        return out.reshape(self.n_layers, self.n_experts)
+
+
+def moe_layer(layer, router, router_dtype, n_experts, top_k, normalize):
+    """hale_moe_layer for a device router tensor; the returned struct keeps
+    the tensor alive (the C side only stores its address)."""
+    ly = MoeLayer(layer, ptr(router).value if router is not None else None, router_dtype,
+                  n_experts, top_k, int(normalize))
+    ly._router_ref = router
+    return ly
+
+
+def moe_forward(ctx, pool, layer, x, out, topk_idx=None, topk_w=None, stream=None):
+    ctx.call("hale_moe_forward", ctx.h, pool.h, C.byref(layer), ptr(x), x.shape[0], ptr(out),
+             ptr(topk_idx), ptr(topk_w), _stream(stream))
+
+
+def moe_forward_host(ctx, pool, layer, x, out, topk_idx=None, topk_w=None, stream=None):
+    ctx.call("hale_moe_forward_host", ctx.h, pool.h, C.byref(layer), ptr(x), x.shape[0],
+             ptr(out), ptr(topk_idx), ptr(topk_w), _stream(stream))
+
+
+def moe_route(ctx, layer, hidden, x, topk_idx, topk_w, probs=None, stream=None):
+    ctx.call("hale_moe_route", ctx.h, C.byref(layer), hidden, ptr(x), x.shape[0], ptr(topk_idx),
+             ptr(topk_w), ptr(probs), _stream(stream))
+
+
+def quantize_q8(ctx, x, scales, quants, stream=None):
+    ctx.call("hale_quantize_q8", ctx.h, ptr(x), x.shape[0], x.shape[1], ptr(scales),
+             ptr(quants), _stream(stream))
+
+
+def sample(ctx, logits, params, rng_state, out_tokens, seen_ids=None, stream=None):
+    n_seen = seen_ids.shape[1] if seen_ids is not None else 0
+    ctx.call("hale_sample", ctx.h, ptr(logits), logits.shape[0], logits.shape[1],
+             C.byref(params), ptr(rng_state), ptr(seen_ids), n_seen, ptr(out_tokens),
+             _stream(stream))
+
+
+def row_bytes(dtype, cols):
+    r = lib().hale_row_bytes(dtype, cols)
+    return None if r < 0 else int(r)
+
+
+def expf_host(x):
+    """The device exp evaluated on the host (same source)."""
+    import numpy as np
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().hale_expf_host(ptr(x), ptr(y), x.size)
+    return y

@@ -1,0 +1,960 @@
+// hale_cuda.cu -- C ABI (include/hale_cuda.h) over the sm_100a kernels.
+//
+// Host orchestration only: argument checks mirroring the reference's
+// assertions and HaleError cases, workspace management, and launches. The
+// arithmetic lives in hale_kernels.cuh.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/hale_cuda.h"
+#include "hale_kernels.cuh"
+
+using namespace hale;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+namespace {
+thread_local std::string g_thread_msg;
+thread_local hale_status g_thread_status = HALE_OK;
+}  // namespace
+
+struct hale_ctx {
+    int device = 0;
+    int sm_count = 0;
+    std::string msg;
+    hale_status status = HALE_OK;
+    uint32_t* d_err = nullptr;
+    // MoE / route workspace (capacity-based layout; counters first)
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int capM = 0, capE = 0, capK = 0, capH = 0, capI = 0;
+    // scratch for unit-level calls
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    uint64_t launches = 0;
+    // per-kernel event timing (hale_ctx_profile)
+    bool profiling = false;
+    struct Mark {
+        std::string name;
+        cudaEvent_t a, b;
+    };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> spare;
+    std::map<std::string, std::pair<uint64_t, double>> totals;
+};
+
+struct hale_matrix {
+    hale_ctx* ctx;
+    hale_dtype dtype;
+    uint32_t rows, cols, rows_pad;
+    uint32_t nb;     // quantized: blocks per row; float: steps of 8
+    uint8_t* data;
+    size_t bytes;
+};
+
+struct hale_pool {
+    hale_ctx* ctx;
+    hale_dtype dtype;
+    uint32_t H, I, L, E;
+    size_t expert_stride;   // tiled bytes per expert
+    size_t record_bytes;    // reference pack record bytes per expert
+    uint8_t* data = nullptr;
+    uint8_t* staging = nullptr;
+    unsigned long long* d_routing = nullptr;  // [L * E]
+    std::vector<uint8_t> resident;             // [L * E]
+    std::vector<uint32_t> layer_resident;      // count per layer
+    std::vector<uint64_t> host_routing;        // fetch() records
+    hale_cache_stats stats{};
+};
+
+static hale_status fail(hale_ctx* ctx, hale_status st, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_thread_msg = buf;
+    g_thread_status = st;
+    if (ctx) {
+        ctx->msg = buf;
+        ctx->status = st;
+    }
+    return st;
+}
+
+#define CUDA_TRY(ctx, call)                                                                    \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail((ctx), e_ == cudaErrorMemoryAllocation ? HALE_E_OUT_OF_MEMORY : HALE_E_CUDA, \
+                        "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__);  \
+    } while (0)
+
+static hale_status check_launch(hale_ctx* ctx, const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(ctx, HALE_E_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
+    ctx->launches++;
+    return HALE_OK;
+}
+
+static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static cudaEvent_t take_event(hale_ctx* ctx) {
+    if (!ctx->spare.empty()) {
+        cudaEvent_t e = ctx->spare.back();
+        ctx->spare.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Brackets one launch with events when profiling is on.
+struct ProfScope {
+    hale_ctx* ctx;
+    const char* name;
+    cudaStream_t st;
+    cudaEvent_t a = nullptr;
+    ProfScope(hale_ctx* c, const char* n, cudaStream_t s) : ctx(c), name(n), st(s) {
+        if (ctx->profiling) {
+            a = take_event(ctx);
+            cudaEventRecord(a, st);
+        }
+    }
+    ~ProfScope() {
+        if (a) {
+            cudaEvent_t b = take_event(ctx);
+            cudaEventRecord(b, st);
+            ctx->marks.push_back({name, a, b});
+        }
+    }
+};
+
+static void drain_marks(hale_ctx* ctx) {
+    for (auto& m : ctx->marks) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(m.b) == cudaSuccess && cudaEventElapsedTime(&ms, m.a, m.b) == cudaSuccess) {
+            auto& t = ctx->totals[m.name];
+            t.first++;
+            t.second += ms;
+        }
+        ctx->spare.push_back(m.a);
+        ctx->spare.push_back(m.b);
+    }
+    ctx->marks.clear();
+    cudaGetLastError();
+}
+
+static bool stream_capturing(void* stream) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(S(stream), &cs) != cudaSuccess) return false;
+    return cs != cudaStreamCaptureStatusNone;
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static bool is_quant(hale_dtype d) { return d == HALE_Q8_0 || d == HALE_Q4_0; }
+static bool is_float(hale_dtype d) { return d == HALE_F32 || d == HALE_F16 || d == HALE_BF16; }
+static int block_len(hale_dtype d) { return is_quant(d) ? 32 : 1; }
+static int block_bytes(hale_dtype d) {
+    switch (d) {
+    case HALE_F32: return 4;
+    case HALE_F16:
+    case HALE_BF16: return 2;
+    case HALE_Q8_0: return 34;
+    case HALE_Q4_0: return 18;
+    }
+    return 0;
+}
+static int float_code(hale_dtype d) { return d == HALE_F32 ? 0 : (d == HALE_F16 ? 1 : 2); }
+
+extern "C" int64_t hale_row_bytes(hale_dtype dtype, uint64_t cols) {
+    int bb = block_bytes(dtype);
+    if (bb == 0) return -1;
+    uint64_t bl = (uint64_t)block_len(dtype);
+    if (cols % bl) return -1;
+    return (int64_t)(cols / bl * (uint64_t)bb);
+}
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+extern "C" hale_status hale_ctx_create(int device, hale_ctx** out) {
+    if (!out) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ctx_create: out is NULL");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(nullptr, HALE_E_NO_DEVICE, "no CUDA device is visible");
+    }
+    if (device < 0 || device >= n)
+        return fail(nullptr, HALE_E_INVALID_ARGUMENT, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+        return fail(nullptr, HALE_E_CUDA, "cudaGetDeviceProperties failed");
+    if (prop.major != 10)
+        return fail(nullptr, HALE_E_NO_DEVICE,
+                    "device %d is compute capability %d.%d; this library is built for sm_100a (B200)",
+                    device, prop.major, prop.minor);
+    hale_ctx* c = new hale_ctx();
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&c->d_err, 4) != cudaSuccess ||
+        cudaMemset(c->d_err, 0, 4) != cudaSuccess) {
+        delete c;
+        return fail(nullptr, HALE_E_CUDA, "context setup failed on device %d", device);
+    }
+    *out = c;
+    return HALE_OK;
+}
+
+extern "C" void hale_ctx_destroy(hale_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaFree(ctx->d_err);
+    cudaFree(ctx->ws);
+    cudaFree(ctx->scratch);
+    drain_marks(ctx);
+    for (cudaEvent_t e : ctx->spare) cudaEventDestroy(e);
+    delete ctx;
+}
+
+extern "C" hale_status hale_ctx_profile(hale_ctx* ctx, int enable) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ctx_profile: ctx is NULL");
+    ctx->profiling = enable != 0;
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_ctx_profile_read(hale_ctx* ctx, const char* kernel, uint64_t* launches,
+                                             double* total_ms) {
+    if (!ctx || !kernel) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ctx_profile_read: NULL argument");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    drain_marks(ctx);
+    auto it = ctx->totals.find(kernel);
+    uint64_t n = it == ctx->totals.end() ? 0 : it->second.first;
+    double ms = it == ctx->totals.end() ? 0.0 : it->second.second;
+    if (launches) *launches = n;
+    if (total_ms) *total_ms = ms;
+    if (it != ctx->totals.end()) ctx->totals.erase(it);
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_last_error(const hale_ctx* ctx, char* buf, size_t len) {
+    const std::string& m = ctx ? ctx->msg : g_thread_msg;
+    if (buf && len) {
+        size_t n = std::min(len - 1, m.size());
+        memcpy(buf, m.data(), n);
+        buf[n] = 0;
+    }
+    return ctx ? ctx->status : g_thread_status;
+}
+
+extern "C" uint64_t hale_ctx_launch_count(const hale_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+// Counter region of the MoE workspace (zero between calls).
+struct MoeLayout {
+    size_t tile_cnt, grid_cnt, gu_cnt, comb_cnt, counters_end;
+    size_t logits, topk_idx, topk_w, xq, xaux, elist_off, elist, active, n_active;
+    size_t gu, hq, haux, ybuf, total;
+};
+
+static MoeLayout moe_layout(int M, int E, int k, int H, int I) {
+    MoeLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = o;
+        o = align_up(o + bytes, 256);
+        return at;
+    };
+    L.tile_cnt = take((size_t)M * 4);
+    L.grid_cnt = take(4);
+    L.gu_cnt = take((size_t)E * std::max(I / 32, 1) * 4);
+    L.comb_cnt = take((size_t)M * std::max(H / 32, 1) * 4);
+    L.counters_end = o;
+    L.logits = take((size_t)M * E * 4);
+    L.topk_idx = take((size_t)M * k * 4);
+    L.topk_w = take((size_t)M * k * 4);
+    L.xq = take((size_t)M * H);
+    L.xaux = take((size_t)M * (H / 32) * 8);
+    L.elist_off = take((size_t)(E + 1) * 4);
+    L.elist = take((size_t)M * k * 4);
+    L.active = take((size_t)E * 4);
+    L.n_active = take(4);
+    L.gu = take((size_t)M * k * 2 * I * 4);
+    L.hq = take((size_t)M * k * I);
+    L.haux = take((size_t)M * k * (I / 32) * 8);
+    L.ybuf = take((size_t)M * k * H * 4);
+    L.total = o;
+    return L;
+}
+
+// Ensures the MoE workspace covers (M, E, k, H, I); the layout is computed
+// from the capacities so counters never move between calls.
+static hale_status ensure_moe_ws(hale_ctx* ctx, int M, int E, int k, int H, int I, void* stream,
+                                 MoeLayout* out) {
+    if (M <= ctx->capM && E <= ctx->capE && k <= ctx->capK && H <= ctx->capH && I <= ctx->capI && ctx->ws) {
+        *out = moe_layout(ctx->capM, ctx->capE, ctx->capK, ctx->capH, ctx->capI);
+        return HALE_OK;
+    }
+    if (stream_capturing(stream))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT,
+                    "workspace must grow (M=%d) while the stream is being captured; run one call "
+                    "of the largest shape before capturing", M);
+    int cM = std::max(M, ctx->capM), cE = std::max(E, ctx->capE), cK = std::max(k, ctx->capK);
+    int cH = std::max(H, ctx->capH), cI = std::max(I, ctx->capI);
+    MoeLayout L = moe_layout(cM, cE, cK, cH, cI);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    CUDA_TRY(ctx, cudaDeviceSynchronize());
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    CUDA_TRY(ctx, cudaMalloc(&ctx->ws, L.total));
+    CUDA_TRY(ctx, cudaMemset(ctx->ws, 0, L.total));
+    ctx->ws_bytes = L.total;
+    ctx->capM = cM; ctx->capE = cE; ctx->capK = cK; ctx->capH = cH; ctx->capI = cI;
+    *out = L;
+    return HALE_OK;
+}
+
+static hale_status ensure_scratch(hale_ctx* ctx, size_t bytes, void* stream) {
+    if (bytes <= ctx->scratch_bytes && ctx->scratch) return HALE_OK;
+    if (stream_capturing(stream))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "scratch must grow while the stream is being captured");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    CUDA_TRY(ctx, cudaDeviceSynchronize());
+    cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    size_t b = align_up(std::max(bytes, (size_t)1 << 20), 1 << 20);
+    CUDA_TRY(ctx, cudaMalloc(&ctx->scratch, b));
+    ctx->scratch_bytes = b;
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_ctx_check(hale_ctx* ctx, void* stream) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ctx_check: ctx is NULL");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    CUDA_TRY(ctx, cudaStreamSynchronize(S(stream)));
+    uint32_t err = 0;
+    CUDA_TRY(ctx, cudaMemcpy(&err, ctx->d_err, 4, cudaMemcpyDeviceToHost));
+    if (!err) return HALE_OK;
+    CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, 4));
+    if (ctx->ws) {  // a kernel stopped early: counters may be stale
+        MoeLayout L = moe_layout(ctx->capM, ctx->capE, ctx->capK, ctx->capH, ctx->capI);
+        CUDA_TRY(ctx, cudaMemset(ctx->ws, 0, L.counters_end));
+    }
+    if (err & kErrTimeout) return fail(ctx, HALE_E_TIMEOUT, "a device-side wait exceeded its bound");
+    return fail(ctx, HALE_E_DEVICE_CHECK, "a device-side bounds check failed (0x%x)", err);
+}
+
+// ---------------------------------------------------------------------------
+// repack launches
+// ---------------------------------------------------------------------------
+static hale_status launch_repack(hale_ctx* ctx, hale_dtype dt, const uint8_t* src, uint8_t* dst,
+                                 uint32_t rows, uint32_t cols, cudaStream_t st) {
+    uint32_t rows_pad = (rows + 31) / 32 * 32;
+    if (is_quant(dt)) {
+        int nb = (int)(cols / 32);
+        long long total = (long long)rows_pad * nb;
+        int bb = block_bytes(dt), qb = dt == HALE_Q4_0 ? 16 : 32;
+        repack_quant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, dst, (int)rows, (int)rows_pad, nb, bb, qb);
+    } else {
+        int steps = (int)((cols + 7) / 8);
+        long long total = (long long)rows_pad * steps;
+        repack_float_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, dst, (int)rows, (int)rows_pad,
+                                                                               (int)cols, steps, block_bytes(dt));
+    }
+    return check_launch(ctx, "repack");
+}
+
+static size_t tiled_bytes(hale_dtype dt, uint32_t rows, uint32_t cols) {
+    size_t rows_pad = (rows + 31) / 32 * 32;
+    if (is_quant(dt)) return rows_pad * (cols / 32) * block_bytes(dt);
+    return rows_pad * ((cols + 7) / 8) * 8 * block_bytes(dt);
+}
+
+// ---------------------------------------------------------------------------
+// matrices
+// ---------------------------------------------------------------------------
+extern "C" hale_status hale_matrix_create(hale_ctx* ctx, hale_dtype dtype, uint32_t rows, uint32_t cols,
+                                          const void* encoded, uint64_t encoded_bytes, int on_device,
+                                          hale_matrix** out) {
+    if (!ctx || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_create: NULL argument");
+    *out = nullptr;
+    int64_t rb = hale_row_bytes(dtype, cols);
+    if (rb < 0)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "dtype %d needs row length divisible by %d, got %u",
+                    (int)dtype, block_len(dtype), cols);
+    if (rows == 0 || cols == 0) return fail(ctx, HALE_E_INVALID_ARGUMENT, "matrix %ux%u is empty", rows, cols);
+    if ((uint64_t)rows * (uint64_t)rb != encoded_bytes)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "matrix %ux%u dtype %d needs %llu bytes, got %llu", rows,
+                    cols, (int)dtype, (unsigned long long)rows * (unsigned long long)rb,
+                    (unsigned long long)encoded_bytes);
+    if (!encoded) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_create: data is NULL");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_matrix* m = new hale_matrix();
+    m->ctx = ctx;
+    m->dtype = dtype;
+    m->rows = rows;
+    m->cols = cols;
+    m->rows_pad = (rows + 31) / 32 * 32;
+    m->nb = is_quant(dtype) ? cols / 32 : (cols + 7) / 8;
+    m->bytes = tiled_bytes(dtype, rows, cols);
+    if (cudaMalloc(&m->data, m->bytes) != cudaSuccess) {
+        delete m;
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "cannot allocate %zu bytes for a matrix", m->bytes);
+    }
+    const uint8_t* src = static_cast<const uint8_t*>(encoded);
+    uint8_t* tmp = nullptr;
+    if (!on_device) {
+        if (cudaMalloc(&tmp, encoded_bytes) != cudaSuccess ||
+            cudaMemcpy(tmp, encoded, encoded_bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+            cudaFree(tmp);
+            cudaFree(m->data);
+            delete m;
+            return fail(ctx, HALE_E_CUDA, "cannot stage %llu bytes of matrix data", (unsigned long long)encoded_bytes);
+        }
+        src = tmp;
+    }
+    hale_status st = launch_repack(ctx, dtype, src, m->data, rows, cols, 0);
+    cudaError_t e = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (st != HALE_OK || e != cudaSuccess) {
+        cudaFree(m->data);
+        delete m;
+        return st != HALE_OK ? st : fail(ctx, HALE_E_CUDA, "repack failed: %s", cudaGetErrorString(e));
+    }
+    *out = m;
+    return HALE_OK;
+}
+
+extern "C" void hale_matrix_destroy(hale_matrix* m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    cudaFree(m->data);
+    delete m;
+}
+
+static int ring_stages(hale_dtype dt) { return dt == HALE_Q4_0 ? 4 : 3; }
+static size_t ring_smem(hale_dtype dt) {
+    int rec = 32 * block_bytes(dt);
+    int S = ring_stages(dt);
+    return (size_t)S * kStageBlocks * rec + (size_t)S * 8;
+}
+
+// Largest activation-row count a tile sees -> compiled pass width.
+static int tg_max(long long rows) {
+    if (rows <= 1) return 1;
+    if (rows <= 2) return 2;
+    if (rows <= 4) return 4;
+    if (rows <= 8) return 8;
+    if (rows <= 16) return 16;
+    return 32;
+}
+
+template <int QT, int TG>
+static void qgemv_go(const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M, float* out,
+                     int32_t* dbg, int S_, size_t smem, uint32_t* err, cudaStream_t st) {
+    qgemv_kernel<QT, TG><<<m->rows_pad / 32, 32, smem, st>>>(m->data, (int)m->rows, (int)m->nb, xq, xaux, (int)M,
+                                                             out, dbg, S_, err);
+}
+
+template <int QT>
+static void qgemv_tg(int tg, const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M, float* out,
+                     int32_t* dbg, int S_, size_t smem, uint32_t* err, cudaStream_t st) {
+    switch (tg) {
+    case 1: qgemv_go<QT, 1>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    case 2: qgemv_go<QT, 2>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    case 4: qgemv_go<QT, 4>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    case 8: qgemv_go<QT, 8>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    case 16: qgemv_go<QT, 16>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    default: qgemv_go<QT, 32>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
+    }
+}
+
+static hale_status qgemv_launch(hale_ctx* ctx, const hale_matrix* m, const int8_t* xq, const int2* xaux,
+                                uint32_t M, float* out, int32_t* dbg, cudaStream_t st) {
+    int S_ = ring_stages(m->dtype);
+    size_t smem = ring_smem(m->dtype);
+    int tg = tg_max(M);
+    ProfScope ps_(ctx, "qgemv", st);
+    if (m->dtype == HALE_Q4_0)
+        qgemv_tg<0>(tg, m, xq, xaux, M, out, dbg, S_, smem, ctx->d_err, st);
+    else
+        qgemv_tg<1>(tg, m, xq, xaux, M, out, dbg, S_, smem, ctx->d_err, st);
+    return check_launch(ctx, "qgemv");
+}
+
+template <int DT>
+static void fgemv_dispatch(const hale_matrix* m, const float* x, uint32_t M, float* out, int vec, cudaStream_t st) {
+    unsigned grid = (m->rows_pad / 32 + 3) / 4;
+    if (M <= 1)
+        fgemv_kernel<DT, 1><<<grid, 128, 0, st>>>(m->data, (int)m->rows, (int)m->cols, (int)m->nb, x, (int)M, out, vec);
+    else if (M <= 2)
+        fgemv_kernel<DT, 2><<<grid, 128, 0, st>>>(m->data, (int)m->rows, (int)m->cols, (int)m->nb, x, (int)M, out, vec);
+    else if (M <= 4)
+        fgemv_kernel<DT, 4><<<grid, 128, 0, st>>>(m->data, (int)m->rows, (int)m->cols, (int)m->nb, x, (int)M, out, vec);
+    else
+        fgemv_kernel<DT, 8><<<grid, 128, 0, st>>>(m->data, (int)m->rows, (int)m->cols, (int)m->nb, x, (int)M, out, vec);
+}
+
+static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float* x, uint32_t M, float* out,
+                                cudaStream_t st) {
+    int vec = (m->cols % 4 == 0) && (((uintptr_t)x & 15) == 0);
+    ProfScope ps_(ctx, "fgemv", st);
+    switch (m->dtype) {
+    case HALE_F32: fgemv_dispatch<0>(m, x, M, out, vec, st); break;
+    case HALE_F16: fgemv_dispatch<1>(m, x, M, out, vec, st); break;
+    default: fgemv_dispatch<2>(m, x, M, out, vec, st); break;
+    }
+    return check_launch(ctx, "fgemv");
+}
+
+extern "C" hale_status hale_quantize_q8(hale_ctx* ctx, const float* x, uint32_t m_rows, uint32_t cols,
+                                        float* scales, int8_t* quants, void* stream) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_quantize_q8: ctx is NULL");
+    if (cols % 32) return fail(ctx, HALE_E_INVALID_ARGUMENT, "activation length must be a multiple of 32, got %u", cols);
+    if (m_rows == 0) return HALE_OK;
+    if (!x || !scales || !quants) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_quantize_q8: NULL buffer");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    unsigned grid = (m_rows * 32 + 255) / 256;
+    ProfScope ps_(ctx, "quantize", S(stream));
+    quantize_rows_kernel<<<grid, 256, 0, S(stream)>>>(x, (int)m_rows, (int)cols, quants, scales, nullptr);
+    return check_launch(ctx, "quantize");
+}
+
+extern "C" hale_status hale_matrix_matvec(hale_ctx* ctx, const hale_matrix* m, const float* x, uint32_t m_rows,
+                                          float* out, int32_t* block_sums, void* stream) {
+    if (!ctx || !m) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec: NULL argument");
+    if (m_rows == 0) return HALE_OK;
+    if (!x || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec: NULL buffer");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    if (is_float(m->dtype)) {
+        if (block_sums) return fail(ctx, HALE_E_INVALID_ARGUMENT, "block sums exist only for quantized matrices");
+        return fgemv_launch(ctx, m, x, m_rows, out, st);
+    }
+    size_t qbytes = align_up((size_t)m_rows * m->cols, 256);
+    size_t abytes = (size_t)m_rows * m->nb * 8;
+    hale_status rs = ensure_scratch(ctx, qbytes + abytes, stream);
+    if (rs) return rs;
+    int8_t* xq = static_cast<int8_t*>(ctx->scratch);
+    int2* xaux = reinterpret_cast<int2*>(static_cast<uint8_t*>(ctx->scratch) + qbytes);
+    unsigned grid = (m_rows * 32 + 255) / 256;
+    {
+        ProfScope ps_(ctx, "quantize", st);
+        quantize_rows_kernel<<<grid, 256, 0, st>>>(x, (int)m_rows, (int)m->cols, xq, nullptr, xaux);
+    }
+    hale_status r = check_launch(ctx, "quantize");
+    if (r) return r;
+    return qgemv_launch(ctx, m, xq, xaux, m_rows, out, block_sums, st);
+}
+
+extern "C" hale_status hale_matrix_matvec_q8(hale_ctx* ctx, const hale_matrix* m, const float* x_scales,
+                                             const int8_t* x_quants, uint32_t m_rows, float* out,
+                                             int32_t* block_sums, void* stream) {
+    if (!ctx || !m) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec_q8: NULL argument");
+    if (!is_quant(m->dtype))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "dot_quantized called with float dtype %d", (int)m->dtype);
+    if (m_rows == 0) return HALE_OK;
+    if (!x_scales || !x_quants || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec_q8: NULL buffer");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    hale_status rs = ensure_scratch(ctx, (size_t)m_rows * m->nb * 8, stream);
+    if (rs) return rs;
+    int2* xaux = static_cast<int2*>(ctx->scratch);
+    long long n = (long long)m_rows * m->nb;
+    aux_from_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x_scales, x_quants, (int)m_rows, (int)m->cols, xaux);
+    hale_status r = check_launch(ctx, "aux");
+    if (r) return r;
+    if (((uintptr_t)x_quants & 15) != 0)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "x_quants must be 16-byte aligned");
+    return qgemv_launch(ctx, m, x_quants, xaux, m_rows, out, block_sums, st);
+}
+
+// ---------------------------------------------------------------------------
+// expert pool
+// ---------------------------------------------------------------------------
+extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
+                                        uint32_t n_layers, uint32_t n_experts, hale_pool** out) {
+    if (!ctx || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_pool_create: NULL argument");
+    *out = nullptr;
+    if (!is_quant(dtype)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert pool dtype must be q8_0 or q4_0");
+    if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hidden (%u) and intermediate (%u) must be non-zero multiples of 32",
+                    hidden, inter);
+    if (n_layers == 0 || n_experts == 0 || n_experts > 256)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "need 1..256 experts and >= 1 layer (got %u, %u)", n_experts, n_layers);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_pool* p = new hale_pool();
+    p->ctx = ctx;
+    p->dtype = dtype;
+    p->H = hidden;
+    p->I = inter;
+    p->L = n_layers;
+    p->E = n_experts;
+    p->expert_stride = 2 * tiled_bytes(dtype, inter, hidden) + tiled_bytes(dtype, hidden, inter);
+    p->record_bytes = 2 * (size_t)inter * hale_row_bytes(dtype, hidden) + (size_t)hidden * hale_row_bytes(dtype, inter);
+    size_t total = p->expert_stride * n_layers * n_experts;
+    if (cudaMalloc(&p->data, total) != cudaSuccess || cudaMalloc(&p->staging, p->record_bytes) != cudaSuccess ||
+        cudaMalloc(&p->d_routing, (size_t)n_layers * n_experts * 8) != cudaSuccess ||
+        cudaMemset(p->d_routing, 0, (size_t)n_layers * n_experts * 8) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p->data);
+        cudaFree(p->staging);
+        cudaFree(p->d_routing);
+        delete p;
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "cannot allocate %zu bytes of expert pool", total);
+    }
+    p->resident.assign((size_t)n_layers * n_experts, 0);
+    p->layer_resident.assign(n_layers, 0);
+    p->host_routing.assign((size_t)n_layers * n_experts, 0);
+    *out = p;
+    return HALE_OK;
+}
+
+extern "C" void hale_pool_destroy(hale_pool* p) {
+    if (!p) return;
+    cudaSetDevice(p->ctx->device);
+    cudaFree(p->data);
+    cudaFree(p->staging);
+    cudaFree(p->d_routing);
+    delete p;
+}
+
+extern "C" uint64_t hale_pool_expert_bytes(const hale_pool* p) { return p ? p->record_bytes : 0; }
+
+extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uint32_t expert, const void* record,
+                                               uint64_t record_bytes, int on_device, void* stream) {
+    if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_upload_expert: pool is NULL");
+    hale_ctx* ctx = p->ctx;
+    if (layer >= p->L || expert >= p->E)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u out of range", layer, expert);
+    if (!record) return fail(ctx, HALE_E_INVALID_ARGUMENT, "record is NULL");
+    if (record_bytes != p->record_bytes)
+        return fail(ctx, HALE_E_BAD_TENSOR, "L%uE%u: record is %llu bytes, expected %zu", layer, expert,
+                    (unsigned long long)record_bytes, p->record_bytes);
+    auto t0 = std::chrono::steady_clock::now();
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    const uint8_t* src = static_cast<const uint8_t*>(record);
+    if (!on_device) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(p->staging, record, record_bytes, cudaMemcpyHostToDevice, st));
+        src = p->staging;
+    }
+    uint8_t* dst = p->data + ((size_t)layer * p->E + expert) * p->expert_stride;
+    size_t proj = (size_t)p->I * hale_row_bytes(p->dtype, p->H);
+    size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
+    hale_status r;
+    if ((r = launch_repack(ctx, p->dtype, src, dst, p->I, p->H, st))) return r;
+    if ((r = launch_repack(ctx, p->dtype, src + proj, dst + gu_tiled, p->I, p->H, st))) return r;
+    if ((r = launch_repack(ctx, p->dtype, src + 2 * proj, dst + 2 * gu_tiled, p->H, p->I, st))) return r;
+    CUDA_TRY(ctx, cudaStreamSynchronize(st));
+    size_t i = (size_t)layer * p->E + expert;
+    if (!p->resident[i]) {
+        p->resident[i] = 1;
+        p->layer_resident[layer]++;
+        p->stats.pinned_experts++;
+        p->stats.pinned_bytes += p->record_bytes;
+    }
+    p->stats.bytes_loaded += record_bytes;
+    p->stats.load_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys, uint64_t n, hale_expert_view* out) {
+    if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: pool is NULL");
+    hale_ctx* ctx = p->ctx;
+    if (n && (!keys || !out)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: NULL buffer");
+    // routing is recorded before lookup, like ExpertCache::fetch (cache.rs:125-128)
+    for (uint64_t i = 0; i < n; i++)
+        if (keys[i].layer < p->L && keys[i].expert < p->E) p->host_routing[(size_t)keys[i].layer * p->E + keys[i].expert]++;
+    uint64_t hits = 0;
+    for (uint64_t i = 0; i < n; i++) {
+        const hale_expert_key k = keys[i];
+        if (k.layer >= p->L || k.expert >= p->E) {
+            p->stats.misses++;
+            return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u out of range", k.layer, k.expert);
+        }
+        size_t idx = (size_t)k.layer * p->E + k.expert;
+        if (!p->resident[idx]) {
+            p->stats.misses++;
+            return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u is not resident in the pool", k.layer, k.expert);
+        }
+        const uint8_t* base = p->data + idx * p->expert_stride;
+        size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
+        out[i].gate = base;
+        out[i].up = base + gu_tiled;
+        out[i].down = base + 2 * gu_tiled;
+        hits++;
+    }
+    p->stats.pinned_hits += hits;
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_pool_routing_counts(hale_pool* p, uint64_t* counts, uint64_t n) {
+    if (!p || !counts) return fail(p ? p->ctx : nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_routing_counts: NULL");
+    size_t total = (size_t)p->L * p->E;
+    if (n < total) return fail(p->ctx, HALE_E_INVALID_ARGUMENT, "counts needs %zu entries", total);
+    CUDA_TRY(p->ctx, cudaSetDevice(p->ctx->device));
+    std::vector<uint64_t> dev(total);
+    CUDA_TRY(p->ctx, cudaDeviceSynchronize());
+    CUDA_TRY(p->ctx, cudaMemcpy(dev.data(), p->d_routing, total * 8, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < total; i++) counts[i] = dev[i] + p->host_routing[i];
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_pool_stats(hale_pool* p, hale_cache_stats* out) {
+    if (!p || !out) return fail(p ? p->ctx : nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_stats: NULL");
+    size_t total = (size_t)p->L * p->E;
+    std::vector<uint64_t> dev(total);
+    CUDA_TRY(p->ctx, cudaSetDevice(p->ctx->device));
+    CUDA_TRY(p->ctx, cudaDeviceSynchronize());
+    CUDA_TRY(p->ctx, cudaMemcpy(dev.data(), p->d_routing, total * 8, cudaMemcpyDeviceToHost));
+    *out = p->stats;
+    for (size_t i = 0; i < total; i++) out->pinned_hits += dev[i];
+    return HALE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// MoE layer
+// ---------------------------------------------------------------------------
+static hale_status check_layer(hale_ctx* ctx, const hale_moe_layer* ly, uint32_t H) {
+    if (!ly) return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer is NULL");
+    if (!ly->router) return fail(ctx, HALE_E_INVALID_ARGUMENT, "router weights are NULL");
+    if (!is_float(ly->router_dtype))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "router dtype must be f32, f16 or bf16");
+    if (ly->n_experts == 0 || ly->n_experts > 256)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "router has %u experts (1..256 supported)", ly->n_experts);
+    if (ly->top_k == 0 || ly->top_k > ly->n_experts || ly->top_k > 32)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "num_experts_per_tok (%u) must be in 1..=%u", ly->top_k,
+                    std::min(ly->n_experts, 32u));
+    if (H == 0) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hidden size is 0");
+    return HALE_OK;
+}
+
+static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32_t H, const float* x, uint32_t M,
+                                 const MoeLayout& L, bool full, int32_t* user_idx, float* user_w, float* probs,
+                                 unsigned long long* routing, cudaStream_t st) {
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    RouterArgs a{};
+    a.w = ly->router;
+    a.wdtype = float_code(ly->router_dtype);
+    a.E = (int)ly->n_experts;
+    a.H = (int)H;
+    a.M = (int)M;
+    a.k = (int)ly->top_k;
+    a.normalize = ly->normalize_topk ? 1 : 0;
+    a.TT = M >= 4 ? 4 : (M >= 2 ? 2 : 1);
+    a.ET = 32 / a.TT;
+    a.x = x;
+    a.logits = reinterpret_cast<float*>(ws + L.logits);
+    a.probs_out = probs;
+    a.topk_idx = reinterpret_cast<int*>(ws + L.topk_idx);
+    a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+    a.user_idx = user_idx;
+    a.user_w = user_w;
+    a.xq = full ? reinterpret_cast<int8_t*>(ws + L.xq) : nullptr;
+    a.xaux = reinterpret_cast<int2*>(ws + L.xaux);
+    a.elist_off = full ? reinterpret_cast<int*>(ws + L.elist_off) : nullptr;
+    a.elist = reinterpret_cast<int*>(ws + L.elist);
+    a.active = reinterpret_cast<int*>(ws + L.active);
+    a.n_active = reinterpret_cast<int*>(ws + L.n_active);
+    a.routing_counts = routing;
+    a.tile_cnt = reinterpret_cast<unsigned*>(ws + L.tile_cnt);
+    a.grid_cnt = reinterpret_cast<unsigned*>(ws + L.grid_cnt);
+    dim3 grid((M + a.TT - 1) / a.TT, (a.E + a.ET - 1) / a.ET);
+    ProfScope ps_(ctx, "router", st);
+    router_kernel<<<grid, 256, 0, st>>>(a);
+    return check_launch(ctx, "router");
+}
+
+extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, uint32_t hidden, const float* x,
+                                      uint32_t M, int32_t* topk_idx, float* topk_w, float* probs, void* stream) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_moe_route: ctx is NULL");
+    hale_status r = check_layer(ctx, ly, hidden);
+    if (r) return r;
+    if (M == 0) return HALE_OK;
+    if (!x || !topk_idx || !topk_w) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_route: NULL buffer");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    MoeLayout L;
+    int Hq = (int)((hidden + 31) / 32 * 32);
+    if ((r = ensure_moe_ws(ctx, (int)M, (int)ly->n_experts, (int)ly->top_k, Hq, ctx->capI > 0 ? ctx->capI : 32, stream, &L)))
+        return r;
+    return launch_router(ctx, ly, hidden, x, M, L, false, topk_idx, topk_w, probs, nullptr, S(stream));
+}
+
+template <int QT, int TG>
+static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned g1, unsigned g2, size_t smem,
+                             cudaStream_t st) {
+    {
+        ProfScope ps_(ctx, "expert_gate_up", st);
+        expert_gate_up_kernel<QT, TG><<<g1, 32, smem, st>>>(a);
+    }
+    hale_status r = check_launch(ctx, "expert_gate_up");
+    if (r) return r;
+    ProfScope ps_(ctx, "expert_down", st);
+    expert_down_kernel<QT, TG><<<g2, 32, smem, st>>>(a);
+    return HALE_OK;
+}
+
+template <int QT>
+static hale_status expert_launch(hale_ctx* ctx, int tg, const ExpertArgs& a, unsigned g1, unsigned g2,
+                                 size_t smem, cudaStream_t st) {
+    switch (tg) {
+    case 1: return expert_go<QT, 1>(ctx, a, g1, g2, smem, st);
+    case 2: return expert_go<QT, 2>(ctx, a, g1, g2, smem, st);
+    case 4: return expert_go<QT, 4>(ctx, a, g1, g2, smem, st);
+    case 8: return expert_go<QT, 8>(ctx, a, g1, g2, smem, st);
+    case 16: return expert_go<QT, 16>(ctx, a, g1, g2, smem, st);
+    default: return expert_go<QT, 32>(ctx, a, g1, g2, smem, st);
+    }
+}
+
+extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
+                                        uint32_t M, float* out, int32_t* topk_idx, float* topk_w, void* stream) {
+    if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL ctx or pool");
+    if (p->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "pool belongs to another context");
+    hale_status r = check_layer(ctx, ly, p->H);
+    if (r) return r;
+    if (ly->layer >= p->L) return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u has no experts in the pool", ly->layer);
+    if (ly->n_experts != p->E)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "router has %u experts, pool has %u", ly->n_experts, p->E);
+    if (p->layer_resident[ly->layer] != p->E)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: only %u of %u experts are resident", ly->layer,
+                    p->layer_resident[ly->layer], p->E);
+    if (M == 0) return HALE_OK;
+    if (!x || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL buffer");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int E = (int)p->E, k = (int)ly->top_k, H = (int)p->H, I = (int)p->I;
+    MoeLayout L;
+    if ((r = ensure_moe_ws(ctx, (int)M, E, k, H, I, stream, &L))) return r;
+    cudaStream_t st = S(stream);
+    if ((r = launch_router(ctx, ly, p->H, x, M, L, true, topk_idx, topk_w, nullptr,
+                           p->d_routing + (size_t)ly->layer * p->E, st)))
+        return r;
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    ExpertArgs a{};
+    a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+    a.expert_stride = p->expert_stride;
+    a.H = H;
+    a.I = I;
+    a.k = k;
+    a.M = (int)M;
+    a.elist_off = reinterpret_cast<int*>(ws + L.elist_off);
+    a.elist = reinterpret_cast<int*>(ws + L.elist);
+    a.active = reinterpret_cast<int*>(ws + L.active);
+    a.n_active = reinterpret_cast<int*>(ws + L.n_active);
+    a.xq = reinterpret_cast<int8_t*>(ws + L.xq);
+    a.xaux = reinterpret_cast<int2*>(ws + L.xaux);
+    a.gu = reinterpret_cast<float*>(ws + L.gu);
+    a.gu_cnt = reinterpret_cast<unsigned*>(ws + L.gu_cnt);
+    a.hq = reinterpret_cast<int8_t*>(ws + L.hq);
+    a.haux = reinterpret_cast<int2*>(ws + L.haux);
+    a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+    a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
+    a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+    a.out = out;
+    a.S = ring_stages(p->dtype);
+    a.err = ctx->d_err;
+    size_t smem = ring_smem(p->dtype);
+    unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
+    unsigned g1 = max_active * 2 * (I / 32), g2 = max_active * (H / 32);
+    // an expert sees at most M tokens (each token picks distinct experts)
+    int tg = tg_max(M);
+    if (p->dtype == HALE_Q4_0)
+        r = expert_launch<0>(ctx, tg, a, g1, g2, smem, st);
+    else
+        r = expert_launch<1>(ctx, tg, a, g1, g2, smem, st);
+    if (r) return r;
+    return check_launch(ctx, "expert_down");
+}
+
+extern "C" hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly,
+                                             const float* x_host, uint32_t M, float* out_host,
+                                             int32_t* idx_host, float* w_host, void* stream) {
+    if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward_host: NULL ctx or pool");
+    if (M == 0) return HALE_OK;
+    if (!x_host || !out_host) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward_host: NULL buffer");
+    hale_status r = check_layer(ctx, ly, p->H);
+    if (r) return r;
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    size_t xb = (size_t)M * p->H * 4, kb = (size_t)M * ly->top_k * 4;
+    size_t need = 2 * align_up(xb, 256) + 2 * align_up(kb, 256);
+    if ((r = ensure_scratch(ctx, need, stream))) return r;
+    uint8_t* s = static_cast<uint8_t*>(ctx->scratch);
+    float* dx = reinterpret_cast<float*>(s);
+    float* dout = reinterpret_cast<float*>(s + align_up(xb, 256));
+    int32_t* didx = reinterpret_cast<int32_t*>(s + 2 * align_up(xb, 256));
+    float* dw = reinterpret_cast<float*>(s + 2 * align_up(xb, 256) + align_up(kb, 256));
+    cudaStream_t st = S(stream);
+    CUDA_TRY(ctx, cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
+    if ((r = hale_moe_forward(ctx, p, ly, dx, M, dout, idx_host ? didx : nullptr, w_host ? dw : nullptr, stream)))
+        return r;
+    CUDA_TRY(ctx, cudaMemcpyAsync(out_host, dout, xb, cudaMemcpyDeviceToHost, st));
+    if (idx_host) CUDA_TRY(ctx, cudaMemcpyAsync(idx_host, didx, kb, cudaMemcpyDeviceToHost, st));
+    if (w_host) CUDA_TRY(ctx, cudaMemcpyAsync(w_host, dw, kb, cudaMemcpyDeviceToHost, st));
+    return hale_ctx_check(ctx, stream);
+}
+
+// ---------------------------------------------------------------------------
+// sampling tail
+// ---------------------------------------------------------------------------
+extern "C" hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, const float* hidden, uint32_t batch,
+                                    float* logits, void* stream) {
+    if (!ctx || !lm_head) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_lm_head: NULL argument");
+    if (!is_float(lm_head->dtype)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "lm_head must be f32, f16 or bf16");
+    return hale_matrix_matvec(ctx, lm_head, hidden, batch, logits, nullptr, stream);
+}
+
+extern "C" hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t batch, uint32_t vocab,
+                                   const hale_sampling_params* prm, uint64_t* rng_state, const int32_t* seen_ids,
+                                   uint32_t n_seen, int32_t* out_tokens, void* stream) {
+    if (!ctx || !prm) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_sample: NULL argument");
+    if (batch == 0) return HALE_OK;
+    if (!logits || !out_tokens) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_sample: NULL buffer");
+    if (vocab == 0 || vocab > (1u << 30)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "vocab %u out of range", vocab);
+    float pen = prm->repetition_penalty;
+    if (!(pen > 0.0f)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "repetition_penalty must be > 0");
+    int K = (int)vocab;
+    if (prm->temperature > 0.0f) {
+        if (!rng_state) return fail(ctx, HALE_E_INVALID_ARGUMENT, "rng_state is NULL");
+        K = prm->top_k == 0 ? (int)vocab : (int)std::min<uint32_t>(prm->top_k, vocab);
+        if (K > kSampleMaxK)
+            return fail(ctx, HALE_E_UNSUPPORTED, "top_k=%u over vocab %u keeps %d candidates; this build sorts at most %d",
+                        prm->top_k, vocab, K, kSampleMaxK);
+    }
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    SampleArgs a{};
+    a.logits = logits;
+    a.V = (int)vocab;
+    a.temperature = prm->temperature;
+    a.top_p = prm->top_p;
+    a.penalty = pen;
+    a.top_k = K;
+    a.rng = rng_state;
+    a.seen = seen_ids;
+    a.n_seen = (int)n_seen;
+    a.out = out_tokens;
+    size_t smem = (seen_ids && n_seen && pen != 1.0f) ? (size_t)((vocab + 31) / 32) * 4 : 0;
+    if (smem > 200 * 1024) return fail(ctx, HALE_E_UNSUPPORTED, "vocab %u too large for the penalty bitmap", vocab);
+    if (smem > 48 * 1024) CUDA_TRY(ctx, cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ProfScope ps_(ctx, "sample", S(stream));
+    sample_kernel<<<batch, kSampleThreads, smem, S(stream)>>>(a);
+    return check_launch(ctx, "sample");
+}
+
+// ---------------------------------------------------------------------------
+// self-check
+// ---------------------------------------------------------------------------
+extern "C" void hale_expf_host(const float* x, float* y, uint64_t n) {
+    for (uint64_t i = 0; i < n; i++) y[i] = hale::hale_expf(x[i]);
+}

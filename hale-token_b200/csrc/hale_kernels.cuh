@@ -1,0 +1,938 @@
+// hale_kernels.cuh -- the B200 kernels of the MoE expert path and the
+// sampling tail. Each kernel names the reference code it reproduces (paths
+// inside the Rust reference crate).
+//
+// Quantized weight layout in HBM ("row tiles"). A matrix of R rows x C cols
+// (nb = C/32 blocks per row) is cut into tiles of 32 consecutive rows. Tile
+// g holds, for every block b in order, a 32*BB-byte record:
+//     [32 rows x QB bytes of quants][32 rows x 2 bytes f16 scale]
+// with BB = 18 (q4_0; QB = 16 nibble bytes, same j / j+16 pairing as the
+// reference) or 34 (q8_0; QB = 32). A tile is nb * 32 * BB bytes -- the same
+// bytes as the reference's 32 rows, reordered so that a warp (lane = row)
+// reads one block of all 32 rows as one contiguous 512 B / 1 KiB run, and a
+// stage of consecutive blocks is one contiguous span for a bulk async copy.
+//
+// Float matrices (router excluded, which is read row-major) use
+//     tile g, step i: [32 rows x 8 elements]
+// so a thread owning row r reads the 8 elements of step i that feed the
+// reference's 8 accumulator lanes, and a warp reads 32 rows contiguously.
+#pragma once
+
+#include "hale_device.cuh"
+
+namespace hale {
+
+constexpr int kTileRows = 32;
+constexpr int kQK = 32;
+constexpr int kStageBlocks = 8;  // blocks per bulk-copy stage
+
+template <int QT>
+struct QFmt;
+template <>
+struct QFmt<0> {  // q4_0
+    static constexpr int BB = 18, QB = 16;
+};
+template <>
+struct QFmt<1> {  // q8_0
+    static constexpr int BB = 34, QB = 32;
+};
+
+// ---------------------------------------------------------------------------
+// repack: reference row-major encoding -> row tiles
+// ---------------------------------------------------------------------------
+__global__ void repack_quant_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                    int rows, int rows_pad, int nb, int BB, int QB) {
+    long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    long long total = (long long)rows_pad * nb;
+    if (idx >= total) return;
+    int r = (int)(idx / nb), b = (int)(idx % nb);
+    int g = r / kTileRows, lane = r % kTileRows;
+    size_t tile_bytes = (size_t)nb * kTileRows * BB;
+    uint8_t* rec = dst + (size_t)g * tile_bytes + (size_t)b * kTileRows * BB;
+    uint8_t* q = rec + lane * QB;
+    uint8_t* s = rec + kTileRows * QB + lane * 2;
+    if (r < rows) {
+        const uint8_t* blk = src + (size_t)r * nb * BB + (size_t)b * BB;
+        s[0] = blk[0];
+        s[1] = blk[1];
+        for (int j = 0; j < QB; j++) q[j] = blk[2 + j];
+    } else {
+        s[0] = 0;
+        s[1] = 0;
+        for (int j = 0; j < QB; j++) q[j] = 0;
+    }
+}
+
+__global__ void repack_float_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                    int rows, int rows_pad, int cols, int steps, int esize) {
+    long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    long long total = (long long)rows_pad * steps;
+    if (idx >= total) return;
+    int r = (int)(idx / steps), i = (int)(idx % steps);
+    int g = r / kTileRows, lane = r % kTileRows;
+    uint8_t* d = dst + (((size_t)g * steps + i) * kTileRows + lane) * 8 * esize;
+    for (int l = 0; l < 8; l++) {
+        int c = i * 8 + l;
+        for (int k = 0; k < esize; k++)
+            d[l * esize + k] = (r < rows && c < cols) ? src[((size_t)r * cols + c) * esize + k] : 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q8Activations::quantize (src/tensor/quant.rs:77-93), one warp per row.
+// Writes quants [rows, cols] i8 and, per block, the f32 scale (scales,
+// nullable) and aux = (scale bits, -8 * sum of the block's quants) (aux,
+// nullable). The -8*sum term turns the nibble dot into the reference's
+// sum of (n - 8) * x exactly (integer arithmetic).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void quantize_block(const float* __restrict__ xb, int8_t* __restrict__ q,
+                                               float* scale_out, int* sum_out) {
+    float amax = 0.0f;
+    for (int j = 0; j < kQK; j++) amax = fmaxf(amax, fabsf(xb[j]));
+    float scale = fdiv(amax, 127.0f);
+    float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
+    int s = 0;
+    for (int j = 0; j < kQK; j++) {
+        int v = sat_i8(roundf(fmul(xb[j], inv)));
+        q[j] = (int8_t)v;
+        s += v;
+    }
+    *scale_out = scale;
+    *sum_out = s;
+}
+
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int rows, int cols,
+                                     int8_t* __restrict__ quants, float* __restrict__ scales,
+                                     int2* __restrict__ aux) {
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    int nb = cols / kQK;
+    const float* xr = x + (size_t)warp * cols;
+    for (int b = lane; b < nb; b += 32) {
+        float sc;
+        int sm;
+        quantize_block(xr + b * kQK, quants + (size_t)warp * cols + b * kQK, &sc, &sm);
+        if (scales) scales[(size_t)warp * nb + b] = sc;
+        if (aux) aux[(size_t)warp * nb + b] = make_int2(__float_as_int(sc), -8 * sm);
+    }
+}
+
+// aux from caller-supplied Q8Activations (scales + quants).
+__global__ void aux_from_q8_kernel(const float* __restrict__ scales,
+                                   const int8_t* __restrict__ quants, int rows, int cols,
+                                   int2* __restrict__ aux) {
+    long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    int nb = cols / kQK;
+    if (idx >= (long long)rows * nb) return;
+    int r = (int)(idx / nb), b = (int)(idx % nb);
+    const int8_t* q = quants + (size_t)r * cols + b * kQK;
+    int s = 0;
+    for (int j = 0; j < kQK; j++) s += q[j];
+    aux[idx] = make_int2(__float_as_int(scales[idx]), -8 * s);
+}
+
+// ---------------------------------------------------------------------------
+// The quantized row-tile dot product (dot_q8_0 / dot_q4_0, quant.rs:115-144)
+// for one warp: lane = row of the tile, TG activation rows at once.
+//
+// Weights stream HBM -> shared memory with cp.async.bulk (the TMA engine)
+// through a ring of S stages of kStageBlocks blocks, each completing on its
+// own mbarrier; lane 0 issues, the warp consumes. Per block and activation
+// row the integer dot is 8 dp4a (exact int32), then the reference's float
+// step total += (w_scale * x_scale) * isum, in block order, unfused.
+// ---------------------------------------------------------------------------
+struct Ring {
+    uint8_t* buf;      // S * stage_bytes
+    uint64_t* bars;    // S mbarriers
+    int S;
+    int stage_bytes;   // kStageBlocks * 32 * BB
+    uint32_t phase;    // bit s = parity of the next completion of slot s
+};
+
+template <int QT>
+__device__ __forceinline__ void ring_issue(Ring& rg, const uint8_t* gtile, int nb, int st) {
+    constexpr int REC = kTileRows * QFmt<QT>::BB;
+    int slot = st % rg.S;
+    int nblk = min(kStageBlocks, nb - st * kStageBlocks);
+    uint32_t bytes = (uint32_t)(nblk * REC);
+    mbar_arrive_expect_tx(&rg.bars[slot], bytes);
+    bulk_g2s(rg.buf + (size_t)slot * rg.stage_bytes, gtile + (size_t)st * kStageBlocks * REC, bytes,
+             &rg.bars[slot]);
+}
+
+// Computes acc[j] = dot(row lane of the tile, activation row xr[j]) for
+// j < TG. Returns false if a wait timed out (results then invalid).
+template <int QT, int TG>
+__device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
+                         const int8_t* __restrict__ xq, const int2* __restrict__ xaux, int cols,
+                         const int (&xr)[TG], int nvalid, float (&acc)[TG], int32_t* dbg,
+                         size_t dbg_row_stride, uint32_t* err) {
+    constexpr int BB = QFmt<QT>::BB, QB = QFmt<QT>::QB, REC = kTileRows * BB;
+    const int lane = threadIdx.x & 31;
+    const int nst = (nb + kStageBlocks - 1) / kStageBlocks;
+#pragma unroll
+    for (int j = 0; j < TG; j++) acc[j] = 0.0f;
+    if (lane == 0) {
+        fence_proxy_async_smem();  // earlier passes read these slots
+        for (int st = 0; st < min(rg.S, nst); st++) ring_issue<QT>(rg, gtile, nb, st);
+    }
+    bool ok = true;
+    for (int st = 0; st < nst; st++) {
+        int slot = st % rg.S;
+        if (!mbar_wait(&rg.bars[slot], (rg.phase >> slot) & 1u, err)) {
+            ok = false;
+            // drain: give the copies already issued a bounded chance to land
+            for (int s2 = st; s2 < min(st + rg.S, nst); s2++)
+                mbar_wait(&rg.bars[s2 % rg.S], (rg.phase >> (s2 % rg.S)) & 1u, nullptr, 400000000LL);
+            break;
+        }
+        rg.phase ^= 1u << slot;
+        const uint8_t* sbuf = rg.buf + (size_t)slot * rg.stage_bytes;
+        int nblk = min(kStageBlocks, nb - st * kStageBlocks);
+#pragma unroll 1
+        for (int bi = 0; bi < nblk; bi++) {
+            const int b = st * kStageBlocks + bi;
+            const uint8_t* rec = sbuf + bi * REC;
+            float ws = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rec + kTileRows * QB + lane * 2));
+            int w[8];
+            if (QT == 0) {
+                uint4 nib = *reinterpret_cast<const uint4*>(rec + lane * QB);
+                w[0] = nib.x & 0x0F0F0F0F;
+                w[1] = nib.y & 0x0F0F0F0F;
+                w[2] = nib.z & 0x0F0F0F0F;
+                w[3] = nib.w & 0x0F0F0F0F;
+                w[4] = (nib.x >> 4) & 0x0F0F0F0F;
+                w[5] = (nib.y >> 4) & 0x0F0F0F0F;
+                w[6] = (nib.z >> 4) & 0x0F0F0F0F;
+                w[7] = (nib.w >> 4) & 0x0F0F0F0F;
+            } else {
+                uint4 q0 = *reinterpret_cast<const uint4*>(rec + lane * QB);
+                uint4 q1 = *reinterpret_cast<const uint4*>(rec + lane * QB + 16);
+                w[0] = q0.x; w[1] = q0.y; w[2] = q0.z; w[3] = q0.w;
+                w[4] = q1.x; w[5] = q1.y; w[6] = q1.z; w[7] = q1.w;
+            }
+#pragma unroll
+            for (int j = 0; j < TG; j++) {
+                const int8_t* xp = xq + (size_t)xr[j] * cols + b * kQK;
+                uint4 xa = __ldg(reinterpret_cast<const uint4*>(xp));
+                uint4 xb = __ldg(reinterpret_cast<const uint4*>(xp + 16));
+                int2 ax = __ldg(xaux + (size_t)xr[j] * nb + b);
+                int s = (QT == 0) ? ax.y : 0;
+                s = __dp4a(w[0], (int)xa.x, s);
+                s = __dp4a(w[1], (int)xa.y, s);
+                s = __dp4a(w[2], (int)xa.z, s);
+                s = __dp4a(w[3], (int)xa.w, s);
+                s = __dp4a(w[4], (int)xb.x, s);
+                s = __dp4a(w[5], (int)xb.y, s);
+                s = __dp4a(w[6], (int)xb.z, s);
+                s = __dp4a(w[7], (int)xb.w, s);
+                if (dbg && j < nvalid) dbg[(size_t)xr[j] * dbg_row_stride + (size_t)lane * nb + b] = s;
+                acc[j] = fadd(acc[j], fmul(fmul(ws, __int_as_float(ax.x)), __int2float_rn(s)));
+            }
+        }
+        __syncwarp();
+        if (st + rg.S < nst && lane == 0) {
+            fence_proxy_async_smem();
+            ring_issue<QT>(rg, gtile, nb, st + rg.S);
+        }
+    }
+    __syncwarp();
+    return ok;
+}
+
+__device__ __forceinline__ void ring_init(Ring& rg, uint8_t* smem, int S, int stage_bytes) {
+    rg.buf = smem;
+    rg.bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    rg.S = S;
+    rg.stage_bytes = stage_bytes;
+    rg.phase = 0;
+    if ((threadIdx.x & 31) == 0) {
+        for (int s = 0; s < S; s++) mbar_init(&rg.bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+}
+
+// Runs the tile dot over `count` activation rows given by row_of(j) in passes
+// of <= 32, calling emit(j, value) for each (lane = tile row). The pass
+// width is the smallest power of two covering the remaining rows.
+template <int QT, int TG, class RowOf, class Emit>
+__device__ bool tile_pass(Ring& rg, const uint8_t* gtile, int nb, const int8_t* xq,
+                          const int2* xaux, int cols, int base, int n, RowOf row_of, Emit emit,
+                          int32_t* dbg, size_t dbg_row_stride, uint32_t* err) {
+    int xr[TG];
+    float acc[TG];
+#pragma unroll
+    for (int j = 0; j < TG; j++) xr[j] = row_of(base + (j < n ? j : 0));
+    bool ok = tile_dot<QT, TG>(rg, gtile, nb, xq, xaux, cols, xr, n, acc, dbg, dbg_row_stride, err);
+    if (ok) {
+#pragma unroll
+        for (int j = 0; j < TG; j++)
+            if (j < n) emit(base + j, acc[j]);
+    }
+    return ok;
+}
+
+// All `count` activation rows, in passes of at most TGMAX rows; each pass
+// uses the smallest power-of-two width that covers it. TGMAX is a launch
+// parameter (the largest row count any tile can see), so small-batch
+// launches are compiled with few registers.
+template <int QT, int TGMAX, class RowOf, class Emit>
+__device__ bool tile_all_rows(Ring& rg, const uint8_t* gtile, int nb, const int8_t* xq,
+                              const int2* xaux, int cols, int count, RowOf row_of, Emit emit,
+                              int32_t* dbg, size_t dbg_row_stride, uint32_t* err) {
+    bool ok = true;
+    for (int base = 0; base < count && ok; base += TGMAX) {
+        int n = min(TGMAX, count - base);
+        if (n <= 1 || TGMAX == 1)
+            ok = tile_pass<QT, 1>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+        else if (n <= 2 || TGMAX == 2)
+            ok = tile_pass<QT, 2>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+        else if (n <= 4 || TGMAX == 4)
+            ok = tile_pass<QT, 4>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+        else if (n <= 8 || TGMAX == 8)
+            ok = tile_pass<QT, 8>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+        else if (n <= 16 || TGMAX == 16)
+            ok = tile_pass<QT, 16>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+        else
+            ok = tile_pass<QT, 32>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
+    }
+    return ok;
+}
+
+// ---------------------------------------------------------------------------
+// WeightMatrix::matvec for quantized matrices (matrix.rs:115-126): one warp
+// per row tile, all activation rows. dbg: block sums [M, rows_pad, nb].
+// ---------------------------------------------------------------------------
+template <int QT, int TGMAX>
+__global__ void __launch_bounds__(32) qgemv_kernel(const uint8_t* __restrict__ W, int rows, int nb,
+                                                   const int8_t* __restrict__ xq,
+                                                   const int2* __restrict__ xaux, int M,
+                                                   float* __restrict__ out, int32_t* dbg,
+                                                   int S, uint32_t* err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int REC = kTileRows * QFmt<QT>::BB;
+    const int g = blockIdx.x, lane = threadIdx.x & 31, cols = nb * kQK;
+    Ring rg;
+    ring_init(rg, smem, S, kStageBlocks * REC);
+    const uint8_t* gtile = W + (size_t)g * nb * REC;
+    const int row = g * kTileRows + lane;
+    // block sums [M, rows, nb]; rows of the padded tail are not written
+    int32_t* dbg_base = (dbg && row < rows) ? dbg + (size_t)g * kTileRows * nb : nullptr;
+    tile_all_rows<QT, TGMAX>(
+        rg, gtile, nb, xq, xaux, cols, M, [](int j) { return j; },
+        [&](int j, float v) {
+            if (row < rows) out[(size_t)j * rows + row] = v;
+        },
+        dbg_base, (size_t)rows * nb, err);
+}
+
+// ---------------------------------------------------------------------------
+// Router: MoeLayer::route (src/model/moe.rs:36-53).
+//
+// Logits: each (token, expert) pair is 8 threads, thread l owning the
+// reference's accumulator lane l (quant.rs:152-160): acc += w[8i+l]*x[8i+l]
+// over i in order, then reduce() (quant.rs:37-41) and the tail. The last CTA
+// to finish a token tile then runs softmax (activation.rs:11-21), top-k with
+// (score desc, index asc) (topk.rs:27-61), the weight normalisation, and
+// quantizes the tile's activation rows. The last such CTA of the grid
+// groups the routes by expert for the expert kernels.
+// ---------------------------------------------------------------------------
+struct RouterArgs {
+    const void* w;
+    int wdtype;  // 0 f32, 1 f16, 2 bf16
+    int E, H, M, k, normalize, TT, ET;
+    const float* x;
+    float* logits;          // [M, E]
+    float* probs_out;       // [M, E] nullable
+    int* topk_idx;          // [M, k]
+    float* topk_w;          // [M, k]
+    int* user_idx;          // nullable copies for the caller
+    float* user_w;
+    int8_t* xq;             // [M, H] nullable (route-only calls skip it)
+    int2* xaux;             // [M, H/32]
+    int* elist_off;         // [E + 1]   (nullable: route-only)
+    int* elist;             // [M * k]
+    int* active;            // [E]
+    int* n_active;          // [1]
+    unsigned long long* routing_counts;  // [E] nullable
+    unsigned* tile_cnt;     // [ceil(M / TT)]
+    unsigned* grid_cnt;     // [1]
+};
+
+__device__ __forceinline__ float load_w(const void* w, int dt, size_t i) {
+    if (dt == 0) return __ldg(reinterpret_cast<const float*>(w) + i);
+    uint16_t h = __ldg(reinterpret_cast<const unsigned short*>(w) + i);
+    if (dt == 2) return __uint_as_float((uint32_t)h << 16);
+    return half_bits_to_float(h);
+}
+
+__global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
+    __shared__ unsigned s_flag;
+    __shared__ float s_e[8][256];
+    __shared__ int s_cnt[256];
+    __shared__ int s_cur[256];
+    const int tid = threadIdx.x, lane8 = tid & 7, pair = tid >> 3;
+    const int t = blockIdx.x * a.TT + pair / a.ET;
+    const int e = blockIdx.y * a.ET + pair % a.ET;
+    const bool valid = (pair / a.ET) < a.TT && t < a.M && e < a.E;
+    const int full = a.H / 8;
+    float acc = 0.0f;
+    if (valid) {
+        const float* xt = a.x + (size_t)t * a.H;
+        size_t wrow = (size_t)e * a.H;
+#pragma unroll 8
+        for (int i = 0; i < full; i++) {
+            int c = 8 * i + lane8;
+            acc = fadd(acc, fmul(load_w(a.w, a.wdtype, wrow + c), __ldg(xt + c)));
+        }
+    }
+    // reduce(): ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+    float s = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
+    float p = fadd(s, __shfl_down_sync(0xffffffffu, s, 1, 8));
+    float r = fadd(p, __shfl_down_sync(0xffffffffu, p, 2, 8));
+    if (valid && lane8 == 0) {
+        float tail = -0.0f;
+        const float* xt = a.x + (size_t)t * a.H;
+        for (int c = full * 8; c < a.H; c++)
+            tail = fadd(tail, fmul(load_w(a.w, a.wdtype, (size_t)e * a.H + c), xt[c]));
+        a.logits[(size_t)t * a.E + e] = fadd(r, tail);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_flag = (atomicAdd(&a.tile_cnt[blockIdx.x], 1u) == gridDim.y - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!s_flag) return;
+    __threadfence();
+
+    // ---- last CTA of this token tile: softmax, top-k, quantize ----------
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int tt = warp; tt < a.TT; tt += 8) {
+        const int tok = blockIdx.x * a.TT + tt;
+        if (tok >= a.M) break;
+        const float* lg = a.logits + (size_t)tok * a.E;
+        float mx = -__int_as_float(0x7f800000);
+        for (int i = lane; i < a.E; i += 32) mx = fmaxf(mx, __ldcg(lg + i));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int i = lane; i < a.E; i += 32) s_e[warp][i] = hale_expf(fsub(__ldcg(lg + i), mx));
+        __syncwarp();
+        float sum = 0.0f;
+        if (lane == 0)
+            for (int i = 0; i < a.E; i++) sum = fadd(sum, s_e[warp][i]);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        __syncwarp();
+        for (int i = lane; i < a.E; i += 32) {
+            float pv = fdiv(s_e[warp][i], sum);
+            s_e[warp][i] = pv;
+            if (a.probs_out) a.probs_out[(size_t)tok * a.E + i] = pv;
+        }
+        __syncwarp();
+        // top-k by (total_cmp desc, index asc)
+        unsigned taken = 0u;  // bit j: element lane + 32 j selected (E <= 256)
+        float chosen_score = 0.0f;
+        int chosen_idx = -1;
+        float norm = -0.0f;
+        for (int kk = 0; kk < a.k; kk++) {
+            int bk = INT_MIN, bi = INT_MAX;
+            for (int j = 0, i = lane; i < a.E; j++, i += 32) {
+                if (taken & (1u << j)) continue;
+                int key = total_key(s_e[warp][i]);
+                if (key > bk || (key == bk && i < bi)) { bk = key; bi = i; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                int ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ok2 > bk || (ok2 == bk && oi < bi)) { bk = ok2; bi = oi; }
+            }
+            if (bi != INT_MAX && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+            float sc = s_e[warp][bi];
+            norm = fadd(norm, sc);
+            if (lane == kk) { chosen_score = sc; chosen_idx = bi; }
+        }
+        if (lane < a.k) {
+            float wv = a.normalize ? fdiv(chosen_score, norm) : fdiv(chosen_score, 1.0f);
+            a.topk_idx[(size_t)tok * a.k + lane] = chosen_idx;
+            a.topk_w[(size_t)tok * a.k + lane] = wv;
+            if (a.user_idx) a.user_idx[(size_t)tok * a.k + lane] = chosen_idx;
+            if (a.user_w) a.user_w[(size_t)tok * a.k + lane] = wv;
+        }
+        // Q8Activations::quantize of this token (quant.rs:77-93)
+        if (a.xq) {
+            const int nb = a.H / kQK;
+            for (int b = lane; b < nb; b += 32) {
+                float sc;
+                int sm;
+                quantize_block(a.x + (size_t)tok * a.H + b * kQK, a.xq + (size_t)tok * a.H + b * kQK, &sc, &sm);
+                a.xaux[(size_t)tok * nb + b] = make_int2(__float_as_int(sc), -8 * sm);
+            }
+        }
+        __syncwarp();
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        a.tile_cnt[blockIdx.x] = 0u;
+        s_flag = (atomicAdd(a.grid_cnt, 1u) == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_flag || !a.elist_off) {
+        if (s_flag && tid == 0) *a.grid_cnt = 0u;
+        return;
+    }
+    __threadfence();
+
+    // ---- last CTA of the grid: group routes by expert ----------------------
+    const int R = a.M * a.k;
+    for (int i = tid; i < a.E; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < R; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topk_idx + i)], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int off = 0, na = 0;
+        for (int i = 0; i < a.E; i++) {
+            a.elist_off[i] = off;
+            s_cur[i] = off;
+            if (s_cnt[i] > 0) a.active[na++] = i;
+            if (a.routing_counts && s_cnt[i] > 0) a.routing_counts[i] += (unsigned long long)s_cnt[i];
+            off += s_cnt[i];
+        }
+        a.elist_off[a.E] = off;
+        *a.n_active = na;
+    }
+    __syncthreads();
+    for (int i = tid; i < R; i += blockDim.x) {
+        int ex = __ldcg(a.topk_idx + i);
+        int pos = atomicAdd(&s_cur[ex], 1);
+        a.elist[pos] = i;
+    }
+    if (tid == 0) *a.grid_cnt = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Expert kernels: Expert::forward (src/expert/mod.rs:91-103) for all routes
+// of the layer, grouped by expert so each weight tile is read from HBM once
+// for every token routed to it.
+// ---------------------------------------------------------------------------
+struct ExpertArgs {
+    const uint8_t* experts;   // layer base: E experts, each [gate tiles][up tiles][down tiles]
+    size_t expert_stride;     // bytes per expert
+    int H, I, k, M;
+    const int* elist_off;
+    const int* elist;
+    const int* active;
+    const int* n_active;
+    const int8_t* xq;         // [M, H]
+    const int2* xaux;         // [M, H/32]
+    float* gu;                // [M*k, 2, I]
+    unsigned* gu_cnt;         // [E, I/32]
+    int8_t* hq;               // [M*k, I]
+    int2* haux;               // [M*k, I/32]
+    float* ybuf;              // [M*k, H]
+    unsigned* comb_cnt;       // [M, H/32]
+    const float* topk_w;      // [M, k]
+    float* out;               // [M, H]
+    int S;
+    uint32_t* err;
+};
+
+// Phase 1: one CTA (one warp) per (active expert, gate|up, 32-row tile).
+// The second of the gate/up pair to finish forms h = silu(g) * u for its 32
+// rows and quantizes it (the 32 rows are exactly one q8 block of h, which
+// the reference re-quantizes before the down projection, matrix.rs:119-121).
+template <int QT, int TGMAX>
+__global__ void __launch_bounds__(32) expert_gate_up_kernel(ExpertArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int REC = kTileRows * QFmt<QT>::BB;
+    const int TI = a.I / kTileRows, nbh = a.H / kQK;
+    const int per_expert = 2 * TI;
+    const int u = blockIdx.x, ai = u / per_expert;
+    if (ai >= *a.n_active) return;
+    const int m = (u % per_expert) / TI, g = (u % per_expert) % TI;
+    const int e = a.active[ai];
+    const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
+    const int lane = threadIdx.x & 31;
+    const size_t tile_bytes = (size_t)nbh * REC;
+    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)(m * TI + g) * tile_bytes;
+    Ring rg;
+    ring_init(rg, smem, a.S, kStageBlocks * REC);
+    const int* routes = a.elist + beg;
+    const int k = a.k;
+    bool ok = tile_all_rows<QT, TGMAX>(
+        rg, gtile, nbh, a.xq, a.xaux, a.H, T, [&](int j) { return routes[j] / k; },
+        [&](int j, float v) {
+            a.gu[((size_t)routes[j] * 2 + m) * a.I + g * kTileRows + lane] = v;
+        },
+        nullptr, 0, a.err);
+    if (!ok) return;
+    __threadfence();
+    __syncwarp();
+    unsigned old = 0;
+    if (lane == 0) old = atomicAdd(&a.gu_cnt[e * TI + g], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != 1u) return;
+    __threadfence();
+    if (lane == 0) a.gu_cnt[e * TI + g] = 0u;
+    const int nbi = a.I / kQK;
+    for (int j = 0; j < T; j++) {
+        const int r = routes[j];
+        float gv = __ldcg(a.gu + ((size_t)r * 2 + 0) * a.I + g * kTileRows + lane);
+        float uv = __ldcg(a.gu + ((size_t)r * 2 + 1) * a.I + g * kTileRows + lane);
+        float h = fmul(silu(gv), uv);  // expert/mod.rs:100-102
+        float amax = warp_max_abs(h);
+        float scale = fdiv(amax, 127.0f);
+        float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
+        int q = sat_i8(roundf(fmul(h, inv)));
+        int qs = warp_sum_int(q);
+        a.hq[(size_t)r * a.I + g * kTileRows + lane] = (int8_t)q;
+        if (lane == 0) a.haux[(size_t)r * nbi + g] = make_int2(__float_as_int(scale), -8 * qs);
+    }
+}
+
+// Phase 2: one CTA per (active expert, 32-row tile of the down projection);
+// y for every route of the expert. The last of a token's k routes to land
+// for a tile combines them in best-first order (moe.rs:63-68):
+// out = 0; out += w_s * y_s for s = 0..k-1, unfused.
+template <int QT, int TGMAX>
+__global__ void __launch_bounds__(32) expert_down_kernel(ExpertArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int REC = kTileRows * QFmt<QT>::BB;
+    const int TI = a.I / kTileRows, TH = a.H / kTileRows, nbi = a.I / kQK, nbh = a.H / kQK;
+    const int u = blockIdx.x, ai = u / TH, g = u % TH;
+    if (ai >= *a.n_active) return;
+    const int e = a.active[ai];
+    const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
+    const int lane = threadIdx.x & 31;
+    const size_t gu_tile = (size_t)nbh * REC;
+    const size_t d_tile = (size_t)nbi * REC;
+    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)2 * TI * gu_tile + (size_t)g * d_tile;
+    Ring rg;
+    ring_init(rg, smem, a.S, kStageBlocks * REC);
+    const int* routes = a.elist + beg;
+    bool ok = tile_all_rows<QT, TGMAX>(
+        rg, gtile, nbi, a.hq, a.haux, a.I, T, [&](int j) { return routes[j]; },
+        [&](int j, float v) { a.ybuf[(size_t)routes[j] * a.H + g * kTileRows + lane] = v; },
+        nullptr, 0, a.err);
+    if (!ok) return;
+    __threadfence();
+    __syncwarp();
+    const int k = a.k;
+    for (int j = 0; j < T; j++) {
+        const int r = routes[j], tok = r / k;
+        unsigned old = 0;
+        if (lane == 0) old = atomicAdd(&a.comb_cnt[(size_t)tok * TH + g], 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old != (unsigned)(k - 1)) continue;
+        __threadfence();
+        if (lane == 0) a.comb_cnt[(size_t)tok * TH + g] = 0u;
+        float o = 0.0f;
+        for (int s = 0; s < k; s++) {
+            float w = __ldcg(a.topk_w + (size_t)tok * k + s);
+            float y = __ldcg(a.ybuf + ((size_t)tok * k + s) * a.H + g * kTileRows + lane);
+            o = fadd(o, fmul(w, y));
+        }
+        a.out[(size_t)tok * a.H + g * kTileRows + lane] = o;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Float GEMV (quant.rs:146-202 via matrix.rs:115-126): lm_head and float
+// WeightMatrix::matvec. One thread per row owning all 8 accumulator lanes;
+// steps i over the full groups of 8 in order, then reduce() + tail.
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ __forceinline__ void load8(const uint8_t* p, float (&w)[8]) {
+    if (DT == 0) {
+        float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+        w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    } else {
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint16_t lo = (uint16_t)(u[q] & 0xffffu), hi = (uint16_t)(u[q] >> 16);
+            if (DT == 2) {
+                w[2 * q] = __uint_as_float((uint32_t)lo << 16);
+                w[2 * q + 1] = __uint_as_float((uint32_t)hi << 16);
+            } else {
+                w[2 * q] = half_bits_to_float(lo);
+                w[2 * q + 1] = half_bits_to_float(hi);
+            }
+        }
+    }
+}
+
+template <int DT, int TG>
+__global__ void __launch_bounds__(128) fgemv_kernel(const uint8_t* __restrict__ W, int rows,
+                                                    int cols, int steps,
+                                                    const float* __restrict__ x, int M,
+                                                    float* __restrict__ out, int vec_x) {
+    constexpr int ES = DT == 0 ? 4 : 2;
+    const int g = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int rows_pad = (rows + 31) / 32 * 32;
+    if (g * kTileRows >= rows_pad) return;
+    const int row = g * kTileRows + lane;
+    const int full = cols / 8, rem = cols % 8;
+    const uint8_t* base = W + ((size_t)g * steps * kTileRows + lane) * 8 * ES;
+    for (int t0 = 0; t0 < M; t0 += TG) {
+        float acc[TG][8];
+#pragma unroll
+        for (int j = 0; j < TG; j++)
+#pragma unroll
+            for (int l = 0; l < 8; l++) acc[j][l] = 0.0f;
+#pragma unroll 2
+        for (int i = 0; i < full; i++) {
+            float w[8];
+            load8<DT>(base + (size_t)i * kTileRows * 8 * ES, w);
+#pragma unroll
+            for (int j = 0; j < TG; j++) {
+                const float* xp = x + (size_t)min(t0 + j, M - 1) * cols + 8 * i;
+                float xv[8];
+                if (vec_x) {
+                    float4 a = __ldg(reinterpret_cast<const float4*>(xp));
+                    float4 b = __ldg(reinterpret_cast<const float4*>(xp) + 1);
+                    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                    xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+                } else {
+#pragma unroll
+                    for (int l = 0; l < 8; l++) xv[l] = __ldg(xp + l);
+                }
+#pragma unroll
+                for (int l = 0; l < 8; l++) acc[j][l] = fadd(acc[j][l], fmul(w[l], xv[l]));
+            }
+        }
+        float wt[8];
+        if (rem) load8<DT>(base + (size_t)full * kTileRows * 8 * ES, wt);
+#pragma unroll
+        for (int j = 0; j < TG; j++) {
+            if (t0 + j >= M) break;
+            float tail = -0.0f;
+            const float* xp = x + (size_t)(t0 + j) * cols + 8 * full;
+            for (int l = 0; l < rem; l++) tail = fadd(tail, fmul(wt[l], __ldg(xp + l)));
+            float a0 = fadd(fadd(acc[j][0], acc[j][4]), fadd(acc[j][1], acc[j][5]));
+            float a1 = fadd(fadd(acc[j][2], acc[j][6]), fadd(acc[j][3], acc[j][7]));
+            if (row < rows) out[(size_t)(t0 + j) * rows + row] = fadd(fadd(a0, a1), tail);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Sampler (src/generate/sampler.rs): one CTA of 1024 threads per row.
+//   temperature <= 0: argmax, first maximum wins (activation.rs:24-32).
+//   otherwise (sampler.rs:80-123): the top_k best logits (ties: lower index
+//   first), sorted best-first; e_i = exp((l_i - max) / T) summed in order;
+//   nucleus cut at the first prefix whose running mass reaches top_p; draw
+//   r = next_f32() * kept_total and walk down. xorshift64* state per row.
+// Repetition penalty (extension) is applied to each seen id first.
+// ---------------------------------------------------------------------------
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleMaxK = 1024;
+
+struct SampleArgs {
+    const float* logits;
+    int V;
+    float temperature, top_p, penalty;
+    int top_k;  // already clamped: 1..min(V, kSampleMaxK), or V when V <= kSampleMaxK
+    uint64_t* rng;
+    const int32_t* seen;
+    int n_seen;
+    int32_t* out;
+};
+
+__device__ __forceinline__ float penalized(const float* lg, const uint32_t* bits, int i, float p) {
+    float l = lg[i];
+    if (bits && (bits[i >> 5] >> (i & 31)) & 1u) l = l > 0.0f ? fdiv(l, p) : fmul(l, p);
+    return l;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    // layout: [penalty bitmap (V/32 words, when used)] ...
+    __shared__ unsigned s_hist[256];
+    __shared__ int s_ctl[8];
+    __shared__ unsigned long long s_key[kSampleMaxK];
+    __shared__ float s_val[kSampleMaxK];
+    const int row = blockIdx.x, tid = threadIdx.x, V = a.V;
+    const float* lg = a.logits + (size_t)row * V;
+    uint32_t* bits = nullptr;
+    if (a.seen && a.n_seen > 0 && a.penalty != 1.0f) {
+        bits = reinterpret_cast<uint32_t*>(smem);
+        for (int i = tid; i < (V + 31) / 32; i += blockDim.x) bits[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < a.n_seen; i += blockDim.x) {
+            int id = a.seen[(size_t)row * a.n_seen + i];
+            if (id >= 0 && id < V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+        }
+    }
+    __syncthreads();
+
+    if (a.temperature <= 0.0f) {
+        // argmax: strict '>' scan from index 0; NaN never wins, and a NaN at
+        // index 0 is never beaten.
+        float bv = -__int_as_float(0x7f800000);
+        int bi = INT_MAX;
+        for (int i = tid; i < V; i += blockDim.x) {
+            float v = penalized(lg, bits, i, a.penalty);
+            if (v == v && (bi == INT_MAX || v > bv)) { bv = v; bi = i; }
+        }
+        // block reduce: larger value, then lower index
+        __shared__ float r_v[32];
+        __shared__ int r_i[32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        if ((tid & 31) == 0) { r_v[tid >> 5] = bv; r_i[tid >> 5] = bi; }
+        __syncthreads();
+        if (tid < 32) {
+            bv = r_v[tid];
+            bi = r_i[tid];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+            }
+            if (tid == 0) {
+                float v0 = penalized(lg, bits, 0, a.penalty);
+                a.out[row] = (v0 != v0 || bi == INT_MAX) ? 0 : bi;
+            }
+        }
+        return;
+    }
+
+    // ---- candidates: the top_k by (key desc, index asc) ---------------------
+    const int K = a.top_k;
+    // Radix-select the K-th largest ordered key (uk = key ^ 0x80000000).
+    unsigned prefix = 0u, pmask = 0u;
+    int need = K;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += blockDim.x) s_hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < V; i += blockDim.x) {
+            unsigned uk = (unsigned)total_key(penalized(lg, bits, i, a.penalty)) ^ 0x80000000u;
+            if ((uk & pmask) == prefix) atomicAdd(&s_hist[(uk >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0, d = 255;
+            for (; d > 0; d--) {
+                if (acc + (int)s_hist[d] >= need) break;
+                acc += (int)s_hist[d];
+            }
+            s_ctl[0] = d;
+            s_ctl[1] = need - acc;
+        }
+        __syncthreads();
+        prefix |= (unsigned)s_ctl[0] << shift;
+        pmask |= 255u << shift;
+        need = s_ctl[1];
+        __syncthreads();
+    }
+    // Threshold key `prefix`; take every key above it and the `need` lowest
+    // indices equal to it. Contiguous chunks per thread keep index order.
+    const int chunk = (V + blockDim.x - 1) / blockDim.x;
+    const int lo = tid * chunk, hi = min(V, lo + chunk);
+    int n_gt = 0, n_eq = 0;
+    for (int i = lo; i < hi; i++) {
+        unsigned uk = (unsigned)total_key(penalized(lg, bits, i, a.penalty)) ^ 0x80000000u;
+        n_gt += uk > prefix;
+        n_eq += uk == prefix;
+    }
+    // exclusive scans of n_gt and n_eq over threads (in index order)
+    __shared__ int w_gt[32], w_eq[32];
+    int lane = tid & 31, warp = tid >> 5;
+    int sg = n_gt, se = n_eq;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int tg = __shfl_up_sync(0xffffffffu, sg, o), te = __shfl_up_sync(0xffffffffu, se, o);
+        if (lane >= o) { sg += tg; se += te; }
+    }
+    if (lane == 31) { w_gt[warp] = sg; w_eq[warp] = se; }
+    __syncthreads();
+    if (tid == 0) {
+        int cg = 0, ce = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+            int tg = w_gt[w], te = w_eq[w];
+            w_gt[w] = cg; w_eq[w] = ce;
+            cg += tg; ce += te;
+        }
+        s_ctl[2] = cg;  // total strictly greater
+    }
+    __syncthreads();
+    int pos_gt = w_gt[warp] + sg - n_gt, pos_eq = w_eq[warp] + se - n_eq;
+    const int total_gt = s_ctl[2];
+    for (int i = lo; i < hi; i++) {
+        float v = penalized(lg, bits, i, a.penalty);
+        unsigned uk = (unsigned)total_key(v) ^ 0x80000000u;
+        int slot = -1;
+        if (uk > prefix) slot = pos_gt++;
+        else if (uk == prefix) { if (pos_eq < need) slot = total_gt + pos_eq; pos_eq++; }
+        if (slot >= 0 && slot < K) {
+            // sort key: ordered key high, inverted index low -> descending
+            s_key[slot] = ((unsigned long long)uk << 32) | (unsigned)(0x7fffffff - i);
+            s_val[slot] = v;
+        }
+    }
+    // pad to a power of two for the bitonic sort
+    int P = 1;
+    while (P < K) P <<= 1;
+    for (int i = K + tid; i < P; i += blockDim.x) { s_key[i] = 0ull; s_val[i] = 0.0f; }
+    __syncthreads();
+    // bitonic sort, descending by s_key
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < P; i += blockDim.x) {
+                int j = i ^ stride;
+                if (j > i) {
+                    bool desc = (i & size) == 0;
+                    unsigned long long ki = s_key[i], kj = s_key[j];
+                    if (desc ? (ki < kj) : (ki > kj)) {
+                        s_key[i] = kj; s_key[j] = ki;
+                        float t = s_val[i]; s_val[i] = s_val[j]; s_val[j] = t;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // softmax with temperature over the survivors (sampler.rs:96-101)
+    const float mx = s_val[0];
+    for (int i = tid; i < K; i += blockDim.x) s_val[i] = hale_expf(fdiv(fsub(s_val[i], mx), a.temperature));
+    __syncthreads();
+    if (tid == 0) {
+        float total = 0.0f;
+        for (int i = 0; i < K; i++) total = fadd(total, s_val[i]);
+        float mass = 0.0f;
+        int keep = K;
+        for (int i = 0; i < K; i++) {
+            mass = fadd(mass, fdiv(s_val[i], total));
+            if (mass >= a.top_p) { keep = i + 1; break; }
+        }
+        float kept = -0.0f;
+        for (int i = 0; i < keep; i++) kept = fadd(kept, s_val[i]);
+        uint64_t st = a.rng[row];
+        st ^= st >> 12;
+        st ^= st << 25;
+        st ^= st >> 27;
+        a.rng[row] = st;
+        uint64_t u = st * 0x2545F4914F6CDD1DULL;
+        float r = fmul(fdiv((float)(u >> 40), 16777216.0f), kept);
+        int pick = 0x7fffffff - (int)(unsigned)(s_key[keep - 1] & 0xffffffffull);
+        for (int i = 0; i < keep; i++) {
+            r = fsub(r, s_val[i]);
+            if (r <= 0.0f) {
+                pick = 0x7fffffff - (int)(unsigned)(s_key[i] & 0xffffffffull);
+                break;
+            }
+        }
+        a.out[row] = pick;
+    }
+}
+
+}  // namespace hale

@@ -1,0 +1,261 @@
+/*
+ * hale_cuda.h -- C ABI of the B200 (sm_100a) implementation of Hale-Token's
+ * MoE quantized-expert forward and sampling tail.
+ *
+ * The entry points replace the Rust reference's operator surface on this
+ * path (paths relative to the reference crate):
+ *   ExpertProvider / ExpertCache ........ src/expert/mod.rs:128-137, src/expert/cache.rs:124-203
+ *   ExpertSource::load (pack record) .... src/expert/pack.rs:264-271
+ *   WeightMatrix::new / matvec .......... src/tensor/matrix.rs:29-45, 115-126
+ *   Q8Activations::quantize ............. src/tensor/quant.rs:77-93
+ *   quant::dot_quantized ................ src/tensor/quant.rs:107-144
+ *   MoeLayer::route / forward ........... src/model/moe.rs:36-70
+ *   Transformer::logits (lm_head) ....... src/model/transformer.rs:217-221
+ *   Sampler::sample / SamplingParams .... src/generate/sampler.rs:7-123
+ *
+ * Conventions (mirroring the reference):
+ *   - Every function returns hale_status: 0 = OK, negative = error. Negative
+ *     codes mirror HaleError kinds (src/error.rs:10-57) plus CUDA / timeout
+ *     codes. Nothing panics or aborts across this boundary; a message for
+ *     the last failure is available from hale_last_error().
+ *   - Buffers are caller-owned. Unless a name ends in _host, data pointers
+ *     are DEVICE pointers on the context's GPU, and work is enqueued on the
+ *     given stream (a cudaStream_t passed as void*; NULL = legacy stream).
+ *   - A hale_ctx is bound to one GPU. Calls on one ctx must not overlap
+ *     (the ctx owns one workspace); use one ctx per host thread / stream.
+ *   - Results are deterministic: bit-identical run to run, and bit-identical
+ *     to the reference's CPU arithmetic (f32, no FMA contraction, glibc expf)
+ *     for the quantized expert path, router top-k and greedy sampling.
+ */
+#ifndef HALE_CUDA_H
+#define HALE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define HALE_API __attribute__((visibility("default")))
+#else
+#define HALE_API
+#endif
+
+typedef int32_t hale_status;
+
+/* Status codes. The first group mirrors HaleError (src/error.rs:10-57). */
+#define HALE_OK 0
+#define HALE_E_INVALID_ARGUMENT (-1) /* HaleError::InvalidArgument */
+#define HALE_E_BAD_TENSOR (-2)       /* HaleError::BadTensor */
+#define HALE_E_IO (-3)               /* HaleError::Io */
+#define HALE_E_CONTEXT_OVERFLOW (-4) /* HaleError::ContextOverflow */
+#define HALE_E_CUDA (-10)            /* a CUDA runtime call failed */
+#define HALE_E_NO_DEVICE (-11)       /* no usable sm_100 device */
+#define HALE_E_OUT_OF_MEMORY (-12)   /* device allocation failed */
+#define HALE_E_TIMEOUT (-13)         /* a device-side wait hit its bound */
+#define HALE_E_DEVICE_CHECK (-14)    /* a device-side bounds check tripped */
+#define HALE_E_UNSUPPORTED (-15)     /* valid request this build does not serve */
+
+/* Storage formats, same discriminants as DType (src/tensor/dtype.rs:15-25). */
+typedef enum {
+    HALE_F32 = 0,
+    HALE_F16 = 1,
+    HALE_BF16 = 2,
+    HALE_Q8_0 = 3, /* 34-byte blocks: f16 scale + 32 x i8 */
+    HALE_Q4_0 = 4  /* 18-byte blocks: f16 scale + 16 B nibbles (j | j+16) */
+} hale_dtype;
+
+typedef struct hale_ctx hale_ctx;       /* one GPU + workspace */
+typedef struct hale_matrix hale_matrix; /* a WeightMatrix resident in HBM */
+typedef struct hale_pool hale_pool;     /* HBM-resident expert store */
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Binds to CUDA device `device` (must be compute capability 10.x). */
+HALE_API hale_status hale_ctx_create(int device, hale_ctx** out);
+HALE_API void hale_ctx_destroy(hale_ctx* ctx);
+/* Copies the message of the last failure on `ctx` (or, with ctx == NULL, of
+ * the last failure on this host thread) into buf. Returns its status. */
+HALE_API hale_status hale_last_error(const hale_ctx* ctx, char* buf, size_t len);
+/* Waits for the ctx's work on `stream` and reports device-side errors
+ * (HALE_E_TIMEOUT / HALE_E_DEVICE_CHECK) raised by kernels since the last
+ * check; clears them. */
+HALE_API hale_status hale_ctx_check(hale_ctx* ctx, void* stream);
+/* Number of this library's kernels launched on ctx so far. */
+HALE_API uint64_t hale_ctx_launch_count(const hale_ctx* ctx);
+/* Per-kernel timing: while enabled, every launch on ctx is bracketed by a
+ * pair of CUDA events on its stream. hale_ctx_profile_read synchronises,
+ * and returns the launches and summed device milliseconds recorded for the
+ * kernel family `kernel` ("router", "expert_gate_up", "expert_down",
+ * "qgemv", "fgemv", "sample", ...) since the last reset, then resets it. */
+HALE_API hale_status hale_ctx_profile(hale_ctx* ctx, int enable);
+HALE_API hale_status hale_ctx_profile_read(hale_ctx* ctx, const char* kernel, uint64_t* launches,
+                                           double* total_ms);
+
+/* ---- formats (src/tensor/dtype.rs) ---------------------------------------- */
+
+/* DType::row_bytes (dtype.rs:53-61); returns -1 when cols is not a
+ * multiple of the block length or dtype is unknown. */
+HALE_API int64_t hale_row_bytes(hale_dtype dtype, uint64_t cols);
+
+/* ---- weight matrices (src/tensor/matrix.rs) ------------------------------- */
+
+/* WeightMatrix::new (matrix.rs:29-45): takes `rows` encoded rows (the
+ * reference byte layout: row-major, GGML blocks for q8_0/q4_0) from
+ * `encoded` (device memory when on_device != 0, else host memory), checks
+ * the byte count and repacks them into the GPU tile layout. */
+HALE_API hale_status hale_matrix_create(hale_ctx* ctx, hale_dtype dtype, uint32_t rows, uint32_t cols,
+                               const void* encoded, uint64_t encoded_bytes, int on_device,
+                               hale_matrix** out);
+HALE_API void hale_matrix_destroy(hale_matrix* m);
+
+/* WeightMatrix::matvec (matrix.rs:115-126) for `m_rows` independent inputs:
+ * out[t, r] = dot(row r, x[t, :]). x is [m_rows, cols] f32, out is
+ * [m_rows, rows] f32 (device). Quantized matrices quantize each x row once
+ * (quant.rs:77-93), exactly like the reference. block_sums (nullable,
+ * quantized only) receives the int32 block dot products
+ * [m_rows, rows, cols/32] -- the bit-exact intermediate of dot_q8_0 /
+ * dot_q4_0 (quant.rs:115-144). */
+HALE_API hale_status hale_matrix_matvec(hale_ctx* ctx, const hale_matrix* m, const float* x,
+                               uint32_t m_rows, float* out, int32_t* block_sums, void* stream);
+
+/* quant::dot_quantized applied to every row with caller-supplied quantized
+ * activations (Q8Activations: scales [m_rows, cols/32] f32 and quants
+ * [m_rows, cols] i8, device). Same outputs as hale_matrix_matvec. */
+HALE_API hale_status hale_matrix_matvec_q8(hale_ctx* ctx, const hale_matrix* m, const float* x_scales,
+                                  const int8_t* x_quants, uint32_t m_rows, float* out,
+                                  int32_t* block_sums, void* stream);
+
+/* Q8Activations::quantize (quant.rs:77-93) for [m_rows, cols] f32 rows. */
+HALE_API hale_status hale_quantize_q8(hale_ctx* ctx, const float* x, uint32_t m_rows, uint32_t cols,
+                             float* scales, int8_t* quants, void* stream);
+
+/* ---- expert pool: ExpertProvider (src/expert/mod.rs:128-137) -------------- */
+
+/* CacheStats (src/expert/cache.rs:15-33). Every expert of the pool lives in
+ * HBM, so requests are served from the pinned tier; `misses` counts requests
+ * for experts that were never uploaded (which fail). */
+typedef struct {
+    uint64_t pinned_hits;
+    uint64_t lru_hits;
+    uint64_t misses;
+    uint64_t bytes_loaded;   /* bytes uploaded into HBM */
+    double load_seconds;     /* host wall time spent uploading */
+    uint64_t pinned_experts; /* experts resident in HBM */
+    uint64_t pinned_bytes;
+    uint64_t lru_experts;
+    uint64_t lru_bytes;
+    uint64_t lru_capacity_bytes;
+    int32_t passthrough;
+} hale_cache_stats;
+
+/* ExpertKey (src/expert/mod.rs:50-62). */
+typedef struct {
+    uint32_t layer;
+    uint32_t expert;
+} hale_expert_key;
+
+/* Device view of one resident expert, returned by hale_pool_fetch. */
+typedef struct {
+    const void* gate; /* tiled [I, H] */
+    const void* up;   /* tiled [I, H] */
+    const void* down; /* tiled [H, I] */
+} hale_expert_view;
+
+/* Creates an HBM store for n_layers x n_experts SwiGLU experts of shape
+ * gate/up [inter, hidden], down [hidden, inter] in `dtype` (q8_0 or q4_0).
+ * hidden and inter must be multiples of 32. */
+HALE_API hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
+                             uint32_t n_layers, uint32_t n_experts, hale_pool** out);
+HALE_API void hale_pool_destroy(hale_pool* pool);
+
+/* Uploads one expert from a pack record -- gate | up | down in the pack's
+ * byte layout, exactly what PackExpertSource::load reads (pack.rs:264-271,
+ * decode_record 125-133). `record` is host memory (on_device = 0) or device
+ * memory (on_device != 0); the record is repacked into the tile layout. */
+HALE_API hale_status hale_pool_upload_expert(hale_pool* pool, uint32_t layer, uint32_t expert,
+                                    const void* record, uint64_t record_bytes, int on_device,
+                                    void* stream);
+
+/* ExpertProvider::fetch (mod.rs:128-137, cache.rs:124-194): resolves keys in
+ * request order, records routing counts and cache counters. */
+HALE_API hale_status hale_pool_fetch(hale_pool* pool, const hale_expert_key* keys, uint64_t n,
+                            hale_expert_view* out);
+/* ExpertProvider::stats (cache.rs:196-198). Includes routes served by
+ * hale_moe_forward on device (read back, which synchronises the ctx). */
+HALE_API hale_status hale_pool_stats(hale_pool* pool, hale_cache_stats* out);
+/* ExpertProvider::routing_stats: counts[n_layers * n_experts] (u64). */
+HALE_API hale_status hale_pool_routing_counts(hale_pool* pool, uint64_t* counts, uint64_t n);
+/* Bytes of one expert record (ExpertSource::expert_bytes). */
+HALE_API uint64_t hale_pool_expert_bytes(const hale_pool* pool);
+
+/* ---- the MoE layer (src/model/moe.rs:25-70) ---------------------------- */
+
+/* Router description for MoeLayer (moe.rs:25-32): `router` is the [E, H]
+ * router matrix in reference encoding (f32 / f16 / bf16 rows, device). */
+typedef struct {
+    uint32_t layer;
+    const void* router;
+    hale_dtype router_dtype;
+    uint32_t n_experts;
+    uint32_t top_k;
+    int32_t normalize_topk;
+} hale_moe_layer;
+
+/* MoeLayer::forward (moe.rs:56-70) for m_tokens independent tokens:
+ * out[t] = sum over the top-k routes of weight * Expert(x[t]), combined in
+ * best-first order. x, out: [m_tokens, H] f32 (device). topk_idx / topk_w
+ * (nullable): [m_tokens, top_k] expert ids (i32) and weights (f32), the
+ * output of MoeLayer::route (moe.rs:36-53). */
+HALE_API hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* pool, const hale_moe_layer* layer,
+                             const float* x, uint32_t m_tokens, float* out, int32_t* topk_idx,
+                             float* topk_w, void* stream);
+/* Same with host buffers: copies x in, runs, copies out, and synchronises. */
+HALE_API hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* pool, const hale_moe_layer* layer,
+                                  const float* x_host, uint32_t m_tokens, float* out_host,
+                                  int32_t* topk_idx_host, float* topk_w_host, void* stream);
+/* MoeLayer::route only (moe.rs:36-53): top-k expert ids and weights. */
+HALE_API hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* layer, uint32_t hidden,
+                           const float* x, uint32_t m_tokens, int32_t* topk_idx, float* topk_w,
+                           float* probs, void* stream);
+
+/* ---- sampling tail -------------------------------------------------------- */
+
+/* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .
+ * hidden[b, :] for b < batch, with lm_head a float hale_matrix [V, H]. */
+HALE_API hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, const float* hidden,
+                         uint32_t batch, float* logits, void* stream);
+
+/* SamplingParams (sampler.rs:22-43) plus a repetition penalty, which the
+ * reference does not have (1.0 disables it; HF convention: a seen id's
+ * logit l becomes l / p when l > 0, else l * p, before temperature). */
+typedef struct {
+    float temperature; /* <= 0: greedy argmax */
+    float top_p;       /* 1.0 disables the nucleus cut */
+    uint32_t top_k;    /* 0 disables top-k */
+    float repetition_penalty;
+} hale_sampling_params;
+
+/* Sampler::sample (sampler.rs:14-18, 80-123) for `batch` rows of logits
+ * [batch, vocab] (device). rng_state [batch] u64 (device) holds each row's
+ * XorShift64 state (seed.max(1) initially, sampler.rs:131-133) and is
+ * advanced in place. seen_ids [batch, n_seen] i32 (nullable; entries < 0
+ * are ignored) feeds the repetition penalty. out_tokens [batch] i32. */
+HALE_API hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t batch, uint32_t vocab,
+                        const hale_sampling_params* params, uint64_t* rng_state,
+                        const int32_t* seen_ids, uint32_t n_seen, int32_t* out_tokens,
+                        void* stream);
+
+/* ---- self-checks ----------------------------------------------------------- */
+
+/* The exp used by the device kernels, evaluated on the host from the same
+ * source (y[i] = exp(x[i]) for i < n). It restates glibc's expf so softmax
+ * and SiLU match the reference's CPU results bit for bit. */
+HALE_API void hale_expf_host(const float* x, float* y, uint64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HALE_CUDA_H */
