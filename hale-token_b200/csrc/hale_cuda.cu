@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -107,6 +108,25 @@ static hale_status check_launch(hale_ctx* ctx, const char* what) {
 }
 
 static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Opts a kernel into more than 48 KB of dynamic shared memory (once per
+// kernel and size; the attribute is per function, not per launch).
+// Static shared memory counts toward the same 48 KB default, so the opt-in
+// is made for every dynamic size, cached per device and function.
+template <class F>
+static cudaError_t allow_smem(F* func, size_t bytes) {
+    if (bytes == 0) return cudaSuccess;
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, size_t> granted;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& g = granted[{dev, reinterpret_cast<const void*>(func)}];
+    if (bytes <= g) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) g = bytes;
+    return e;
+}
 
 static cudaEvent_t take_event(hale_ctx* ctx) {
     if (!ctx->spare.empty()) {
@@ -263,9 +283,9 @@ extern "C" uint64_t hale_ctx_launch_count(const hale_ctx* ctx) { return ctx ? ct
 
 // Counter region of the MoE workspace (zero between calls).
 struct MoeLayout {
-    size_t tile_cnt, grid_cnt, gu_cnt, comb_cnt, counters_end;
+    size_t tile_cnt, grid_cnt, comb_cnt, counters_end;
     size_t logits, topk_idx, topk_w, xq, xaux, elist_off, elist, active, n_active;
-    size_t gu, hq, haux, ybuf, total;
+    size_t hq, haux, ybuf, total;
 };
 
 static MoeLayout moe_layout(int M, int E, int k, int H, int I) {
@@ -276,23 +296,22 @@ static MoeLayout moe_layout(int M, int E, int k, int H, int I) {
         o = align_up(o + bytes, 256);
         return at;
     };
-    L.tile_cnt = take((size_t)M * 4);
+    const size_t nbph = (size_t)aux_stride(std::max(H / 32, 1)), nbpi = (size_t)aux_stride(std::max(I / 32, 1));
+    L.tile_cnt = take((size_t)(M + kRouterTT - 1) / kRouterTT * 4);
     L.grid_cnt = take(4);
-    L.gu_cnt = take((size_t)E * std::max(I / 32, 1) * 4);
-    L.comb_cnt = take((size_t)M * std::max(H / 32, 1) * 4);
+    L.comb_cnt = take((size_t)M * ((H + 127) / 128) * 4);
     L.counters_end = o;
     L.logits = take((size_t)M * E * 4);
     L.topk_idx = take((size_t)M * k * 4);
     L.topk_w = take((size_t)M * k * 4);
     L.xq = take((size_t)M * H);
-    L.xaux = take((size_t)M * (H / 32) * 8);
+    L.xaux = take((size_t)M * nbph * 8);
     L.elist_off = take((size_t)(E + 1) * 4);
     L.elist = take((size_t)M * k * 4);
     L.active = take((size_t)E * 4);
     L.n_active = take(4);
-    L.gu = take((size_t)M * k * 2 * I * 4);
     L.hq = take((size_t)M * k * I);
-    L.haux = take((size_t)M * k * (I / 32) * 8);
+    L.haux = take((size_t)M * k * nbpi * 8);
     L.ybuf = take((size_t)M * k * H * 4);
     L.total = o;
     return L;
@@ -443,53 +462,31 @@ extern "C" void hale_matrix_destroy(hale_matrix* m) {
     delete m;
 }
 
-static int ring_stages(hale_dtype dt) { return dt == HALE_Q4_0 ? 4 : 3; }
-static size_t ring_smem(hale_dtype dt) {
-    int rec = 32 * block_bytes(dt);
-    int S = ring_stages(dt);
-    return (size_t)S * kStageBlocks * rec + (size_t)S * 8;
-}
-
-// Largest activation-row count a tile sees -> compiled pass width.
-static int tg_max(long long rows) {
-    if (rows <= 1) return 1;
-    if (rows <= 2) return 2;
-    if (rows <= 4) return 4;
-    if (rows <= 8) return 8;
-    if (rows <= 16) return 16;
-    return 32;
-}
-
-template <int QT, int TG>
-static void qgemv_go(const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M, float* out,
-                     int32_t* dbg, int S_, size_t smem, uint32_t* err, cudaStream_t st) {
-    qgemv_kernel<QT, TG><<<m->rows_pad / 32, 32, smem, st>>>(m->data, (int)m->rows, (int)m->nb, xq, xaux, (int)M,
-                                                             out, dbg, S_, err);
-}
+// Bulk-copy ring depth per warp: 3 stages of 8 q4 blocks (13.8 KB in flight
+// per warp) or 2 stages of 8 q8 blocks (17.4 KB).
+static int ring_stages(hale_dtype dt) { return dt == HALE_Q4_0 ? 3 : 2; }
 
 template <int QT>
-static void qgemv_tg(int tg, const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M, float* out,
-                     int32_t* dbg, int S_, size_t smem, uint32_t* err, cudaStream_t st) {
-    switch (tg) {
-    case 1: qgemv_go<QT, 1>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    case 2: qgemv_go<QT, 2>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    case 4: qgemv_go<QT, 4>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    case 8: qgemv_go<QT, 8>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    case 16: qgemv_go<QT, 16>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    default: qgemv_go<QT, 32>(m, xq, xaux, M, out, dbg, S_, smem, err, st); break;
-    }
+static hale_status qgemv_go(hale_ctx* ctx, const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M,
+                            float* out, int32_t* dbg, int S_, cudaStream_t st) {
+    SmemPlan P = smem_plan(QFmt<QT>::BB, S_, 4, (int)m->cols);
+    CUDA_TRY(ctx, allow_smem(qgemv_kernel<QT>, (size_t)P.total));
+    unsigned grid = (m->rows_pad / 32 + 3) / 4;
+    qgemv_kernel<QT><<<grid, 128, P.total, st>>>(m->data, (int)m->rows, (int)m->nb, xq, xaux, (int)M, out, dbg,
+                                                 S_, ctx->d_err);
+    return HALE_OK;
 }
 
 static hale_status qgemv_launch(hale_ctx* ctx, const hale_matrix* m, const int8_t* xq, const int2* xaux,
                                 uint32_t M, float* out, int32_t* dbg, cudaStream_t st) {
     int S_ = ring_stages(m->dtype);
-    size_t smem = ring_smem(m->dtype);
-    int tg = tg_max(M);
-    ProfScope ps_(ctx, "qgemv", st);
-    if (m->dtype == HALE_Q4_0)
-        qgemv_tg<0>(tg, m, xq, xaux, M, out, dbg, S_, smem, ctx->d_err, st);
-    else
-        qgemv_tg<1>(tg, m, xq, xaux, M, out, dbg, S_, smem, ctx->d_err, st);
+    hale_status r;
+    {
+        ProfScope ps_(ctx, "qgemv", st);
+        r = m->dtype == HALE_Q4_0 ? qgemv_go<0>(ctx, m, xq, xaux, M, out, dbg, S_, st)
+                                  : qgemv_go<1>(ctx, m, xq, xaux, M, out, dbg, S_, st);
+    }
+    if (r) return r;
     return check_launch(ctx, "qgemv");
 }
 
@@ -543,7 +540,7 @@ extern "C" hale_status hale_matrix_matvec(hale_ctx* ctx, const hale_matrix* m, c
         return fgemv_launch(ctx, m, x, m_rows, out, st);
     }
     size_t qbytes = align_up((size_t)m_rows * m->cols, 256);
-    size_t abytes = (size_t)m_rows * m->nb * 8;
+    size_t abytes = (size_t)m_rows * aux_stride((int)m->nb) * 8;
     hale_status rs = ensure_scratch(ctx, qbytes + abytes, stream);
     if (rs) return rs;
     int8_t* xq = static_cast<int8_t*>(ctx->scratch);
@@ -568,7 +565,7 @@ extern "C" hale_status hale_matrix_matvec_q8(hale_ctx* ctx, const hale_matrix* m
     if (!x_scales || !x_quants || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec_q8: NULL buffer");
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     cudaStream_t st = S(stream);
-    hale_status rs = ensure_scratch(ctx, (size_t)m_rows * m->nb * 8, stream);
+    hale_status rs = ensure_scratch(ctx, (size_t)m_rows * aux_stride((int)m->nb) * 8, stream);
     if (rs) return rs;
     int2* xaux = static_cast<int2*>(ctx->scratch);
     long long n = (long long)m_rows * m->nb;
@@ -753,8 +750,7 @@ static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32
     a.M = (int)M;
     a.k = (int)ly->top_k;
     a.normalize = ly->normalize_topk ? 1 : 0;
-    a.TT = M >= 4 ? 4 : (M >= 2 ? 2 : 1);
-    a.ET = 32 / a.TT;
+    a.staged = (H % 8 == 0) ? 1 : 0;
     a.x = x;
     a.logits = reinterpret_cast<float*>(ws + L.logits);
     a.probs_out = probs;
@@ -771,9 +767,12 @@ static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32
     a.routing_counts = routing;
     a.tile_cnt = reinterpret_cast<unsigned*>(ws + L.tile_cnt);
     a.grid_cnt = reinterpret_cast<unsigned*>(ws + L.grid_cnt);
-    dim3 grid((M + a.TT - 1) / a.TT, (a.E + a.ET - 1) / a.ET);
+    a.err = ctx->d_err;
+    dim3 grid((M + kRouterTT - 1) / kRouterTT, (a.E + kRouterET - 1) / kRouterET);
+    size_t smem = a.staged ? (size_t)2 * router_slot_bytes(a.wdtype == 0 ? 4 : 2) + 16 : 0;
+    CUDA_TRY(ctx, allow_smem(router_kernel, smem));
     ProfScope ps_(ctx, "router", st);
-    router_kernel<<<grid, 256, 0, st>>>(a);
+    router_kernel<<<grid, 256, smem, st>>>(a);
     return check_launch(ctx, "router");
 }
 
@@ -792,31 +791,25 @@ extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, u
     return launch_router(ctx, ly, hidden, x, M, L, false, topk_idx, topk_w, probs, nullptr, S(stream));
 }
 
-template <int QT, int TG>
-static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned g1, unsigned g2, size_t smem,
-                             cudaStream_t st) {
+template <int QT, int RT>
+static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
+    const int TI = a.I / 32, TH = a.H / 32;
+    SmemPlan P1 = smem_plan(QFmt<QT>::BB, a.S, 2 * RT, a.H);
+    SmemPlan P2 = smem_plan(QFmt<QT>::BB, a.S, 4, a.I);
+    CUDA_TRY(ctx, allow_smem(expert_gate_up_kernel<QT, RT>, (size_t)P1.total));
+    CUDA_TRY(ctx, allow_smem(expert_down_kernel<QT>, (size_t)P2.total));
+    unsigned g1 = max_active * (unsigned)((TI + RT - 1) / RT), g2 = max_active * (unsigned)((TH + 3) / 4);
     {
         ProfScope ps_(ctx, "expert_gate_up", st);
-        expert_gate_up_kernel<QT, TG><<<g1, 32, smem, st>>>(a);
+        expert_gate_up_kernel<QT, RT><<<g1, 64 * RT, P1.total, st>>>(a);
     }
     hale_status r = check_launch(ctx, "expert_gate_up");
     if (r) return r;
-    ProfScope ps_(ctx, "expert_down", st);
-    expert_down_kernel<QT, TG><<<g2, 32, smem, st>>>(a);
-    return HALE_OK;
-}
-
-template <int QT>
-static hale_status expert_launch(hale_ctx* ctx, int tg, const ExpertArgs& a, unsigned g1, unsigned g2,
-                                 size_t smem, cudaStream_t st) {
-    switch (tg) {
-    case 1: return expert_go<QT, 1>(ctx, a, g1, g2, smem, st);
-    case 2: return expert_go<QT, 2>(ctx, a, g1, g2, smem, st);
-    case 4: return expert_go<QT, 4>(ctx, a, g1, g2, smem, st);
-    case 8: return expert_go<QT, 8>(ctx, a, g1, g2, smem, st);
-    case 16: return expert_go<QT, 16>(ctx, a, g1, g2, smem, st);
-    default: return expert_go<QT, 32>(ctx, a, g1, g2, smem, st);
+    {
+        ProfScope ps_(ctx, "expert_down", st);
+        expert_down_kernel<QT><<<g2, 128, P2.total, st>>>(a);
     }
+    return check_launch(ctx, "expert_down");
 }
 
 extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
@@ -855,8 +848,6 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.n_active = reinterpret_cast<int*>(ws + L.n_active);
     a.xq = reinterpret_cast<int8_t*>(ws + L.xq);
     a.xaux = reinterpret_cast<int2*>(ws + L.xaux);
-    a.gu = reinterpret_cast<float*>(ws + L.gu);
-    a.gu_cnt = reinterpret_cast<unsigned*>(ws + L.gu_cnt);
     a.hq = reinterpret_cast<int8_t*>(ws + L.hq);
     a.haux = reinterpret_cast<int2*>(ws + L.haux);
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
@@ -865,17 +856,12 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.out = out;
     a.S = ring_stages(p->dtype);
     a.err = ctx->d_err;
-    size_t smem = ring_smem(p->dtype);
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
-    unsigned g1 = max_active * 2 * (I / 32), g2 = max_active * (H / 32);
-    // an expert sees at most M tokens (each token picks distinct experts)
-    int tg = tg_max(M);
+    // small batches: one row tile per CTA pair of warps, for more CTAs
+    bool small = M <= 2;
     if (p->dtype == HALE_Q4_0)
-        r = expert_launch<0>(ctx, tg, a, g1, g2, smem, st);
-    else
-        r = expert_launch<1>(ctx, tg, a, g1, g2, smem, st);
-    if (r) return r;
-    return check_launch(ctx, "expert_down");
+        return small ? expert_go<0, 1>(ctx, a, max_active, st) : expert_go<0, 2>(ctx, a, max_active, st);
+    return small ? expert_go<1, 1>(ctx, a, max_active, st) : expert_go<1, 2>(ctx, a, max_active, st);
 }
 
 extern "C" hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly,

@@ -82,9 +82,12 @@ __global__ void repack_float_kernel(const uint8_t* __restrict__ src, uint8_t* __
 // Q8Activations::quantize (src/tensor/quant.rs:77-93), one warp per row.
 // Writes quants [rows, cols] i8 and, per block, the f32 scale (scales,
 // nullable) and aux = (scale bits, -8 * sum of the block's quants) (aux,
-// nullable). The -8*sum term turns the nibble dot into the reference's
-// sum of (n - 8) * x exactly (integer arithmetic).
+// nullable; row stride nbp = nb rounded up to even so every aux row starts
+// on a 16-byte boundary for bulk copies). The -8*sum term turns the nibble
+// dot into the reference's sum of (n - 8) * x exactly (integer arithmetic).
 // ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int aux_stride(int nb) { return (nb + 1) & ~1; }
+
 __device__ __forceinline__ void quantize_block(const float* __restrict__ xb, int8_t* __restrict__ q,
                                                float* scale_out, int* sum_out) {
     float amax = 0.0f;
@@ -106,14 +109,14 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int rows, int 
                                      int2* __restrict__ aux) {
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
-    int nb = cols / kQK;
+    int nb = cols / kQK, nbp = aux_stride(nb);
     const float* xr = x + (size_t)warp * cols;
     for (int b = lane; b < nb; b += 32) {
         float sc;
         int sm;
         quantize_block(xr + b * kQK, quants + (size_t)warp * cols + b * kQK, &sc, &sm);
         if (scales) scales[(size_t)warp * nb + b] = sc;
-        if (aux) aux[(size_t)warp * nb + b] = make_int2(__float_as_int(sc), -8 * sm);
+        if (aux) aux[(size_t)warp * nbp + b] = make_int2(__float_as_int(sc), -8 * sm);
     }
 }
 
@@ -128,7 +131,7 @@ __global__ void aux_from_q8_kernel(const float* __restrict__ scales,
     const int8_t* q = quants + (size_t)r * cols + b * kQK;
     int s = 0;
     for (int j = 0; j < kQK; j++) s += q[j];
-    aux[idx] = make_int2(__float_as_int(scales[idx]), -8 * s);
+    aux[(size_t)r * aux_stride(nb) + b] = make_int2(__float_as_int(scales[idx]), -8 * s);
 }
 
 // ---------------------------------------------------------------------------
@@ -136,11 +139,16 @@ __global__ void aux_from_q8_kernel(const float* __restrict__ scales,
 // for one warp: lane = row of the tile, TG activation rows at once.
 //
 // Weights stream HBM -> shared memory with cp.async.bulk (the TMA engine)
-// through a ring of S stages of kStageBlocks blocks, each completing on its
-// own mbarrier; lane 0 issues, the warp consumes. Per block and activation
-// row the integer dot is 8 dp4a (exact int32), then the reference's float
-// step total += (w_scale * x_scale) * isum, in block order, unfused.
+// through a per-warp ring of S stages of kStageBlocks blocks, each landing
+// on its own mbarrier; lane 0 issues, the warp consumes. The activation rows
+// of the pass sit in shared memory (XStage, gathered by bulk copies once per
+// CTA and pass). Per block and activation row the integer dot is 8 dp4a
+// (exact int32); then the reference's float step
+//     total += (w_scale * x_scale) * isum,
+// in block order and unfused.
 // ---------------------------------------------------------------------------
+constexpr int kPassRows = 8;  // activation rows per pass
+
 struct Ring {
     uint8_t* buf;      // S * stage_bytes
     uint64_t* bars;    // S mbarriers
@@ -160,13 +168,75 @@ __device__ __forceinline__ void ring_issue(Ring& rg, const uint8_t* gtile, int n
              &rg.bars[slot]);
 }
 
-// Computes acc[j] = dot(row lane of the tile, activation row xr[j]) for
-// j < TG. Returns false if a wait timed out (results then invalid).
+__device__ __forceinline__ void ring_init(Ring& rg, uint8_t* buf, uint64_t* bars, int S, int stage_bytes) {
+    rg.buf = buf;
+    rg.bars = bars;
+    rg.S = S;
+    rg.stage_bytes = stage_bytes;
+    rg.phase = 0;
+    if ((threadIdx.x & 31) == 0) {
+        for (int s = 0; s < S; s++) mbar_init(&rg.bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+}
+
+// Activation rows of one pass, in shared memory: quants [kPassRows][cols]
+// and aux [kPassRows][nbp].
+struct XStage {
+    int8_t* q;
+    int2* a;
+    uint64_t* bar;
+    uint32_t phase;
+};
+
+__device__ __forceinline__ void xstage_init(XStage& xs, int8_t* q, int2* a, uint64_t* bar) {
+    xs.q = q;
+    xs.a = a;
+    xs.bar = bar;
+    xs.phase = 0;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+}
+
+// Gathers activation rows row_of(base .. base+n-1) into the stage (all
+// threads call; thread 0 issues). contiguous: the rows are consecutive in
+// global memory (one copy each for quants and aux).
+template <class RowOf>
+__device__ bool xstage_load(XStage& xs, const int8_t* __restrict__ gq, const int2* __restrict__ ga,
+                            int cols, int nbp, int base, int n, bool contiguous, RowOf row_of,
+                            uint32_t* err) {
+    __syncthreads();  // every warp is done with the previous pass
+    if (threadIdx.x == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(xs.bar, (uint32_t)n * (uint32_t)(cols + nbp * 8));
+        if (contiguous) {
+            int r = row_of(base);
+            bulk_g2s(xs.q, gq + (size_t)r * cols, (uint32_t)(n * cols), xs.bar);
+            bulk_g2s(xs.a, ga + (size_t)r * nbp, (uint32_t)(n * nbp * 8), xs.bar);
+        } else {
+            for (int j = 0; j < n; j++) {
+                int r = row_of(base + j);
+                bulk_g2s(xs.q + (size_t)j * cols, gq + (size_t)r * cols, (uint32_t)cols, xs.bar);
+                bulk_g2s(xs.a + (size_t)j * nbp, ga + (size_t)r * nbp, (uint32_t)(nbp * 8), xs.bar);
+            }
+        }
+    }
+    bool ok = mbar_wait(xs.bar, xs.phase, err);
+    xs.phase ^= 1u;
+    return __syncthreads_and(ok ? 1 : 0) != 0;  // one verdict for the whole CTA
+}
+
+// acc[j] = dot(row `lane` of the tile, staged activation row j), j < TG.
+// dbg (nullable): block sums of staged row j at dbg[j * dbg_stride + lane*nb + b]
+// for j < nvalid. Returns false if a wait timed out.
 template <int QT, int TG>
-__device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
-                         const int8_t* __restrict__ xq, const int2* __restrict__ xaux, int cols,
-                         const int (&xr)[TG], int nvalid, float (&acc)[TG], int32_t* dbg,
-                         size_t dbg_row_stride, uint32_t* err) {
+__device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, const XStage& xs,
+                         int cols, int nbp, float (&acc)[TG], int32_t* dbg, size_t dbg_stride,
+                         int nvalid, uint32_t* err) {
     constexpr int BB = QFmt<QT>::BB, QB = QFmt<QT>::QB, REC = kTileRows * BB;
     const int lane = threadIdx.x & 31;
     const int nst = (nb + kStageBlocks - 1) / kStageBlocks;
@@ -179,7 +249,7 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
     bool ok = true;
     for (int st = 0; st < nst; st++) {
         int slot = st % rg.S;
-        if (!mbar_wait(&rg.bars[slot], (rg.phase >> slot) & 1u, err)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&rg.bars[slot], (rg.phase >> slot) & 1u, err))) {
             ok = false;
             // drain: give the copies already issued a bounded chance to land
             for (int s2 = st; s2 < min(st + rg.S, nst); s2++)
@@ -188,8 +258,8 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
         }
         rg.phase ^= 1u << slot;
         const uint8_t* sbuf = rg.buf + (size_t)slot * rg.stage_bytes;
-        int nblk = min(kStageBlocks, nb - st * kStageBlocks);
-#pragma unroll 1
+        const int nblk = min(kStageBlocks, nb - st * kStageBlocks);
+#pragma unroll 2
         for (int bi = 0; bi < nblk; bi++) {
             const int b = st * kStageBlocks + bi;
             const uint8_t* rec = sbuf + bi * REC;
@@ -213,10 +283,10 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
             }
 #pragma unroll
             for (int j = 0; j < TG; j++) {
-                const int8_t* xp = xq + (size_t)xr[j] * cols + b * kQK;
-                uint4 xa = __ldg(reinterpret_cast<const uint4*>(xp));
-                uint4 xb = __ldg(reinterpret_cast<const uint4*>(xp + 16));
-                int2 ax = __ldg(xaux + (size_t)xr[j] * nb + b);
+                const int8_t* xp = xs.q + j * cols + b * kQK;
+                uint4 xa = *reinterpret_cast<const uint4*>(xp);
+                uint4 xb = *reinterpret_cast<const uint4*>(xp + 16);
+                int2 ax = xs.a[j * nbp + b];
                 int s = (QT == 0) ? ax.y : 0;
                 s = __dp4a(w[0], (int)xa.x, s);
                 s = __dp4a(w[1], (int)xa.y, s);
@@ -226,7 +296,7 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
                 s = __dp4a(w[5], (int)xb.y, s);
                 s = __dp4a(w[6], (int)xb.z, s);
                 s = __dp4a(w[7], (int)xb.w, s);
-                if (dbg && j < nvalid) dbg[(size_t)xr[j] * dbg_row_stride + (size_t)lane * nb + b] = s;
+                if (dbg && j < nvalid) dbg[(size_t)j * dbg_stride + (size_t)lane * nb + b] = s;
                 acc[j] = fadd(acc[j], fmul(fmul(ws, __int_as_float(ax.x)), __int2float_rn(s)));
             }
         }
@@ -240,91 +310,89 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb,
     return ok;
 }
 
-__device__ __forceinline__ void ring_init(Ring& rg, uint8_t* smem, int S, int stage_bytes) {
-    rg.buf = smem;
-    rg.bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
-    rg.S = S;
-    rg.stage_bytes = stage_bytes;
-    rg.phase = 0;
-    if ((threadIdx.x & 31) == 0) {
-        for (int s = 0; s < S; s++) mbar_init(&rg.bars[s], 1);
-        fence_mbar_init();
-    }
-    __syncwarp();
-}
-
-// Runs the tile dot over `count` activation rows given by row_of(j) in passes
-// of <= 32, calling emit(j, value) for each (lane = tile row). The pass
-// width is the smallest power of two covering the remaining rows.
-template <int QT, int TG, class RowOf, class Emit>
-__device__ bool tile_pass(Ring& rg, const uint8_t* gtile, int nb, const int8_t* xq,
-                          const int2* xaux, int cols, int base, int n, RowOf row_of, Emit emit,
-                          int32_t* dbg, size_t dbg_row_stride, uint32_t* err) {
-    int xr[TG];
-    float acc[TG];
+// Runs tile_dot with the pass width TG chosen at run time (smallest power of
+// two >= n, at most kPassRows) and hands the results to emit(j, value).
+template <int QT, class Emit>
+__device__ bool tile_dot_n(Ring& rg, const uint8_t* gtile, int nb, const XStage& xs, int cols, int nbp,
+                           int n, int32_t* dbg, size_t dbg_stride, uint32_t* err, Emit emit) {
+    bool ok;
+    if (n <= 1) {
+        float acc[1];
+        ok = tile_dot<QT, 1>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
+        if (ok) emit(0, acc[0]);
+    } else if (n <= 2) {
+        float acc[2];
+        ok = tile_dot<QT, 2>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
+        if (ok)
 #pragma unroll
-    for (int j = 0; j < TG; j++) xr[j] = row_of(base + (j < n ? j : 0));
-    bool ok = tile_dot<QT, TG>(rg, gtile, nb, xq, xaux, cols, xr, n, acc, dbg, dbg_row_stride, err);
-    if (ok) {
+            for (int j = 0; j < 2; j++) if (j < n) emit(j, acc[j]);
+    } else if (n <= 4) {
+        float acc[4];
+        ok = tile_dot<QT, 4>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
+        if (ok)
 #pragma unroll
-        for (int j = 0; j < TG; j++)
-            if (j < n) emit(base + j, acc[j]);
+            for (int j = 0; j < 4; j++) if (j < n) emit(j, acc[j]);
+    } else {
+        float acc[8];
+        ok = tile_dot<QT, 8>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
+        if (ok)
+#pragma unroll
+            for (int j = 0; j < 8; j++) if (j < n) emit(j, acc[j]);
     }
     return ok;
 }
 
-// All `count` activation rows, in passes of at most TGMAX rows; each pass
-// uses the smallest power-of-two width that covers it. TGMAX is a launch
-// parameter (the largest row count any tile can see), so small-batch
-// launches are compiled with few registers.
-template <int QT, int TGMAX, class RowOf, class Emit>
-__device__ bool tile_all_rows(Ring& rg, const uint8_t* gtile, int nb, const int8_t* xq,
-                              const int2* xaux, int cols, int count, RowOf row_of, Emit emit,
-                              int32_t* dbg, size_t dbg_row_stride, uint32_t* err) {
-    bool ok = true;
-    for (int base = 0; base < count && ok; base += TGMAX) {
-        int n = min(TGMAX, count - base);
-        if (n <= 1 || TGMAX == 1)
-            ok = tile_pass<QT, 1>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-        else if (n <= 2 || TGMAX == 2)
-            ok = tile_pass<QT, 2>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-        else if (n <= 4 || TGMAX == 4)
-            ok = tile_pass<QT, 4>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-        else if (n <= 8 || TGMAX == 8)
-            ok = tile_pass<QT, 8>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-        else if (n <= 16 || TGMAX == 16)
-            ok = tile_pass<QT, 16>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-        else
-            ok = tile_pass<QT, 32>(rg, gtile, nb, xq, xaux, cols, base, n, row_of, emit, dbg, dbg_row_stride, err);
-    }
-    return ok;
+// Shared-memory plan of the GEMV kernels: per-warp rings, then the
+// activation stage, then the barriers.
+struct SmemPlan {
+    int stage_bytes, ring_bytes, xq_off, xa_off, bars_off, total;
+};
+
+__host__ __device__ inline SmemPlan smem_plan(int BB, int S, int warps, int cols) {
+    SmemPlan p;
+    p.stage_bytes = kStageBlocks * kTileRows * BB;
+    p.ring_bytes = S * p.stage_bytes;
+    p.xq_off = warps * p.ring_bytes;
+    int nbp = aux_stride(cols / kQK);
+    p.xa_off = p.xq_off + ((kPassRows * cols + 15) & ~15);
+    p.bars_off = p.xa_off + kPassRows * nbp * 8;
+    p.total = p.bars_off + (warps * S + 1) * 8;
+    return p;
 }
 
 // ---------------------------------------------------------------------------
-// WeightMatrix::matvec for quantized matrices (matrix.rs:115-126): one warp
-// per row tile, all activation rows. dbg: block sums [M, rows_pad, nb].
+// WeightMatrix::matvec for quantized matrices (matrix.rs:115-126): a CTA of
+// 4 warps covers 4 row tiles (128 rows); activation rows go in passes of 8.
+// dbg: block sums [M, rows, nb].
 // ---------------------------------------------------------------------------
-template <int QT, int TGMAX>
-__global__ void __launch_bounds__(32) qgemv_kernel(const uint8_t* __restrict__ W, int rows, int nb,
-                                                   const int8_t* __restrict__ xq,
-                                                   const int2* __restrict__ xaux, int M,
-                                                   float* __restrict__ out, int32_t* dbg,
-                                                   int S, uint32_t* err) {
+template <int QT>
+__global__ void __launch_bounds__(128) qgemv_kernel(const uint8_t* __restrict__ W, int rows, int nb,
+                                                    const int8_t* __restrict__ xq,
+                                                    const int2* __restrict__ xaux, int M,
+                                                    float* __restrict__ out, int32_t* dbg,
+                                                    int S, uint32_t* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int REC = kTileRows * QFmt<QT>::BB;
-    const int g = blockIdx.x, lane = threadIdx.x & 31, cols = nb * kQK;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, cols = nb * kQK, nbp = aux_stride(nb);
+    const SmemPlan P = smem_plan(QFmt<QT>::BB, S, 4, cols);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bars_off);
     Ring rg;
-    ring_init(rg, smem, S, kStageBlocks * REC);
-    const uint8_t* gtile = W + (size_t)g * nb * REC;
+    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * S, S, P.stage_bytes);
+    XStage xs;
+    xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
+                 bars + 4 * S);
+    const int ntiles = (rows + kTileRows - 1) / kTileRows;
+    const int g = blockIdx.x * 4 + warp;
     const int row = g * kTileRows + lane;
-    // block sums [M, rows, nb]; rows of the padded tail are not written
-    int32_t* dbg_base = (dbg && row < rows) ? dbg + (size_t)g * kTileRows * nb : nullptr;
-    tile_all_rows<QT, TGMAX>(
-        rg, gtile, nb, xq, xaux, cols, M, [](int j) { return j; },
-        [&](int j, float v) {
-            if (row < rows) out[(size_t)j * rows + row] = v;
-        },
-        dbg_base, (size_t)rows * nb, err);
+    const uint8_t* gtile = W + (size_t)g * nb * kTileRows * QFmt<QT>::BB;
+    for (int base = 0; base < M; base += kPassRows) {
+        const int n = min(kPassRows, M - base);
+        if (!xstage_load(xs, xq, xaux, cols, nbp, base, n, true, [](int j) { return j; }, err)) return;
+        if (g >= ntiles) continue;
+        int32_t* d = (dbg && row < rows) ? dbg + (size_t)base * rows * nb + (size_t)g * kTileRows * nb : nullptr;
+        tile_dot_n<QT>(rg, gtile, nb, xs, cols, nbp, n, d, (size_t)rows * nb, err, [&](int j, float v) {
+            if (row < rows) out[(size_t)(base + j) * rows + row] = v;
+        });
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -332,16 +400,22 @@ __global__ void __launch_bounds__(32) qgemv_kernel(const uint8_t* __restrict__ W
 //
 // Logits: each (token, expert) pair is 8 threads, thread l owning the
 // reference's accumulator lane l (quant.rs:152-160): acc += w[8i+l]*x[8i+l]
-// over i in order, then reduce() (quant.rs:37-41) and the tail. The last CTA
-// to finish a token tile then runs softmax (activation.rs:11-21), top-k with
-// (score desc, index asc) (topk.rs:27-61), the weight normalisation, and
-// quantizes the tile's activation rows. The last such CTA of the grid
-// groups the routes by expert for the expert kernels.
+// over i in order, then reduce() (quant.rs:37-41) and the tail. A CTA covers
+// 4 tokens x 8 experts; the router rows and token rows stream into shared
+// memory in column chunks by bulk copies (two-slot ring), so the 8-lane
+// chains run from shared memory. The last CTA to finish a token tile then
+// runs softmax (activation.rs:11-21), top-k with (score desc, index asc)
+// (topk.rs:27-61) and the weight normalisation, and quantizes the tile's
+// activation rows. The last such CTA of the grid groups the routes by
+// expert for the expert kernels.
 // ---------------------------------------------------------------------------
+constexpr int kRouterTT = 4, kRouterET = 8, kRouterCH = 512, kRouterPad = 8;  // pad: 8-bank row skew
+
 struct RouterArgs {
     const void* w;
     int wdtype;  // 0 f32, 1 f16, 2 bf16
-    int E, H, M, k, normalize, TT, ET;
+    int E, H, M, k, normalize;
+    int staged;             // rows stream through shared memory (H % 8 == 0)
     const float* x;
     float* logits;          // [M, E]
     float* probs_out;       // [M, E] nullable
@@ -350,7 +424,7 @@ struct RouterArgs {
     int* user_idx;          // nullable copies for the caller
     float* user_w;
     int8_t* xq;             // [M, H] nullable (route-only calls skip it)
-    int2* xaux;             // [M, H/32]
+    int2* xaux;             // [M, nbp(H)]
     int* elist_off;         // [E + 1]   (nullable: route-only)
     int* elist;             // [M * k]
     int* active;            // [E]
@@ -358,6 +432,7 @@ struct RouterArgs {
     unsigned long long* routing_counts;  // [E] nullable
     unsigned* tile_cnt;     // [ceil(M / TT)]
     unsigned* grid_cnt;     // [1]
+    uint32_t* err;
 };
 
 __device__ __forceinline__ float load_w(const void* w, int dt, size_t i) {
@@ -367,18 +442,83 @@ __device__ __forceinline__ float load_w(const void* w, int dt, size_t i) {
     return half_bits_to_float(h);
 }
 
+__device__ __forceinline__ float smem_w(const uint8_t* row, int dt, int c) {
+    if (dt == 0) return reinterpret_cast<const float*>(row)[c];
+    uint16_t h = reinterpret_cast<const uint16_t*>(row)[c];
+    if (dt == 2) return __uint_as_float((uint32_t)h << 16);
+    return half_bits_to_float(h);
+}
+
+__host__ __device__ inline int router_slot_bytes(int wbytes) {
+    return kRouterET * (kRouterCH + kRouterPad) * wbytes + kRouterTT * (kRouterCH + kRouterPad) * 4;
+}
+
 __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned s_flag;
     __shared__ float s_e[8][256];
     __shared__ int s_cnt[256];
     __shared__ int s_cur[256];
     const int tid = threadIdx.x, lane8 = tid & 7, pair = tid >> 3;
-    const int t = blockIdx.x * a.TT + pair / a.ET;
-    const int e = blockIdx.y * a.ET + pair % a.ET;
-    const bool valid = (pair / a.ET) < a.TT && t < a.M && e < a.E;
+    const int tl = pair / kRouterET, el = pair % kRouterET;
+    const int t = blockIdx.x * kRouterTT + tl;
+    const int e = blockIdx.y * kRouterET + el;
+    const bool valid = t < a.M && e < a.E;
     const int full = a.H / 8;
+    const int wb = a.wdtype == 0 ? 4 : 2;
     float acc = 0.0f;
-    if (valid) {
+    if (a.staged) {
+        // two-slot ring of column chunks: [8 router rows][4 token rows]
+        const int slot_bytes = router_slot_bytes(wb);
+        uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * slot_bytes);
+        const int nch = (a.H + kRouterCH - 1) / kRouterCH;
+        const int rpitch = (kRouterCH + kRouterPad) * wb, xpitch = (kRouterCH + kRouterPad) * 4;
+        if (tid == 0) {
+            mbar_init(&bars[0], 1);
+            mbar_init(&bars[1], 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        auto issue = [&](int c) {
+            uint8_t* slot = smem + (c & 1) * slot_bytes;
+            const int c0 = c * kRouterCH, len = min(kRouterCH, a.H - c0);
+            const int nr = min(kRouterET, a.E - (int)blockIdx.y * kRouterET);
+            const int nt = min(kRouterTT, a.M - (int)blockIdx.x * kRouterTT);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&bars[c & 1], (uint32_t)(nr * len * wb + nt * len * 4));
+            for (int r = 0; r < nr; r++)
+                bulk_g2s(slot + r * rpitch,
+                         reinterpret_cast<const uint8_t*>(a.w) + ((size_t)(blockIdx.y * kRouterET + r) * a.H + c0) * wb,
+                         (uint32_t)(len * wb), &bars[c & 1]);
+            for (int r = 0; r < nt; r++)
+                bulk_g2s(slot + kRouterET * rpitch + r * xpitch,
+                         a.x + (size_t)(blockIdx.x * kRouterTT + r) * a.H + c0, (uint32_t)(len * 4),
+                         &bars[c & 1]);
+        };
+        if (tid == 0) {
+            issue(0);
+            if (nch > 1) issue(1);
+        }
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int c = 0; c < nch; c++) {
+            // every chunk is waited on (bounded) even after a timeout, so no
+            // copy is still landing when the CTA moves on
+            ok = mbar_wait(&bars[c & 1], (phase >> (c & 1)) & 1u, a.err) && ok;
+            phase ^= 1u << (c & 1);
+            const uint8_t* slot = smem + (c & 1) * slot_bytes;
+            const uint8_t* wrow = slot + el * rpitch;
+            const float* xrow = reinterpret_cast<const float*>(slot + kRouterET * rpitch + tl * xpitch);
+            const int steps = min(kRouterCH, a.H - c * kRouterCH) / 8;
+            if (valid && ok) {
+#pragma unroll 8
+                for (int i = 0; i < steps; i++)
+                    acc = fadd(acc, fmul(smem_w(wrow, a.wdtype, 8 * i + lane8), xrow[8 * i + lane8]));
+            }
+            __syncthreads();
+            if (tid == 0 && c + 2 < nch) issue(c + 2);
+        }
+    } else if (valid) {
         const float* xt = a.x + (size_t)t * a.H;
         size_t wrow = (size_t)e * a.H;
 #pragma unroll 8
@@ -407,8 +547,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 
     // ---- last CTA of this token tile: softmax, top-k, quantize ----------
     const int warp = tid >> 5, lane = tid & 31;
-    for (int tt = warp; tt < a.TT; tt += 8) {
-        const int tok = blockIdx.x * a.TT + tt;
+    for (int tt = warp; tt < kRouterTT; tt += 8) {
+        const int tok = blockIdx.x * kRouterTT + tt;
         if (tok >= a.M) break;
         const float* lg = a.logits + (size_t)tok * a.E;
         float mx = -__int_as_float(0x7f800000);
@@ -460,12 +600,12 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         }
         // Q8Activations::quantize of this token (quant.rs:77-93)
         if (a.xq) {
-            const int nb = a.H / kQK;
+            const int nb = a.H / kQK, nbp = aux_stride(nb);
             for (int b = lane; b < nb; b += 32) {
                 float sc;
                 int sm;
                 quantize_block(a.x + (size_t)tok * a.H + b * kQK, a.xq + (size_t)tok * a.H + b * kQK, &sc, &sm);
-                a.xaux[(size_t)tok * nb + b] = make_int2(__float_as_int(sc), -8 * sm);
+                a.xaux[(size_t)tok * nbp + b] = make_int2(__float_as_int(sc), -8 * sm);
             }
         }
         __syncwarp();
@@ -511,128 +651,158 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Expert kernels: Expert::forward (src/expert/mod.rs:91-103) for all routes
+// Expert kernels: Expert::forward (src/expert/mod.rs:91-103) for every route
 // of the layer, grouped by expert so each weight tile is read from HBM once
-// for every token routed to it.
+// for all tokens routed to it.
 // ---------------------------------------------------------------------------
 struct ExpertArgs {
     const uint8_t* experts;   // layer base: E experts, each [gate tiles][up tiles][down tiles]
     size_t expert_stride;     // bytes per expert
     int H, I, k, M;
-    const int* elist_off;
-    const int* elist;
+    const int* elist_off;     // [E + 1]: routes of expert e are slots off[e] .. off[e+1]-1
+    const int* elist;         // [M * k]: route id (token * k + s) of each slot
     const int* active;
     const int* n_active;
     const int8_t* xq;         // [M, H]
-    const int2* xaux;         // [M, H/32]
-    float* gu;                // [M*k, 2, I]
-    unsigned* gu_cnt;         // [E, I/32]
-    int8_t* hq;               // [M*k, I]
-    int2* haux;               // [M*k, I/32]
-    float* ybuf;              // [M*k, H]
-    unsigned* comb_cnt;       // [M, H/32]
+    const int2* xaux;         // [M, nbp(H)]
+    int8_t* hq;               // [M*k slots, I]   (slot order)
+    int2* haux;               // [M*k slots, nbp(I)]
+    float* ybuf;              // [M*k routes, H]  (route order)
+    unsigned* comb_cnt;       // [M, ceil(H / 128)]
     const float* topk_w;      // [M, k]
     float* out;               // [M, H]
     int S;
     uint32_t* err;
 };
 
-// Phase 1: one CTA (one warp) per (active expert, gate|up, 32-row tile).
-// The second of the gate/up pair to finish forms h = silu(g) * u for its 32
-// rows and quantizes it (the 32 rows are exactly one q8 block of h, which
-// the reference re-quantizes before the down projection, matrix.rs:119-121).
-template <int QT, int TGMAX>
-__global__ void __launch_bounds__(32) expert_gate_up_kernel(ExpertArgs a) {
+// Phase 1: one CTA per (active expert, RT consecutive 32-row tiles of the
+// intermediate dimension). Warps 0..RT-1 take the gate tiles, RT..2RT-1 the
+// matching up tiles. After each pass the gate warps hand g to the up warps
+// through shared memory, which form h = silu(g) * u (expert/mod.rs:100-102)
+// and quantize it: the 32 rows of a tile are exactly one q8 block of h,
+// which the reference re-quantizes before the down projection
+// (matrix.rs:119-121). h is written in slot order, so each expert's rows are
+// contiguous for phase 2.
+template <int QT, int RT>
+__global__ void __launch_bounds__(64 * RT) expert_gate_up_kernel(ExpertArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float s_g[RT][kPassRows][kTileRows];
     constexpr int REC = kTileRows * QFmt<QT>::BB;
-    const int TI = a.I / kTileRows, nbh = a.H / kQK;
-    const int per_expert = 2 * TI;
-    const int u = blockIdx.x, ai = u / per_expert;
+    constexpr int W = 2 * RT;
+    const int TI = a.I / kTileRows, nbh = a.H / kQK, nbph = aux_stride(nbh), nbpi = aux_stride(a.I / kQK);
+    const int units = (TI + RT - 1) / RT;
+    const int ai = blockIdx.x / units;
     if (ai >= *a.n_active) return;
-    const int m = (u % per_expert) / TI, g = (u % per_expert) % TI;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m = warp / RT, tl = warp % RT;           // m: 0 gate, 1 up
+    const int tile = (blockIdx.x % units) * RT + tl;    // tile of the intermediate dim
     const int e = a.active[ai];
     const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
-    const int lane = threadIdx.x & 31;
-    const size_t tile_bytes = (size_t)nbh * REC;
-    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)(m * TI + g) * tile_bytes;
+    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S, W, a.H);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bars_off);
     Ring rg;
-    ring_init(rg, smem, a.S, kStageBlocks * REC);
+    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S, a.S, P.stage_bytes);
+    XStage xs;
+    xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
+                bars + W * a.S);
+    const size_t tile_bytes = (size_t)nbh * REC;
+    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)(m * TI + tile) * tile_bytes;
     const int* routes = a.elist + beg;
     const int k = a.k;
-    bool ok = tile_all_rows<QT, TGMAX>(
-        rg, gtile, nbh, a.xq, a.xaux, a.H, T, [&](int j) { return routes[j] / k; },
-        [&](int j, float v) {
-            a.gu[((size_t)routes[j] * 2 + m) * a.I + g * kTileRows + lane] = v;
-        },
-        nullptr, 0, a.err);
-    if (!ok) return;
-    __threadfence();
-    __syncwarp();
-    unsigned old = 0;
-    if (lane == 0) old = atomicAdd(&a.gu_cnt[e * TI + g], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != 1u) return;
-    __threadfence();
-    if (lane == 0) a.gu_cnt[e * TI + g] = 0u;
-    const int nbi = a.I / kQK;
-    for (int j = 0; j < T; j++) {
-        const int r = routes[j];
-        float gv = __ldcg(a.gu + ((size_t)r * 2 + 0) * a.I + g * kTileRows + lane);
-        float uv = __ldcg(a.gu + ((size_t)r * 2 + 1) * a.I + g * kTileRows + lane);
-        float h = fmul(silu(gv), uv);  // expert/mod.rs:100-102
-        float amax = warp_max_abs(h);
-        float scale = fdiv(amax, 127.0f);
-        float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
-        int q = sat_i8(roundf(fmul(h, inv)));
-        int qs = warp_sum_int(q);
-        a.hq[(size_t)r * a.I + g * kTileRows + lane] = (int8_t)q;
-        if (lane == 0) a.haux[(size_t)r * nbi + g] = make_int2(__float_as_int(scale), -8 * qs);
+    const bool live = tile < TI;
+    for (int base = 0; base < T; base += kPassRows) {
+        const int n = min(kPassRows, T - base);
+        if (!xstage_load(xs, a.xq, a.xaux, a.H, nbph, base, n, false, [&](int j) { return routes[j] / k; }, a.err))
+            return;
+        float myv[kPassRows];
+#pragma unroll
+        for (int j = 0; j < kPassRows; j++) myv[j] = 0.0f;
+        bool ok = true;
+        if (live)
+            ok = tile_dot_n<QT>(rg, gtile, nbh, xs, a.H, nbph, n, nullptr, 0, a.err, [&](int j, float v) {
+#pragma unroll
+                for (int q = 0; q < kPassRows; q++) if (q == j) myv[q] = v;
+            });
+        if (m == 0 && live)
+#pragma unroll
+            for (int j = 0; j < kPassRows; j++) s_g[tl][j][lane] = myv[j];
+        if (!__syncthreads_and(ok ? 1 : 0)) return;  // also publishes s_g
+        if (m == 1 && live) {
+            for (int j = 0; j < n; j++) {
+                const int slot = beg + base + j;
+                float h = fmul(silu(s_g[tl][j][lane]), myv[j]);
+                float amax = warp_max_abs(h);
+                float scale = fdiv(amax, 127.0f);
+                float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
+                int q = sat_i8(roundf(fmul(h, inv)));
+                int qs = warp_sum_int(q);
+                a.hq[(size_t)slot * a.I + tile * kTileRows + lane] = (int8_t)q;
+                if (lane == 0) a.haux[(size_t)slot * nbpi + tile] = make_int2(__float_as_int(scale), -8 * qs);
+            }
+        }
     }
 }
 
-// Phase 2: one CTA per (active expert, 32-row tile of the down projection);
-// y for every route of the expert. The last of a token's k routes to land
-// for a tile combines them in best-first order (moe.rs:63-68):
-// out = 0; out += w_s * y_s for s = 0..k-1, unfused.
-template <int QT, int TGMAX>
-__global__ void __launch_bounds__(32) expert_down_kernel(ExpertArgs a) {
+// Phase 2: one CTA (4 warps) per (active expert, 4 consecutive 32-row tiles
+// of the down projection); y for every route of the expert. The last of a
+// token's k routes to land for a 128-row group combines them in best-first
+// order (moe.rs:63-68): out = 0; out += w_s * y_s for s = 0..k-1, unfused.
+template <int QT>
+__global__ void __launch_bounds__(128) expert_down_kernel(ExpertArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_last[kPassRows];
     constexpr int REC = kTileRows * QFmt<QT>::BB;
     const int TI = a.I / kTileRows, TH = a.H / kTileRows, nbi = a.I / kQK, nbh = a.H / kQK;
-    const int u = blockIdx.x, ai = u / TH, g = u % TH;
+    const int nbpi = aux_stride(nbi);
+    const int groups = (TH + 3) / 4;
+    const int ai = blockIdx.x / groups, grp = blockIdx.x % groups;
     if (ai >= *a.n_active) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = grp * 4 + warp;
+    const bool live = tile < TH;
     const int e = a.active[ai];
     const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
-    const int lane = threadIdx.x & 31;
-    const size_t gu_tile = (size_t)nbh * REC;
-    const size_t d_tile = (size_t)nbi * REC;
-    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)2 * TI * gu_tile + (size_t)g * d_tile;
+    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S, 4, a.I);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bars_off);
     Ring rg;
-    ring_init(rg, smem, a.S, kStageBlocks * REC);
+    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S, a.S, P.stage_bytes);
+    XStage xs;
+    xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
+                bars + 4 * a.S);
+    const size_t gu_tile = (size_t)nbh * REC, d_tile = (size_t)nbi * REC;
+    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)2 * TI * gu_tile + (size_t)tile * d_tile;
     const int* routes = a.elist + beg;
-    bool ok = tile_all_rows<QT, TGMAX>(
-        rg, gtile, nbi, a.hq, a.haux, a.I, T, [&](int j) { return routes[j]; },
-        [&](int j, float v) { a.ybuf[(size_t)routes[j] * a.H + g * kTileRows + lane] = v; },
-        nullptr, 0, a.err);
-    if (!ok) return;
-    __threadfence();
-    __syncwarp();
     const int k = a.k;
-    for (int j = 0; j < T; j++) {
-        const int r = routes[j], tok = r / k;
-        unsigned old = 0;
-        if (lane == 0) old = atomicAdd(&a.comb_cnt[(size_t)tok * TH + g], 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != (unsigned)(k - 1)) continue;
+    for (int base = 0; base < T; base += kPassRows) {
+        const int n = min(kPassRows, T - base);
+        if (!xstage_load(xs, a.hq, a.haux, a.I, nbpi, beg + base, n, true, [](int j) { return j; }, a.err))
+            return;
+        bool ok = true;
+        if (live)
+            ok = tile_dot_n<QT>(rg, gtile, nbi, xs, a.I, nbpi, n, nullptr, 0, a.err, [&](int j, float v) {
+                a.ybuf[(size_t)routes[base + j] * a.H + tile * kTileRows + lane] = v;
+            });
         __threadfence();
-        if (lane == 0) a.comb_cnt[(size_t)tok * TH + g] = 0u;
-        float o = 0.0f;
-        for (int s = 0; s < k; s++) {
-            float w = __ldcg(a.topk_w + (size_t)tok * k + s);
-            float y = __ldcg(a.ybuf + ((size_t)tok * k + s) * a.H + g * kTileRows + lane);
-            o = fadd(o, fmul(w, y));
+        if (!__syncthreads_and(ok ? 1 : 0)) return;
+        if (threadIdx.x < n) {
+            const int tok = routes[base + threadIdx.x] / k;
+            unsigned old = atomicAdd(&a.comb_cnt[(size_t)tok * groups + grp], 1u);
+            s_last[threadIdx.x] = old == (unsigned)(k - 1);
+            if (old == (unsigned)(k - 1)) a.comb_cnt[(size_t)tok * groups + grp] = 0u;
         }
-        a.out[(size_t)tok * a.H + g * kTileRows + lane] = o;
+        __syncthreads();
+        __threadfence();
+        for (int j = 0; j < n; j++) {
+            if (!s_last[j] || !live) continue;
+            const int tok = routes[base + j] / k;
+            float o = 0.0f;
+            for (int s2 = 0; s2 < k; s2++) {
+                float w = __ldcg(a.topk_w + (size_t)tok * k + s2);
+                float y = __ldcg(a.ybuf + ((size_t)tok * k + s2) * a.H + tile * kTileRows + lane);
+                o = fadd(o, fmul(w, y));
+            }
+            a.out[(size_t)tok * a.H + tile * kTileRows + lane] = o;
+        }
     }
 }
 
