@@ -462,9 +462,15 @@ extern "C" void hale_matrix_destroy(hale_matrix* m) {
     delete m;
 }
 
-// Bulk-copy ring depth per warp: 3 stages of 8 q4 blocks (13.8 KB in flight
-// per warp) or 2 stages of 8 q8 blocks (17.4 KB).
-static int ring_stages(hale_dtype dt) { return dt == HALE_Q4_0 ? 3 : 2; }
+// Bulk-copy ring depth per warp (stages of 8 blocks: 4.6 KB for q4_0,
+// 8.7 KB for q8_0). Large batches keep 2 stages in flight per warp, which
+// leaves room for 3 CTAs per SM; small batches launch few CTAs, so each warp
+// keeps (up to) its whole 2048-column tile in flight to cover HBM latency.
+static int ring_stages(hale_dtype dt, uint32_t m_rows) {
+    if (m_rows <= 2) return dt == HALE_Q4_0 ? 8 : 4;
+    if (m_rows <= 16) return 4;
+    return 2;
+}
 
 template <int QT>
 static hale_status qgemv_go(hale_ctx* ctx, const hale_matrix* m, const int8_t* xq, const int2* xaux, uint32_t M,
@@ -479,7 +485,7 @@ static hale_status qgemv_go(hale_ctx* ctx, const hale_matrix* m, const int8_t* x
 
 static hale_status qgemv_launch(hale_ctx* ctx, const hale_matrix* m, const int8_t* xq, const int2* xaux,
                                 uint32_t M, float* out, int32_t* dbg, cudaStream_t st) {
-    int S_ = ring_stages(m->dtype);
+    int S_ = std::min(ring_stages(m->dtype, M), ((int)m->nb + kStageBlocks - 1) / kStageBlocks);
     hale_status r;
     {
         ProfScope ps_(ctx, "qgemv", st);
@@ -770,9 +776,10 @@ static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32
     a.err = ctx->d_err;
     dim3 grid((M + kRouterTT - 1) / kRouterTT, (a.E + kRouterET - 1) / kRouterET);
     size_t smem = a.staged ? (size_t)2 * router_slot_bytes(a.wdtype == 0 ? 4 : 2) + 16 : 0;
-    CUDA_TRY(ctx, allow_smem(router_kernel, smem));
+    auto* kern = a.wdtype == 0 ? router_kernel<0> : (a.wdtype == 1 ? router_kernel<1> : router_kernel<2>);
+    CUDA_TRY(ctx, allow_smem(kern, smem));
     ProfScope ps_(ctx, "router", st);
-    router_kernel<<<grid, 256, smem, st>>>(a);
+    kern<<<grid, 256, smem, st>>>(a);
     return check_launch(ctx, "router");
 }
 
@@ -794,8 +801,8 @@ extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, u
 template <int QT, int RT>
 static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
     const int TI = a.I / 32, TH = a.H / 32;
-    SmemPlan P1 = smem_plan(QFmt<QT>::BB, a.S, 2 * RT, a.H);
-    SmemPlan P2 = smem_plan(QFmt<QT>::BB, a.S, 4, a.I);
+    SmemPlan P1 = smem_plan(QFmt<QT>::BB, a.S1, 2 * RT, a.H);
+    SmemPlan P2 = smem_plan(QFmt<QT>::BB, a.S2, 4, a.I);
     CUDA_TRY(ctx, allow_smem(expert_gate_up_kernel<QT, RT>, (size_t)P1.total));
     CUDA_TRY(ctx, allow_smem(expert_down_kernel<QT>, (size_t)P2.total));
     unsigned g1 = max_active * (unsigned)((TI + RT - 1) / RT), g2 = max_active * (unsigned)((TH + 3) / 4);
@@ -854,7 +861,9 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
     a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
     a.out = out;
-    a.S = ring_stages(p->dtype);
+    // ring depth, capped at the stages one tile has
+    a.S1 = std::min(ring_stages(p->dtype, M), (H / 32 + kStageBlocks - 1) / kStageBlocks);
+    a.S2 = std::min(ring_stages(p->dtype, M), (I / 32 + kStageBlocks - 1) / kStageBlocks);
     a.err = ctx->d_err;
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
     // small batches: one row tile per CTA pair of warps, for more CTAs

@@ -287,15 +287,17 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
                 uint4 xa = *reinterpret_cast<const uint4*>(xp);
                 uint4 xb = *reinterpret_cast<const uint4*>(xp + 16);
                 int2 ax = xs.a[j * nbp + b];
-                int s = (QT == 0) ? ax.y : 0;
-                s = __dp4a(w[0], (int)xa.x, s);
-                s = __dp4a(w[1], (int)xa.y, s);
-                s = __dp4a(w[2], (int)xa.z, s);
-                s = __dp4a(w[3], (int)xa.w, s);
-                s = __dp4a(w[4], (int)xb.x, s);
-                s = __dp4a(w[5], (int)xb.y, s);
-                s = __dp4a(w[6], (int)xb.z, s);
-                s = __dp4a(w[7], (int)xb.w, s);
+                // two independent dp4a chains (integer sums are exact in any order)
+                int s0 = (QT == 0) ? ax.y : 0, s1 = 0;
+                s0 = __dp4a(w[0], (int)xa.x, s0);
+                s1 = __dp4a(w[4], (int)xb.x, s1);
+                s0 = __dp4a(w[1], (int)xa.y, s0);
+                s1 = __dp4a(w[5], (int)xb.y, s1);
+                s0 = __dp4a(w[2], (int)xa.z, s0);
+                s1 = __dp4a(w[6], (int)xb.z, s1);
+                s0 = __dp4a(w[3], (int)xa.w, s0);
+                s1 = __dp4a(w[7], (int)xb.w, s1);
+                const int s = s0 + s1;
                 if (dbg && j < nvalid) dbg[(size_t)j * dbg_stride + (size_t)lane * nb + b] = s;
                 acc[j] = fadd(acc[j], fmul(fmul(ws, __int_as_float(ax.x)), __int2float_rn(s)));
             }
@@ -310,36 +312,33 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
     return ok;
 }
 
-// Runs tile_dot with the pass width TG chosen at run time (smallest power of
-// two >= n, at most kPassRows) and hands the results to emit(j, value).
+// Runs tile_dot with the pass width equal to the pass's row count n (1..8,
+// each width its own unrolled instance) and hands the results to
+// emit(j, value).
+template <int QT, int TG, class Emit>
+__device__ __forceinline__ bool tile_dot_w(Ring& rg, const uint8_t* gtile, int nb, const XStage& xs, int cols,
+                                           int nbp, int32_t* dbg, size_t dbg_stride, uint32_t* err, Emit& emit) {
+    float acc[TG];
+    bool ok = tile_dot<QT, TG>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, TG, err);
+    if (ok)
+#pragma unroll
+        for (int j = 0; j < TG; j++) emit(j, acc[j]);
+    return ok;
+}
+
 template <int QT, class Emit>
 __device__ bool tile_dot_n(Ring& rg, const uint8_t* gtile, int nb, const XStage& xs, int cols, int nbp,
                            int n, int32_t* dbg, size_t dbg_stride, uint32_t* err, Emit emit) {
-    bool ok;
-    if (n <= 1) {
-        float acc[1];
-        ok = tile_dot<QT, 1>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
-        if (ok) emit(0, acc[0]);
-    } else if (n <= 2) {
-        float acc[2];
-        ok = tile_dot<QT, 2>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
-        if (ok)
-#pragma unroll
-            for (int j = 0; j < 2; j++) if (j < n) emit(j, acc[j]);
-    } else if (n <= 4) {
-        float acc[4];
-        ok = tile_dot<QT, 4>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
-        if (ok)
-#pragma unroll
-            for (int j = 0; j < 4; j++) if (j < n) emit(j, acc[j]);
-    } else {
-        float acc[8];
-        ok = tile_dot<QT, 8>(rg, gtile, nb, xs, cols, nbp, acc, dbg, dbg_stride, n, err);
-        if (ok)
-#pragma unroll
-            for (int j = 0; j < 8; j++) if (j < n) emit(j, acc[j]);
+    switch (n) {
+    case 1: return tile_dot_w<QT, 1>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 2: return tile_dot_w<QT, 2>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 3: return tile_dot_w<QT, 3>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 4: return tile_dot_w<QT, 4>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 5: return tile_dot_w<QT, 5>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 6: return tile_dot_w<QT, 6>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    case 7: return tile_dot_w<QT, 7>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
+    default: return tile_dot_w<QT, 8>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
     }
-    return ok;
 }
 
 // Shared-memory plan of the GEMV kernels: per-warp rings, then the
@@ -435,17 +434,21 @@ struct RouterArgs {
     uint32_t* err;
 };
 
-__device__ __forceinline__ float load_w(const void* w, int dt, size_t i) {
-    if (dt == 0) return __ldg(reinterpret_cast<const float*>(w) + i);
+// Router weight element c (DT: 0 f32, 1 f16, 2 bf16) -- a compile-time
+// format, so the chains' loads can be issued ahead of the adds.
+template <int DT>
+__device__ __forceinline__ float load_w(const void* w, size_t i) {
+    if (DT == 0) return __ldg(reinterpret_cast<const float*>(w) + i);
     uint16_t h = __ldg(reinterpret_cast<const unsigned short*>(w) + i);
-    if (dt == 2) return __uint_as_float((uint32_t)h << 16);
+    if (DT == 2) return __uint_as_float((uint32_t)h << 16);
     return half_bits_to_float(h);
 }
 
-__device__ __forceinline__ float smem_w(const uint8_t* row, int dt, int c) {
-    if (dt == 0) return reinterpret_cast<const float*>(row)[c];
+template <int DT>
+__device__ __forceinline__ float smem_w(const uint8_t* row, int c) {
+    if (DT == 0) return reinterpret_cast<const float*>(row)[c];
     uint16_t h = reinterpret_cast<const uint16_t*>(row)[c];
-    if (dt == 2) return __uint_as_float((uint32_t)h << 16);
+    if (DT == 2) return __uint_as_float((uint32_t)h << 16);
     return half_bits_to_float(h);
 }
 
@@ -453,6 +456,7 @@ __host__ __device__ inline int router_slot_bytes(int wbytes) {
     return kRouterET * (kRouterCH + kRouterPad) * wbytes + kRouterTT * (kRouterCH + kRouterPad) * 4;
 }
 
+template <int DT>
 __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned s_flag;
@@ -465,7 +469,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const int e = blockIdx.y * kRouterET + el;
     const bool valid = t < a.M && e < a.E;
     const int full = a.H / 8;
-    const int wb = a.wdtype == 0 ? 4 : 2;
+    constexpr int wb = DT == 0 ? 4 : 2;
     float acc = 0.0f;
     if (a.staged) {
         // two-slot ring of column chunks: [8 router rows][4 token rows]
@@ -513,7 +517,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             if (valid && ok) {
 #pragma unroll 8
                 for (int i = 0; i < steps; i++)
-                    acc = fadd(acc, fmul(smem_w(wrow, a.wdtype, 8 * i + lane8), xrow[8 * i + lane8]));
+                    acc = fadd(acc, fmul(smem_w<DT>(wrow, 8 * i + lane8), xrow[8 * i + lane8]));
             }
             __syncthreads();
             if (tid == 0 && c + 2 < nch) issue(c + 2);
@@ -524,7 +528,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 #pragma unroll 8
         for (int i = 0; i < full; i++) {
             int c = 8 * i + lane8;
-            acc = fadd(acc, fmul(load_w(a.w, a.wdtype, wrow + c), __ldg(xt + c)));
+            acc = fadd(acc, fmul(load_w<DT>(a.w, wrow + c), __ldg(xt + c)));
         }
     }
     // reduce(): ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         float tail = -0.0f;
         const float* xt = a.x + (size_t)t * a.H;
         for (int c = full * 8; c < a.H; c++)
-            tail = fadd(tail, fmul(load_w(a.w, a.wdtype, (size_t)e * a.H + c), xt[c]));
+            tail = fadd(tail, fmul(load_w<DT>(a.w, (size_t)e * a.H + c), xt[c]));
         a.logits[(size_t)t * a.E + e] = fadd(r, tail);
     }
     __threadfence();
@@ -558,8 +562,10 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         for (int i = lane; i < a.E; i += 32) s_e[warp][i] = hale_expf(fsub(__ldcg(lg + i), mx));
         __syncwarp();
         float sum = 0.0f;
-        if (lane == 0)
+        if (lane == 0) {
+#pragma unroll 8
             for (int i = 0; i < a.E; i++) sum = fadd(sum, s_e[warp][i]);
+        }
         sum = __shfl_sync(0xffffffffu, sum, 0);
         __syncwarp();
         for (int i = lane; i < a.E; i += 32) {
@@ -629,17 +635,34 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     __syncthreads();
     for (int i = tid; i < R; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topk_idx + i)], 1);
     __syncthreads();
-    if (tid == 0) {
-        int off = 0, na = 0;
-        for (int i = 0; i < a.E; i++) {
-            a.elist_off[i] = off;
-            s_cur[i] = off;
-            if (s_cnt[i] > 0) a.active[na++] = i;
-            if (a.routing_counts && s_cnt[i] > 0) a.routing_counts[i] += (unsigned long long)s_cnt[i];
-            off += s_cnt[i];
+    // exclusive scans over the (<= 256) experts: route offsets and the
+    // compacted list of experts with work; one expert per thread
+    {
+        const int c = tid < a.E ? s_cnt[tid] : 0;
+        int incl = c, act = c > 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int u = __shfl_up_sync(0xffffffffu, incl, o), v = __shfl_up_sync(0xffffffffu, act, o);
+            if (lane >= o) { incl += u; act += v; }
         }
-        a.elist_off[a.E] = off;
-        *a.n_active = na;
+        __shared__ int w_sum[8], w_act[8];
+        if (lane == 31) { w_sum[warp] = incl; w_act[warp] = act; }
+        __syncthreads();
+        int base_s = 0, base_a = 0;
+        for (int w2 = 0; w2 < warp; w2++) { base_s += w_sum[w2]; base_a += w_act[w2]; }
+        if (tid < a.E) {
+            const int off = base_s + incl - c;
+            a.elist_off[tid] = off;
+            s_cur[tid] = off;
+            if (c > 0) {
+                a.active[base_a + act - 1] = tid;
+                if (a.routing_counts) a.routing_counts[tid] += (unsigned long long)c;
+            }
+        }
+        if (tid == a.E - 1) {
+            a.elist_off[a.E] = base_s + incl;
+            *a.n_active = base_a + act;
+        }
     }
     __syncthreads();
     for (int i = tid; i < R; i += blockDim.x) {
@@ -671,7 +694,7 @@ struct ExpertArgs {
     unsigned* comb_cnt;       // [M, ceil(H / 128)]
     const float* topk_w;      // [M, k]
     float* out;               // [M, H]
-    int S;
+    int S1, S2;               // ring depths of the gate/up and down kernels
     uint32_t* err;
 };
 
@@ -698,13 +721,13 @@ __global__ void __launch_bounds__(64 * RT) expert_gate_up_kernel(ExpertArgs a) {
     const int tile = (blockIdx.x % units) * RT + tl;    // tile of the intermediate dim
     const int e = a.active[ai];
     const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
-    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S, W, a.H);
+    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S1, W, a.H);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bars_off);
     Ring rg;
-    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S, a.S, P.stage_bytes);
+    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S1, a.S1, P.stage_bytes);
     XStage xs;
     xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
-                bars + W * a.S);
+                bars + W * a.S1);
     const size_t tile_bytes = (size_t)nbh * REC;
     const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)(m * TI + tile) * tile_bytes;
     const int* routes = a.elist + beg;
@@ -762,13 +785,13 @@ __global__ void __launch_bounds__(128) expert_down_kernel(ExpertArgs a) {
     const bool live = tile < TH;
     const int e = a.active[ai];
     const int beg = a.elist_off[e], T = a.elist_off[e + 1] - beg;
-    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S, 4, a.I);
+    const SmemPlan P = smem_plan(QFmt<QT>::BB, a.S2, 4, a.I);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bars_off);
     Ring rg;
-    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S, a.S, P.stage_bytes);
+    ring_init(rg, smem + warp * P.ring_bytes, bars + warp * a.S2, a.S2, P.stage_bytes);
     XStage xs;
     xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
-                bars + 4 * a.S);
+                bars + 4 * a.S2);
     const size_t gu_tile = (size_t)nbh * REC, d_tile = (size_t)nbi * REC;
     const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)2 * TI * gu_tile + (size_t)tile * d_tile;
     const int* routes = a.elist + beg;
