@@ -182,6 +182,7 @@ static bool stream_capturing(void* stream) {
 }
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 static bool is_quant(hale_dtype d) { return d == HALE_Q8_0 || d == HALE_Q4_0; }
 static bool is_float(hale_dtype d) { return d == HALE_F32 || d == HALE_F16 || d == HALE_BF16; }
@@ -527,6 +528,8 @@ extern "C" hale_status hale_quantize_q8(hale_ctx* ctx, const float* x, uint32_t 
     if (cols % 32) return fail(ctx, HALE_E_INVALID_ARGUMENT, "activation length must be a multiple of 32, got %u", cols);
     if (m_rows == 0) return HALE_OK;
     if (!x || !scales || !quants) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_quantize_q8: NULL buffer");
+    if (!aligned16(x) || !aligned16(quants))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_quantize_q8: x and quants must be 16-byte aligned");
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     unsigned grid = (m_rows * 32 + 255) / 256;
     ProfScope ps_(ctx, "quantize", S(stream));
@@ -545,6 +548,7 @@ extern "C" hale_status hale_matrix_matvec(hale_ctx* ctx, const hale_matrix* m, c
         if (block_sums) return fail(ctx, HALE_E_INVALID_ARGUMENT, "block sums exist only for quantized matrices");
         return fgemv_launch(ctx, m, x, m_rows, out, st);
     }
+    if (!aligned16(x)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_matrix_matvec: x must be 16-byte aligned");
     size_t qbytes = align_up((size_t)m_rows * m->cols, 256);
     size_t abytes = (size_t)m_rows * aux_stride((int)m->nb) * 8;
     hale_status rs = ensure_scratch(ctx, qbytes + abytes, stream);
@@ -756,7 +760,8 @@ static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32
     a.M = (int)M;
     a.k = (int)ly->top_k;
     a.normalize = ly->normalize_topk ? 1 : 0;
-    a.staged = (H % 8 == 0) ? 1 : 0;
+    // rows stream through shared memory when they are 16-byte aligned spans
+    a.staged = (H % 8 == 0 && aligned16(x) && aligned16(ly->router)) ? 1 : 0;
     a.x = x;
     a.logits = reinterpret_cast<float*>(ws + L.logits);
     a.probs_out = probs;
@@ -775,7 +780,8 @@ static hale_status launch_router(hale_ctx* ctx, const hale_moe_layer* ly, uint32
     a.grid_cnt = reinterpret_cast<unsigned*>(ws + L.grid_cnt);
     a.err = ctx->d_err;
     dim3 grid((M + kRouterTT - 1) / kRouterTT, (a.E + kRouterET - 1) / kRouterET);
-    size_t smem = a.staged ? (size_t)2 * router_slot_bytes(a.wdtype == 0 ? 4 : 2) + 16 : 0;
+    const int nslots = std::min<int>(((int)H + kRouterCH - 1) / kRouterCH, kRouterSlots);
+    size_t smem = a.staged ? (size_t)nslots * router_slot_bytes(a.wdtype == 0 ? 4 : 2) + 8 * nslots : 0;
     auto* kern = a.wdtype == 0 ? router_kernel<0> : (a.wdtype == 1 ? router_kernel<1> : router_kernel<2>);
     CUDA_TRY(ctx, allow_smem(kern, smem));
     ProfScope ps_(ctx, "router", st);
@@ -833,6 +839,7 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
                     p->layer_resident[ly->layer], p->E);
     if (M == 0) return HALE_OK;
     if (!x || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL buffer");
+    if (!aligned16(x)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: x must be 16-byte aligned");
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     const int E = (int)p->E, k = (int)ly->top_k, H = (int)p->H, I = (int)p->I;
     MoeLayout L;

@@ -99,7 +99,9 @@ HALE_HD double dmul(double a, double b) {
 #endif
 }
 
-HALE_HD float hale_expf(float x) {
+// exp with the 2^(i/32) table read from `tab` (device code may pass a copy
+// in shared memory); hale_expf below uses the built-in table.
+HALE_HD float hale_expf_tab(float x, const uint64_t* tab) {
     // Polynomial and scaling constants of the published method (N = 32).
     const double kInvLn2N = 0x1.71547652b82fep+0 * 32;
     const double kShift = 0x1.8p+52;
@@ -119,11 +121,7 @@ HALE_HD float hale_expf(float x) {
     uint64_t ki = d2u(kd);
     kd -= kShift;
     double r = dfma(kInvLn2N, xd, -kd);
-#ifdef __CUDA_ARCH__
-    uint64_t t = __ldg(&kExp2TabDev[ki & 31]);
-#else
-    uint64_t t = kExp2TabHost[ki & 31];
-#endif
+    uint64_t t = tab[ki & 31];
     // 2^(k/32) = 2^(i/32) * 2^(k div 32): add k div 32 to the exponent field.
     t += (ki >> 5) << 52;
     double s = u2d(t);
@@ -136,6 +134,14 @@ HALE_HD float hale_expf(float x) {
     return __double2float_rn(y);
 #else
     return (float)y;
+#endif
+}
+
+HALE_HD float hale_expf(float x) {
+#ifdef __CUDA_ARCH__
+    return hale_expf_tab(x, kExp2TabDev);
+#else
+    return hale_expf_tab(x, kExp2TabHost);
 #endif
 }
 

@@ -88,18 +88,37 @@ __global__ void repack_float_kernel(const uint8_t* __restrict__ src, uint8_t* __
 // ---------------------------------------------------------------------------
 __host__ __device__ __forceinline__ int aux_stride(int nb) { return (nb + 1) & ~1; }
 
+// One block of Q8Activations::quantize by one thread: the 32 values come in
+// with eight 16-byte loads and leave with two 16-byte stores (xb, q 16-byte
+// aligned: rows of a multiple of 32 elements).
 __device__ __forceinline__ void quantize_block(const float* __restrict__ xb, int8_t* __restrict__ q,
                                                float* scale_out, int* sum_out) {
+    float v[kQK];
+#pragma unroll
+    for (int j = 0; j < kQK / 4; j++) {
+        float4 f = __ldg(reinterpret_cast<const float4*>(xb) + j);
+        v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    }
     float amax = 0.0f;
-    for (int j = 0; j < kQK; j++) amax = fmaxf(amax, fabsf(xb[j]));
+#pragma unroll
+    for (int j = 0; j < kQK; j++) amax = fmaxf(amax, fabsf(v[j]));
     float scale = fdiv(amax, 127.0f);
     float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
     int s = 0;
-    for (int j = 0; j < kQK; j++) {
-        int v = sat_i8(roundf(fmul(xb[j], inv)));
-        q[j] = (int8_t)v;
-        s += v;
+    uint32_t packed[kQK / 4];
+#pragma unroll
+    for (int j = 0; j < kQK / 4; j++) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int qv = sat_i8(roundf(fmul(v[4 * j + i], inv)));
+            s += qv;
+            w |= ((uint32_t)qv & 0xffu) << (8 * i);
+        }
+        packed[j] = w;
     }
+    reinterpret_cast<uint4*>(q)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    reinterpret_cast<uint4*>(q)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     *scale_out = scale;
     *sum_out = s;
 }
@@ -409,6 +428,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const uint8_t* __restrict__ 
 // expert for the expert kernels.
 // ---------------------------------------------------------------------------
 constexpr int kRouterTT = 4, kRouterET = 8, kRouterCH = 512, kRouterPad = 8;  // pad: 8-bank row skew
+constexpr int kRouterSlots = 4;
 
 struct RouterArgs {
     const void* w;
@@ -460,7 +480,8 @@ template <int DT>
 __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ unsigned s_flag;
-    __shared__ float s_e[8][256];
+    __shared__ uint64_t s_tab[32];
+    __shared__ __align__(16) float s_e[8][256];
     __shared__ int s_cnt[256];
     __shared__ int s_cur[256];
     const int tid = threadIdx.x, lane8 = tid & 7, pair = tid >> 3;
@@ -470,47 +491,49 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const bool valid = t < a.M && e < a.E;
     const int full = a.H / 8;
     constexpr int wb = DT == 0 ? 4 : 2;
+    if (tid < 32) s_tab[tid] = kExp2TabDev[tid];  // exp table for the tail (read after barriers)
     float acc = 0.0f;
     if (a.staged) {
-        // two-slot ring of column chunks: [8 router rows][4 token rows]
+        // ring of column chunks [8 router rows][4 token rows]; with up to
+        // kRouterSlots slots every chunk of a 2048-wide row is in flight at once
         const int slot_bytes = router_slot_bytes(wb);
-        uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * slot_bytes);
         const int nch = (a.H + kRouterCH - 1) / kRouterCH;
+        const int NS = min(nch, kRouterSlots);
+        uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NS * slot_bytes);
         const int rpitch = (kRouterCH + kRouterPad) * wb, xpitch = (kRouterCH + kRouterPad) * 4;
         if (tid == 0) {
-            mbar_init(&bars[0], 1);
-            mbar_init(&bars[1], 1);
+            for (int q = 0; q < NS; q++) mbar_init(&bars[q], 1);
             fence_mbar_init();
         }
         __syncthreads();
         auto issue = [&](int c) {
-            uint8_t* slot = smem + (c & 1) * slot_bytes;
+            const int q = c % NS;
+            uint8_t* slot = smem + q * slot_bytes;
             const int c0 = c * kRouterCH, len = min(kRouterCH, a.H - c0);
             const int nr = min(kRouterET, a.E - (int)blockIdx.y * kRouterET);
             const int nt = min(kRouterTT, a.M - (int)blockIdx.x * kRouterTT);
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&bars[c & 1], (uint32_t)(nr * len * wb + nt * len * 4));
+            mbar_arrive_expect_tx(&bars[q], (uint32_t)(nr * len * wb + nt * len * 4));
             for (int r = 0; r < nr; r++)
                 bulk_g2s(slot + r * rpitch,
                          reinterpret_cast<const uint8_t*>(a.w) + ((size_t)(blockIdx.y * kRouterET + r) * a.H + c0) * wb,
-                         (uint32_t)(len * wb), &bars[c & 1]);
+                         (uint32_t)(len * wb), &bars[q]);
             for (int r = 0; r < nt; r++)
                 bulk_g2s(slot + kRouterET * rpitch + r * xpitch,
                          a.x + (size_t)(blockIdx.x * kRouterTT + r) * a.H + c0, (uint32_t)(len * 4),
-                         &bars[c & 1]);
+                         &bars[q]);
         };
-        if (tid == 0) {
-            issue(0);
-            if (nch > 1) issue(1);
-        }
+        if (tid == 0)
+            for (int c = 0; c < NS; c++) issue(c);
         uint32_t phase = 0;
         bool ok = true;
         for (int c = 0; c < nch; c++) {
+            const int q = c % NS;
             // every chunk is waited on (bounded) even after a timeout, so no
             // copy is still landing when the CTA moves on
-            ok = mbar_wait(&bars[c & 1], (phase >> (c & 1)) & 1u, a.err) && ok;
-            phase ^= 1u << (c & 1);
-            const uint8_t* slot = smem + (c & 1) * slot_bytes;
+            ok = mbar_wait(&bars[q], (phase >> q) & 1u, a.err) && ok;
+            phase ^= 1u << q;
+            const uint8_t* slot = smem + q * slot_bytes;
             const uint8_t* wrow = slot + el * rpitch;
             const float* xrow = reinterpret_cast<const float*>(slot + kRouterET * rpitch + tl * xpitch);
             const int steps = min(kRouterCH, a.H - c * kRouterCH) / 8;
@@ -520,7 +543,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
                     acc = fadd(acc, fmul(smem_w<DT>(wrow, 8 * i + lane8), xrow[8 * i + lane8]));
             }
             __syncthreads();
-            if (tid == 0 && c + 2 < nch) issue(c + 2);
+            if (tid == 0 && c + NS < nch) issue(c + NS);
         }
     } else if (valid) {
         const float* xt = a.x + (size_t)t * a.H;
@@ -559,12 +582,17 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         for (int i = lane; i < a.E; i += 32) mx = fmaxf(mx, __ldcg(lg + i));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        for (int i = lane; i < a.E; i += 32) s_e[warp][i] = hale_expf(fsub(__ldcg(lg + i), mx));
+        for (int i = lane; i < a.E; i += 32) s_e[warp][i] = hale_expf_tab(fsub(__ldcg(lg + i), mx), s_tab);
         __syncwarp();
+        // the reference's left-to-right sum, on one lane, loads batched 4 wide
         float sum = 0.0f;
         if (lane == 0) {
-#pragma unroll 8
-            for (int i = 0; i < a.E; i++) sum = fadd(sum, s_e[warp][i]);
+            int i = 0;
+            for (; i + 4 <= a.E; i += 4) {
+                float4 q4 = *reinterpret_cast<const float4*>(&s_e[warp][i]);
+                sum = fadd(fadd(fadd(fadd(sum, q4.x), q4.y), q4.z), q4.w);
+            }
+            for (; i < a.E; i++) sum = fadd(sum, s_e[warp][i]);
         }
         sum = __shfl_sync(0xffffffffu, sum, 0);
         __syncwarp();
@@ -574,25 +602,29 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             if (a.probs_out) a.probs_out[(size_t)tok * a.E + i] = pv;
         }
         __syncwarp();
-        // top-k by (total_cmp desc, index asc)
+        // top-k by (total_cmp desc, index asc): keys in registers as unsigned
+        // total-order keys; each round a warp max over keys, then the lowest
+        // index holding it (topk.rs:27-35)
+        unsigned ukey[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = lane + 32 * j;
+            ukey[j] = i < a.E ? ((unsigned)total_key(s_e[warp][i]) ^ 0x80000000u) : 0u;
+        }
         unsigned taken = 0u;  // bit j: element lane + 32 j selected (E <= 256)
         float chosen_score = 0.0f;
         int chosen_idx = -1;
         float norm = -0.0f;
         for (int kk = 0; kk < a.k; kk++) {
-            int bk = INT_MIN, bi = INT_MAX;
-            for (int j = 0, i = lane; i < a.E; j++, i += 32) {
-                if (taken & (1u << j)) continue;
-                int key = total_key(s_e[warp][i]);
-                if (key > bk || (key == bk && i < bi)) { bk = key; bi = i; }
-            }
+            unsigned bk = 0u;
+            int bj = -1;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                int ok2 = __shfl_xor_sync(0xffffffffu, bk, o);
-                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ok2 > bk || (ok2 == bk && oi < bi)) { bk = ok2; bi = oi; }
-            }
-            if (bi != INT_MAX && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+            for (int j = 0; j < 8; j++)
+                if (!(taken & (1u << j)) && lane + 32 * j < a.E && (bj < 0 || ukey[j] > bk)) { bk = ukey[j]; bj = j; }
+            const unsigned wk = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
+            const unsigned mine = (bj >= 0 && bk == wk) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
+            const int bi = (int)__reduce_min_sync(0xffffffffu, mine);
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
             float sc = s_e[warp][bi];
             norm = fadd(norm, sc);
             if (lane == kk) { chosen_score = sc; chosen_idx = bi; }

@@ -21,6 +21,8 @@
  *   - Buffers are caller-owned. Unless a name ends in _host, data pointers
  *     are DEVICE pointers on the context's GPU, and work is enqueued on the
  *     given stream (a cudaStream_t passed as void*; NULL = legacy stream).
+ *   - f32 activation buffers (x) start on a 16-byte boundary (any
+ *     cudaMalloc / torch allocation does); misaligned ones are rejected.
  *   - A hale_ctx is bound to one GPU. Calls on one ctx must not overlap
  *     (the ctx owns one workspace); use one ctx per host thread / stream.
  *   - Results are deterministic: bit-identical run to run, and bit-identical
