@@ -85,6 +85,7 @@ SIGNATURES = {
     "hale_moe_forward": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_forward_host": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_route": (I32, [P, C.POINTER(MoeLayer), U32, P, U32, P, P, P, P]),
+    "hale_moe_route_noalloc": (I32, [P, C.c_int, U32, U32, I32, U32, P, U32, P, P, P, P]),
     "hale_lm_head": (I32, [P, P, P, U32, P, P]),
     "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
     "hale_expf_host": (None, [P, P, U64]),
@@ -283,6 +284,14 @@ def moe_forward_host(ctx, pool, layer, x, out, topk_idx=None, topk_w=None, strea
 def moe_route(ctx, layer, hidden, x, topk_idx, topk_w, probs=None, stream=None):
     ctx.call("hale_moe_route", ctx.h, C.byref(layer), hidden, ptr(x), x.shape[0], ptr(topk_idx),
              ptr(topk_w), ptr(probs), _stream(stream))
+
+
+def moe_route_noalloc(router, router_dtype, n_experts, top_k, normalize, hidden, x, topk_idx,
+                      topk_w, probs=None, stream=None):
+    """hale_moe_route_noalloc: routing on the current device with no allocation."""
+    _check(lib().hale_moe_route_noalloc(ptr(router), router_dtype, n_experts, top_k, int(normalize),
+                                        hidden, ptr(x), x.shape[0], ptr(topk_idx), ptr(topk_w),
+                                        ptr(probs), _stream(stream)))
 
 
 def quantize_q8(ctx, x, scales, quants, stream=None):

@@ -955,6 +955,98 @@ extern "C" hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t 
 }
 
 // ---------------------------------------------------------------------------
+// allocation-free routing (hale_moe_route_noalloc)
+//
+// For hosts that cannot call cudaMalloc on the routing path (graph replay,
+// fixed device-memory arenas). The router's scratch lives in a fixed array of
+// this file; every GPU that loads the library holds it until exit.
+// Layout: [0, 1024) counters -- up to 254 token-tile counters, the grid
+// counter and a device error word -- then the [M, E] f32 router logits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = (size_t)1 << 20;
+constexpr size_t kNoAllocCounterBytes = 1024;
+constexpr uint32_t kNoAllocMaxTiles = 254;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (in host code the symbol is only a stand-in, never a device
+// address).
+static hale_status noalloc_scratch(int device, uint8_t** out) {
+    static std::mutex mu;
+    static std::map<int, uint8_t*> addr;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = addr.find(device);
+    if (it != addr.end()) {
+        *out = it->second;
+        return HALE_OK;
+    }
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        return fail(nullptr, HALE_E_CUDA, "cudaGetSymbolAddress of the routing scratch failed on device %d: %s",
+                    device, cudaGetErrorString(e));
+    addr[device] = static_cast<uint8_t*>(p);
+    *out = static_cast<uint8_t*>(p);
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_moe_route_noalloc(const void* router, hale_dtype router_dtype, uint32_t n_experts,
+                                              uint32_t top_k, int32_t normalize_topk, uint32_t hidden,
+                                              const float* x, uint32_t M, int32_t* topk_idx, float* topk_w,
+                                              float* probs, void* stream) {
+    hale_moe_layer ly{0, router, router_dtype, n_experts, top_k, normalize_topk};
+    hale_status r = check_layer(nullptr, &ly, hidden);
+    if (r) return r;
+    if (M == 0) return HALE_OK;
+    if (!x || !topk_idx || !topk_w) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_moe_route_noalloc: NULL buffer");
+    const uint32_t tiles = (M + kRouterTT - 1) / kRouterTT;
+    const size_t logit_bytes = (size_t)M * n_experts * 4;
+    if (tiles > kNoAllocMaxTiles || logit_bytes > kNoAllocScratchBytes - kNoAllocCounterBytes)
+        return fail(nullptr, HALE_E_INVALID_ARGUMENT,
+                    "hale_moe_route_noalloc: %u tokens x %u experts exceeds the fixed scratch "
+                    "(tokens <= %u and tokens * experts <= %zu)",
+                    M, n_experts, kNoAllocMaxTiles * kRouterTT,
+                    (kNoAllocScratchBytes - kNoAllocCounterBytes) / 4);
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return fail(nullptr, HALE_E_NO_DEVICE, "no current CUDA device: %s", cudaGetErrorString(e));
+    uint8_t* scratch = nullptr;
+    if ((r = noalloc_scratch(device, &scratch))) return r;
+    cudaStream_t st = S(stream);
+    // the counters must start at zero; the previous call may have stopped early
+    e = cudaMemsetAsync(scratch, 0, kNoAllocCounterBytes, st);
+    if (e != cudaSuccess) return fail(nullptr, HALE_E_CUDA, "clearing the routing scratch failed: %s", cudaGetErrorString(e));
+    unsigned* counters = reinterpret_cast<unsigned*>(scratch);
+    RouterArgs a{};
+    a.w = router;
+    a.wdtype = float_code(router_dtype);
+    a.E = (int)n_experts;
+    a.H = (int)hidden;
+    a.M = (int)M;
+    a.k = (int)top_k;
+    a.normalize = normalize_topk ? 1 : 0;
+    a.staged = (hidden % 8 == 0 && aligned16(x) && aligned16(router)) ? 1 : 0;
+    a.x = x;
+    a.logits = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
+    a.probs_out = probs;
+    a.topk_idx = topk_idx;
+    a.topk_w = topk_w;
+    a.tile_cnt = counters;
+    a.grid_cnt = counters + kNoAllocMaxTiles;
+    a.err = counters + kNoAllocMaxTiles + 1;
+    dim3 grid(tiles, (n_experts + kRouterET - 1) / kRouterET);
+    const int nslots = std::min<int>(((int)hidden + kRouterCH - 1) / kRouterCH, kRouterSlots);
+    size_t smem = a.staged ? (size_t)nslots * router_slot_bytes(a.wdtype == 0 ? 4 : 2) + 8 * nslots : 0;
+    auto* kern = a.wdtype == 0 ? router_kernel<0> : (a.wdtype == 1 ? router_kernel<1> : router_kernel<2>);
+    e = allow_smem(kern, smem);
+    if (e != cudaSuccess) return fail(nullptr, HALE_E_CUDA, "router shared-memory opt-in failed: %s", cudaGetErrorString(e));
+    kern<<<grid, 256, smem, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(nullptr, HALE_E_CUDA, "launch of router failed: %s", cudaGetErrorString(e));
+    return HALE_OK;
+}
+
+// ---------------------------------------------------------------------------
 // self-check
 // ---------------------------------------------------------------------------
 extern "C" void hale_expf_host(const float* x, float* y, uint64_t n) {

@@ -223,6 +223,27 @@ HALE_API hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* layer, 
                            const float* x, uint32_t m_tokens, int32_t* topk_idx, float* topk_w,
                            float* probs, void* stream);
 
+/* Routing that allocates nothing. No counterpart in the reference: it exists
+ * for hosts that cannot call cudaMalloc on the routing path -- a serving loop
+ * replaying captured CUDA graphs (allocation is not permitted inside stream
+ * capture and would add a device-wide synchronisation), or an embedding that
+ * hands all device memory to its own fixed arena up front. Same arguments and
+ * results as hale_moe_route, without a context: it runs on the calling
+ * thread's current device. Its scratch (router logits and a few counters) is
+ * a fixed 1 MiB array inside this library, held on every GPU that loads the
+ * library until the process exits, so m_tokens * n_experts must be at most
+ * 261,888 and m_tokens at most 1016 (larger requests are rejected with
+ * HALE_E_INVALID_ARGUMENT). The first call on a device looks up that array's
+ * device address; make it before any stream capture. Calls share the array:
+ * calls that overlap on the GPU race, so keep them on one stream. Errors are
+ * reported through hale_last_error(NULL, ...); a device-side wait that times
+ * out is not reported by this entry point. */
+HALE_API hale_status hale_moe_route_noalloc(const void* router, hale_dtype router_dtype,
+                                            uint32_t n_experts, uint32_t top_k,
+                                            int32_t normalize_topk, uint32_t hidden,
+                                            const float* x, uint32_t m_tokens, int32_t* topk_idx,
+                                            float* topk_w, float* probs, void* stream);
+
 /* ---- sampling tail -------------------------------------------------------- */
 
 /* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .
