@@ -142,11 +142,29 @@ def _stream(stream):
 
 
 class Context:
-    """hale_ctx: one GPU and its workspace."""
+    """hale_ctx: one GPU and its workspace.
 
-    def __init__(self, device=0):
+    expert_kernel picks the expert-kernel family for this context: "auto"
+    (by batch shape), "tc" (tensor cores wherever the shapes allow) or "dp4a".
+    The library reads it from HALE_EXPERT_KERNEL when the context is created;
+    None leaves that variable as it is.
+    """
+
+    def __init__(self, device=0, expert_kernel=None):
         h = P()
-        _check(lib().hale_ctx_create(device, C.byref(h)))
+        old = os.environ.get("HALE_EXPERT_KERNEL")
+        if expert_kernel is not None:
+            if expert_kernel not in ("auto", "tc", "dp4a"):
+                raise ValueError(f"expert_kernel must be auto, tc or dp4a, not {expert_kernel!r}")
+            os.environ["HALE_EXPERT_KERNEL"] = expert_kernel
+        try:
+            _check(lib().hale_ctx_create(device, C.byref(h)))
+        finally:
+            if expert_kernel is not None:
+                if old is None:
+                    os.environ.pop("HALE_EXPERT_KERNEL", None)
+                else:
+                    os.environ["HALE_EXPERT_KERNEL"] = old
         self.h = h
         self.device = device
 

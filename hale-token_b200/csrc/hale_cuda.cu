@@ -9,6 +9,7 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -17,6 +18,7 @@
 
 #include "../../include/hale_cuda.h"
 #include "hale_kernels.cuh"
+#include "hale_tc.cuh"
 
 using namespace hale;
 
@@ -31,6 +33,9 @@ thread_local hale_status g_thread_status = HALE_OK;
 struct hale_ctx {
     int device = 0;
     int sm_count = 0;
+    // expert kernel family: 0 = by batch shape, 1 = tensor cores wherever the
+    // shapes allow, 2 = dp4a only (environment HALE_EXPERT_KERNEL=auto|tc|dp4a)
+    int expert_kernel = 0;
     std::string msg;
     hale_status status = HALE_OK;
     uint32_t* d_err = nullptr;
@@ -230,6 +235,10 @@ extern "C" hale_status hale_ctx_create(int device, hale_ctx** out) {
     hale_ctx* c = new hale_ctx();
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
+    if (const char* ek = std::getenv("HALE_EXPERT_KERNEL")) {
+        if (!std::strcmp(ek, "tc")) c->expert_kernel = 1;
+        else if (!std::strcmp(ek, "dp4a")) c->expert_kernel = 2;
+    }
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&c->d_err, 4) != cudaSuccess ||
         cudaMemset(c->d_err, 0, 4) != cudaSuccess) {
         delete c;
@@ -804,6 +813,42 @@ extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, u
     return launch_router(ctx, ly, hidden, x, M, L, false, topk_idx, topk_w, probs, nullptr, S(stream));
 }
 
+// Tensor-core expert kernels (hale_tc.cuh). A kind::i8 tcgen05.mma of K = 32
+// (one quantization block) costs ~190 cycles of issue on B200 whatever its N
+// (16..256), so with one MMA per 128 rows x 1 block they only pay off once
+// experts see many tokens each; measured on the layer shapes here they are not
+// yet faster than the dp4a kernels at any batch size, so "auto" keeps dp4a
+// and HALE_EXPERT_KERNEL=tc selects them.
+static constexpr uint32_t kTcMinTokens = 1u << 30;
+static bool use_tc(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
+    if (ctx->expert_kernel == 2 || I % 64 != 0 || H % 128 != 0) return false;
+    if (ctx->expert_kernel == 0 && M < kTcMinTokens) return false;
+    return tc_plan_ok(dt == HALE_Q4_0 ? tc_plan(QFmt<0>::BB, TcStage<0>::SB) : tc_plan(QFmt<1>::BB, TcStage<1>::SB));
+}
+
+// Persistent launches: one CTA per SM (each holds 512 TMEM columns and most of
+// the shared memory), looping over the (expert, 128-row) units.
+template <int QT, int PW>
+static hale_status expert_go_tc(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
+    const int TI = a.I / 32, TH = a.H / 32;
+    const TcPlan P = tc_plan(QFmt<QT>::BB, TcStage<QT>::SB);
+    CUDA_TRY(ctx, allow_smem(expert_gate_up_tc_kernel<QT, PW>, (size_t)P.total));
+    CUDA_TRY(ctx, allow_smem(expert_down_tc_kernel<QT, PW>, (size_t)P.total));
+    const unsigned sms = (unsigned)ctx->sm_count;
+    unsigned g1 = std::min(max_active * (unsigned)(TI / 2), sms), g2 = std::min(max_active * (unsigned)(TH / 4), sms);
+    {
+        ProfScope ps_(ctx, "expert_gate_up", st);
+        expert_gate_up_tc_kernel<QT, PW><<<g1, kTcThreads, P.total, st>>>(a);
+    }
+    hale_status r = check_launch(ctx, "expert_gate_up_tc");
+    if (r) return r;
+    {
+        ProfScope ps_(ctx, "expert_down", st);
+        expert_down_tc_kernel<QT, PW><<<g2, kTcThreads, P.total, st>>>(a);
+    }
+    return check_launch(ctx, "expert_down_tc");
+}
+
 template <int QT, int RT>
 static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
     const int TI = a.I / 32, TH = a.H / 32;
@@ -873,6 +918,13 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.S2 = std::min(ring_stages(p->dtype, M), (I / 32 + kStageBlocks - 1) / kStageBlocks);
     a.err = ctx->d_err;
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
+    if (use_tc(ctx, p->dtype, M, H, I)) {
+        // 16-token passes once experts average ~16 tokens; 8-token passes below
+        const bool wide = (long long)M * k >= 16LL * E;
+        if (p->dtype == HALE_Q4_0)
+            return wide ? expert_go_tc<0, 16>(ctx, a, max_active, st) : expert_go_tc<0, 8>(ctx, a, max_active, st);
+        return wide ? expert_go_tc<1, 16>(ctx, a, max_active, st) : expert_go_tc<1, 8>(ctx, a, max_active, st);
+    }
     // small batches: one row tile per CTA pair of warps, for more CTAs
     bool small = M <= 2;
     if (p->dtype == HALE_Q4_0)
