@@ -200,14 +200,17 @@ __device__ __forceinline__ void ring_init(Ring& rg, uint8_t* buf, uint64_t* bars
     __syncwarp();
 }
 
-// Activation rows of one pass, in shared memory: quants [kPassRows][cols]
-// and aux [kPassRows][nbp].
+// Activation rows of one pass, in shared memory: quants [kPassRows][stride]
+// with stride = cols + 16 (the pad puts the 8 rows an MMA B fragment reads
+// in distinct banks), and aux [kPassRows][nbp].
 struct XStage {
     int8_t* q;
     int2* a;
     uint64_t* bar;
     uint32_t phase;
 };
+
+__host__ __device__ inline int xstage_stride(int cols) { return cols + 16; }
 
 __device__ __forceinline__ void xstage_init(XStage& xs, int8_t* q, int2* a, uint64_t* bar) {
     xs.q = q;
@@ -223,23 +226,25 @@ __device__ __forceinline__ void xstage_init(XStage& xs, int8_t* q, int2* a, uint
 
 // Gathers activation rows row_of(base .. base+n-1) into the stage (all
 // threads call; thread 0 issues). contiguous: the rows are consecutive in
-// global memory (one copy each for quants and aux).
+// global memory (one copy for the aux rows).
 template <class RowOf>
 __device__ bool xstage_load(XStage& xs, const int8_t* __restrict__ gq, const int2* __restrict__ ga,
                             int cols, int nbp, int base, int n, bool contiguous, RowOf row_of,
                             uint32_t* err) {
     __syncthreads();  // every warp is done with the previous pass
     if (threadIdx.x == 0) {
+        const int stride = xstage_stride(cols);
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(xs.bar, (uint32_t)n * (uint32_t)(cols + nbp * 8));
         if (contiguous) {
             int r = row_of(base);
-            bulk_g2s(xs.q, gq + (size_t)r * cols, (uint32_t)(n * cols), xs.bar);
+            for (int j = 0; j < n; j++)
+                bulk_g2s(xs.q + (size_t)j * stride, gq + (size_t)(r + j) * cols, (uint32_t)cols, xs.bar);
             bulk_g2s(xs.a, ga + (size_t)r * nbp, (uint32_t)(n * nbp * 8), xs.bar);
         } else {
             for (int j = 0; j < n; j++) {
                 int r = row_of(base + j);
-                bulk_g2s(xs.q + (size_t)j * cols, gq + (size_t)r * cols, (uint32_t)cols, xs.bar);
+                bulk_g2s(xs.q + (size_t)j * stride, gq + (size_t)r * cols, (uint32_t)cols, xs.bar);
                 bulk_g2s(xs.a + (size_t)j * nbp, ga + (size_t)r * nbp, (uint32_t)(nbp * 8), xs.bar);
             }
         }
@@ -302,7 +307,7 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
             }
 #pragma unroll
             for (int j = 0; j < TG; j++) {
-                const int8_t* xp = xs.q + j * cols + b * kQK;
+                const int8_t* xp = xs.q + j * xstage_stride(cols) + b * kQK;
                 uint4 xa = *reinterpret_cast<const uint4*>(xp);
                 uint4 xb = *reinterpret_cast<const uint4*>(xp + 16);
                 int2 ax = xs.a[j * nbp + b];
@@ -331,6 +336,119 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
     return ok;
 }
 
+// Exact int -> float of a biased block sum through the f32 significand: for
+// |v| < 2^22 the bits (kMagicI + v) read as a float equal 1.5 * 2^23 + v
+// exactly, and subtracting 1.5 * 2^23 leaves v. Block sums are bounded by
+// 32 * 128 * 127 < 2^22.
+constexpr int kMagicI = 0x4B400000;
+constexpr float kMagicF = 12582912.0f;
+
+// D = A(16x32 s8, row) x B(32x8 s8, col) + C (s32), warp-wide.
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0,
+                                             int c1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+}
+
+// The same dot products as tile_dot for a pass of up to kPassRows tokens, on
+// the warp-level tensor-core MMA: per block, one m16n8k32 per 16 rows gives
+// the integer block sums of 16 rows x 8 tokens; C carries q4_0's -8 * sum(x)
+// and kMagicI, so D reads as the biased sum the exact conversion needs. Then
+// the reference's float step per (row, token), in block order.
+// Lane = 4 g + t holds rows {g, g+8, g+16, g+24} x tokens {2t, 2t+1}. The
+// results land in the warp's ring buffer as float [kPassRows][32] (token,
+// row), which is free once every stage has been consumed.
+template <int QT>
+__device__ bool tile_dot_mma(Ring& rg, const uint8_t* __restrict__ gtile, int nb, const XStage& xs, int cols,
+                             int nbp, uint32_t* err) {
+    constexpr int BB = QFmt<QT>::BB, QB = QFmt<QT>::QB, REC = kTileRows * BB;
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int nst = (nb + kStageBlocks - 1) / kStageBlocks;
+    float acc[2][2][2];  // [16-row half][row g or g+8][token 2t or 2t+1]
+#pragma unroll
+    for (int i = 0; i < 8; i++) (&acc[0][0][0])[i] = 0.0f;
+    if (lane == 0) {
+        fence_proxy_async_smem();  // earlier passes read these slots
+        for (int st = 0; st < min(rg.S, nst); st++) ring_issue<QT>(rg, gtile, nb, st);
+    }
+    const int8_t* xrow = xs.q + g * xstage_stride(cols) + 4 * t;  // token g's row (B column g)
+    const int2* a0row = xs.a + (2 * t) * nbp;
+    const int2* a1row = xs.a + (2 * t + 1) * nbp;
+    bool ok = true;
+    for (int st = 0; st < nst; st++) {
+        int slot = st % rg.S;
+        if (!__all_sync(0xffffffffu, mbar_wait(&rg.bars[slot], (rg.phase >> slot) & 1u, err))) {
+            ok = false;
+            for (int s2 = st; s2 < min(st + rg.S, nst); s2++)
+                mbar_wait(&rg.bars[s2 % rg.S], (rg.phase >> (s2 % rg.S)) & 1u, nullptr, 400000000LL);
+            break;
+        }
+        rg.phase ^= 1u << slot;
+        const uint8_t* sbuf = rg.buf + (size_t)slot * rg.stage_bytes;
+        const int nblk = min(kStageBlocks, nb - st * kStageBlocks);
+#pragma unroll 2
+        for (int bi = 0; bi < nblk; bi++) {
+            const int b = st * kStageBlocks + bi;
+            const uint8_t* rec = sbuf + bi * REC;
+            const uint32_t bf0 = *reinterpret_cast<const uint32_t*>(xrow + b * kQK);
+            const uint32_t bf1 = *reinterpret_cast<const uint32_t*>(xrow + b * kQK + 16);
+            const int2 x0 = a0row[b], x1 = a1row[b];
+            const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
+            const float xs0 = __int_as_float(x0.x), xs1 = __int_as_float(x1.x);
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++) {
+                const int r0 = mt * 16 + g, r1 = r0 + 8;
+                uint32_t a[4];
+                if (QT == 0) {
+                    // byte j of a row holds element j (low nibble) and j + 16 (high)
+                    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 4 * t);
+                    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 4 * t);
+                    a[0] = w0 & 0x0F0F0F0Fu;
+                    a[1] = w1 & 0x0F0F0F0Fu;
+                    a[2] = (w0 >> 4) & 0x0F0F0F0Fu;
+                    a[3] = (w1 >> 4) & 0x0F0F0F0Fu;
+                } else {
+                    a[0] = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 4 * t);
+                    a[1] = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 4 * t);
+                    a[2] = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 16 + 4 * t);
+                    a[3] = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 16 + 4 * t);
+                }
+                int d[4];
+                mma_s8_16832(d, a, bf0, bf1, c0, c1);
+                const float ws0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rec + kTileRows * QB + r0 * 2));
+                const float ws1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rec + kTileRows * QB + r1 * 2));
+                // d: (r0, 2t), (r0, 2t+1), (r1, 2t), (r1, 2t+1)
+                acc[mt][0][0] = fadd(acc[mt][0][0], fmul(fmul(ws0, xs0), fsub(__int_as_float(d[0]), kMagicF)));
+                acc[mt][0][1] = fadd(acc[mt][0][1], fmul(fmul(ws0, xs1), fsub(__int_as_float(d[1]), kMagicF)));
+                acc[mt][1][0] = fadd(acc[mt][1][0], fmul(fmul(ws1, xs0), fsub(__int_as_float(d[2]), kMagicF)));
+                acc[mt][1][1] = fadd(acc[mt][1][1], fmul(fmul(ws1, xs1), fsub(__int_as_float(d[3]), kMagicF)));
+            }
+        }
+        __syncwarp();
+        if (st + rg.S < nst && lane == 0) {
+            fence_proxy_async_smem();
+            ring_issue<QT>(rg, gtile, nb, st + rg.S);
+        }
+    }
+    __syncwarp();
+    if (ok) {
+        float* outb = reinterpret_cast<float*>(rg.buf);  // every issued stage was consumed
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) outb[(2 * t + j) * kTileRows + mt * 16 + h * 8 + g] = acc[mt][h][j];
+    }
+    __syncwarp();
+    return ok;
+}
+
+// Passes of at least this many rows go through tile_dot_mma.
+constexpr int kMmaMinRows = 3;
+
 // Runs tile_dot with the pass width equal to the pass's row count n (1..8,
 // each width its own unrolled instance) and hands the results to
 // emit(j, value).
@@ -345,9 +463,21 @@ __device__ __forceinline__ bool tile_dot_w(Ring& rg, const uint8_t* gtile, int n
     return ok;
 }
 
+// use_mma (uniform across the CTA): passes of kMmaMinRows or more rows take
+// the tensor-core path; the block-sum debug output needs use_mma false.
 template <int QT, class Emit>
 __device__ bool tile_dot_n(Ring& rg, const uint8_t* gtile, int nb, const XStage& xs, int cols, int nbp,
-                           int n, int32_t* dbg, size_t dbg_stride, uint32_t* err, Emit emit) {
+                           int n, int32_t* dbg, size_t dbg_stride, bool use_mma, uint32_t* err, Emit emit) {
+    if (use_mma && n >= kMmaMinRows) {
+        const bool ok = tile_dot_mma<QT>(rg, gtile, nb, xs, cols, nbp, err);
+        if (ok) {
+            const float* res = reinterpret_cast<const float*>(rg.buf);
+            const int lane = threadIdx.x & 31;
+            for (int j = 0; j < n; j++) emit(j, res[j * kTileRows + lane]);
+        }
+        __syncwarp();  // results read before the next pass's copies reuse the ring
+        return ok;
+    }
     switch (n) {
     case 1: return tile_dot_w<QT, 1>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
     case 2: return tile_dot_w<QT, 2>(rg, gtile, nb, xs, cols, nbp, dbg, dbg_stride, err, emit);
@@ -372,7 +502,7 @@ __host__ __device__ inline SmemPlan smem_plan(int BB, int S, int warps, int cols
     p.ring_bytes = S * p.stage_bytes;
     p.xq_off = warps * p.ring_bytes;
     int nbp = aux_stride(cols / kQK);
-    p.xa_off = p.xq_off + ((kPassRows * cols + 15) & ~15);
+    p.xa_off = p.xq_off + kPassRows * xstage_stride(cols);
     p.bars_off = p.xa_off + kPassRows * nbp * 8;
     p.total = p.bars_off + (warps * S + 1) * 8;
     return p;
@@ -407,7 +537,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const uint8_t* __restrict__ 
         if (!xstage_load(xs, xq, xaux, cols, nbp, base, n, true, [](int j) { return j; }, err)) return;
         if (g >= ntiles) continue;
         int32_t* d = (dbg && row < rows) ? dbg + (size_t)base * rows * nb + (size_t)g * kTileRows * nb : nullptr;
-        tile_dot_n<QT>(rg, gtile, nb, xs, cols, nbp, n, d, (size_t)rows * nb, err, [&](int j, float v) {
+        tile_dot_n<QT>(rg, gtile, nb, xs, cols, nbp, n, d, (size_t)rows * nb, dbg == nullptr, err, [&](int j, float v) {
             if (row < rows) out[(size_t)(base + j) * rows + row] = v;
         });
     }
@@ -774,7 +904,7 @@ __global__ void __launch_bounds__(64 * RT) expert_gate_up_kernel(ExpertArgs a) {
         for (int j = 0; j < kPassRows; j++) myv[j] = 0.0f;
         bool ok = true;
         if (live)
-            ok = tile_dot_n<QT>(rg, gtile, nbh, xs, a.H, nbph, n, nullptr, 0, a.err, [&](int j, float v) {
+            ok = tile_dot_n<QT>(rg, gtile, nbh, xs, a.H, nbph, n, nullptr, 0, true, a.err, [&](int j, float v) {
 #pragma unroll
                 for (int q = 0; q < kPassRows; q++) if (q == j) myv[q] = v;
             });
@@ -834,7 +964,7 @@ __global__ void __launch_bounds__(128) expert_down_kernel(ExpertArgs a) {
             return;
         bool ok = true;
         if (live)
-            ok = tile_dot_n<QT>(rg, gtile, nbi, xs, a.I, nbpi, n, nullptr, 0, a.err, [&](int j, float v) {
+            ok = tile_dot_n<QT>(rg, gtile, nbi, xs, a.I, nbpi, n, nullptr, 0, true, a.err, [&](int j, float v) {
                 a.ybuf[(size_t)routes[base + j] * a.H + tile * kTileRows + lane] = v;
             });
         __threadfence();

@@ -97,6 +97,22 @@ def test_quantized_matvec_and_block_sums_are_bit_exact(ctx, dtype, rows, cols, m
 
 
 @pytest.mark.parametrize("dtype", [fmt.Q4_0, fmt.Q8_0])
+@pytest.mark.parametrize("rows,cols,m", [(70, 64, 3), (96, 2048, 8), (33, 768, 13), (768, 2048, 5)])
+def test_quantized_matvec_without_block_sums_is_bit_exact(ctx, dtype, rows, cols, m):
+    """Without the block-sum output, passes of 3+ rows take the warp-level
+    tensor-core MMA path; results must not change."""
+    rng = np.random.default_rng(rows * 11 + cols + m)
+    enc = fmt.encode(dtype, rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((m, cols)).astype(np.float32)
+    mat = hale.Matrix(ctx, dtype, rows, cols, enc)
+    out = torch.zeros((m, rows), dtype=torch.float32, device="cuda")
+    mat.matvec(dev(x), out)
+    torch.cuda.synchronize()
+    want = np.stack([O.matvec(dtype, enc, rows, cols, x[t]) for t in range(m)])
+    assert_bit_equal(out.cpu().numpy(), want, "matvec")
+
+
+@pytest.mark.parametrize("dtype", [fmt.Q4_0, fmt.Q8_0])
 def test_block_sums_are_bit_exact_on_identical_quantized_inputs(ctx, dtype):
     """dot_quantized with caller-supplied Q8Activations (quant.rs:107-113)."""
     rng = np.random.default_rng(11)
