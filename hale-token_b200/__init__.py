@@ -145,7 +145,9 @@ class Context:
     """hale_ctx: one GPU and its workspace.
 
     expert_kernel picks the expert-kernel family for this context: "auto"
-    (by batch shape), "tc" (tensor cores wherever the shapes allow) or "dp4a".
+    (by batch shape), "tc" (tcgen05 kernels), "ps" (persistent streaming
+    warp-MMA kernels) or "dp4a" (per-CTA kernels); the first two wherever the
+    shapes allow.
     The library reads it from HALE_EXPERT_KERNEL when the context is created;
     None leaves that variable as it is.
     """
@@ -154,8 +156,8 @@ class Context:
         h = P()
         old = os.environ.get("HALE_EXPERT_KERNEL")
         if expert_kernel is not None:
-            if expert_kernel not in ("auto", "tc", "dp4a"):
-                raise ValueError(f"expert_kernel must be auto, tc or dp4a, not {expert_kernel!r}")
+            if expert_kernel not in ("auto", "tc", "ps", "dp4a"):
+                raise ValueError(f"expert_kernel must be auto, tc, ps or dp4a, not {expert_kernel!r}")
             os.environ["HALE_EXPERT_KERNEL"] = expert_kernel
         try:
             _check(lib().hale_ctx_create(device, C.byref(h)))

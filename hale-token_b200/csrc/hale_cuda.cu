@@ -19,6 +19,7 @@
 #include "../../include/hale_cuda.h"
 #include "hale_kernels.cuh"
 #include "hale_tc.cuh"
+#include "hale_stream.cuh"
 
 using namespace hale;
 
@@ -33,8 +34,10 @@ thread_local hale_status g_thread_status = HALE_OK;
 struct hale_ctx {
     int device = 0;
     int sm_count = 0;
-    // expert kernel family: 0 = by batch shape, 1 = tensor cores wherever the
-    // shapes allow, 2 = dp4a only (environment HALE_EXPERT_KERNEL=auto|tc|dp4a)
+    // expert kernel family (environment HALE_EXPERT_KERNEL): 0 "auto" = by
+    // batch shape, 1 "tc" = tcgen05 kernels, 2 "dp4a" = per-CTA kernels
+    // (dp4a / warp MMA), 3 "ps" = persistent streaming warp-MMA kernels;
+    // each where the shapes allow, else the per-CTA kernels
     int expert_kernel = 0;
     std::string msg;
     hale_status status = HALE_OK;
@@ -238,6 +241,7 @@ extern "C" hale_status hale_ctx_create(int device, hale_ctx** out) {
     if (const char* ek = std::getenv("HALE_EXPERT_KERNEL")) {
         if (!std::strcmp(ek, "tc")) c->expert_kernel = 1;
         else if (!std::strcmp(ek, "dp4a")) c->expert_kernel = 2;
+        else if (!std::strcmp(ek, "ps")) c->expert_kernel = 3;
     }
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&c->d_err, 4) != cudaSuccess ||
         cudaMemset(c->d_err, 0, 4) != cudaSuccess) {
@@ -821,7 +825,7 @@ extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, u
 // and HALE_EXPERT_KERNEL=tc selects them.
 static constexpr uint32_t kTcMinTokens = 1u << 30;
 static bool use_tc(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
-    if (ctx->expert_kernel == 2 || I % 64 != 0 || H % 128 != 0) return false;
+    if (ctx->expert_kernel == 2 || ctx->expert_kernel == 3 || I % 64 != 0 || H % 128 != 0) return false;
     if (ctx->expert_kernel == 0 && M < kTcMinTokens) return false;
     return tc_plan_ok(dt == HALE_Q4_0 ? tc_plan(QFmt<0>::BB, TcStage<0>::SB) : tc_plan(QFmt<1>::BB, TcStage<1>::SB));
 }
@@ -847,6 +851,36 @@ static hale_status expert_go_tc(hale_ctx* ctx, const ExpertArgs& a, unsigned max
         expert_down_tc_kernel<QT, PW><<<g2, kTcThreads, P.total, st>>>(a);
     }
     return check_launch(ctx, "expert_down_tc");
+}
+
+// Persistent streaming kernels (hale_stream.cuh): one CTA per SM.
+static constexpr int kPsBudget = 219 * 1024;
+static bool use_ps(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
+    if (ctx->expert_kernel != 3 || I % 64 != 0 || H % 128 != 0) return false;
+    const int bb = block_bytes(dt), sb = dt == HALE_Q4_0 ? PsStage<0>::SB : PsStage<1>::SB;
+    return ps_plan_ok(ps_plan(bb, sb, H, kPsBudget), kPsBudget) && ps_plan_ok(ps_plan(bb, sb, I, kPsBudget), kPsBudget);
+}
+
+template <int QT>
+static hale_status expert_go_ps(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
+    const int TI = a.I / 32, TH = a.H / 32;
+    const PsPlan P1 = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.H, kPsBudget);
+    const PsPlan P2 = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.I, kPsBudget);
+    CUDA_TRY(ctx, allow_smem(expert_gate_up_ps_kernel<QT>, (size_t)P1.total));
+    CUDA_TRY(ctx, allow_smem(expert_down_ps_kernel<QT>, (size_t)P2.total));
+    const unsigned sms = (unsigned)ctx->sm_count;
+    unsigned g1 = std::min(max_active * (unsigned)(TI / 2), sms), g2 = std::min(max_active * (unsigned)(TH / 4), sms);
+    {
+        ProfScope ps_(ctx, "expert_gate_up", st);
+        expert_gate_up_ps_kernel<QT><<<g1, kPsThreads, P1.total, st>>>(a, kPsBudget);
+    }
+    hale_status r = check_launch(ctx, "expert_gate_up_ps");
+    if (r) return r;
+    {
+        ProfScope ps_(ctx, "expert_down", st);
+        expert_down_ps_kernel<QT><<<g2, kPsThreads, P2.total, st>>>(a, kPsBudget);
+    }
+    return check_launch(ctx, "expert_down_ps");
 }
 
 template <int QT, int RT>
@@ -925,6 +959,8 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
             return wide ? expert_go_tc<0, 16>(ctx, a, max_active, st) : expert_go_tc<0, 8>(ctx, a, max_active, st);
         return wide ? expert_go_tc<1, 16>(ctx, a, max_active, st) : expert_go_tc<1, 8>(ctx, a, max_active, st);
     }
+    if (use_ps(ctx, p->dtype, M, H, I))
+        return p->dtype == HALE_Q4_0 ? expert_go_ps<0>(ctx, a, max_active, st) : expert_go_ps<1>(ctx, a, max_active, st);
     // small batches: one row tile per CTA pair of warps, for more CTAs
     bool small = M <= 2;
     if (p->dtype == HALE_Q4_0)

@@ -202,7 +202,7 @@ __device__ __forceinline__ void ring_init(Ring& rg, uint8_t* buf, uint64_t* bars
 
 // Activation rows of one pass, in shared memory: quants [kPassRows][stride]
 // with stride = cols + 16 (the pad puts the 8 rows an MMA B fragment reads
-// in distinct banks), and aux [kPassRows][nbp].
+// in distinct banks), and aux [kPassRows][xaux_stride(nbp)].
 struct XStage {
     int8_t* q;
     int2* a;
@@ -211,6 +211,14 @@ struct XStage {
 };
 
 __host__ __device__ inline int xstage_stride(int cols) { return cols + 16; }
+
+// Row stride (int2 units) of the staged aux rows: nbp padded so that
+// stride / 2 is odd, which puts the four token pairs (2t, 2t+1) an MMA lane
+// group reads in distinct banks.
+__host__ __device__ inline int xaux_stride(int nbp) {
+    const int s = nbp + 2;
+    return (s % 4 == 0) ? s + 2 : s;
+}
 
 __device__ __forceinline__ void xstage_init(XStage& xs, int8_t* q, int2* a, uint64_t* bar) {
     xs.q = q;
@@ -236,17 +244,11 @@ __device__ bool xstage_load(XStage& xs, const int8_t* __restrict__ gq, const int
         const int stride = xstage_stride(cols);
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(xs.bar, (uint32_t)n * (uint32_t)(cols + nbp * 8));
-        if (contiguous) {
-            int r = row_of(base);
-            for (int j = 0; j < n; j++)
-                bulk_g2s(xs.q + (size_t)j * stride, gq + (size_t)(r + j) * cols, (uint32_t)cols, xs.bar);
-            bulk_g2s(xs.a, ga + (size_t)r * nbp, (uint32_t)(n * nbp * 8), xs.bar);
-        } else {
-            for (int j = 0; j < n; j++) {
-                int r = row_of(base + j);
-                bulk_g2s(xs.q + (size_t)j * stride, gq + (size_t)r * cols, (uint32_t)cols, xs.bar);
-                bulk_g2s(xs.a + (size_t)j * nbp, ga + (size_t)r * nbp, (uint32_t)(nbp * 8), xs.bar);
-            }
+        const int astride = xaux_stride(nbp);
+        for (int j = 0; j < n; j++) {
+            const int r = contiguous ? row_of(base) + j : row_of(base + j);
+            bulk_g2s(xs.q + (size_t)j * stride, gq + (size_t)r * cols, (uint32_t)cols, xs.bar);
+            bulk_g2s(xs.a + (size_t)j * astride, ga + (size_t)r * nbp, (uint32_t)(nbp * 8), xs.bar);
         }
     }
     bool ok = mbar_wait(xs.bar, xs.phase, err);
@@ -310,7 +312,7 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
                 const int8_t* xp = xs.q + j * xstage_stride(cols) + b * kQK;
                 uint4 xa = *reinterpret_cast<const uint4*>(xp);
                 uint4 xb = *reinterpret_cast<const uint4*>(xp + 16);
-                int2 ax = xs.a[j * nbp + b];
+                int2 ax = xs.a[j * xaux_stride(nbp) + b];
                 // two independent dp4a chains (integer sums are exact in any order)
                 int s0 = (QT == 0) ? ax.y : 0, s1 = 0;
                 s0 = __dp4a(w[0], (int)xa.x, s0);
@@ -343,13 +345,29 @@ __device__ bool tile_dot(Ring& rg, const uint8_t* __restrict__ gtile, int nb, co
 constexpr int kMagicI = 0x4B400000;
 constexpr float kMagicF = 12582912.0f;
 
-// D = A(16x32 s8, row) x B(32x8 s8, col) + C (s32), warp-wide.
+// D = A(16x32 s8, row) x B(32x8 s8, col) + C (s32), warp-wide. A pure
+// function of its operands (not volatile), so the compiler may overlap the
+// MMAs and loads of consecutive blocks.
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0,
                                              int c1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+}
+
+// ldmatrix: lane L supplies the shared-memory address of row L % 8 of matrix
+// L / 8 (16 contiguous bytes); lane 4 g + t receives, from each matrix, the
+// 4 bytes 4t .. 4t+3 of its row g -- the m16n8k32 fragment layout.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(row_addr)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(smem_addr(row_addr)));
 }
 
 // The same dot products as tile_dot for a pass of up to kPassRows tokens, on
@@ -373,9 +391,12 @@ __device__ bool tile_dot_mma(Ring& rg, const uint8_t* __restrict__ gtile, int nb
         fence_proxy_async_smem();  // earlier passes read these slots
         for (int st = 0; st < min(rg.S, nst); st++) ring_issue<QT>(rg, gtile, nb, st);
     }
-    const int8_t* xrow = xs.q + g * xstage_stride(cols) + 4 * t;  // token g's row (B column g)
-    const int2* a0row = xs.a + (2 * t) * nbp;
-    const int2* a1row = xs.a + (2 * t + 1) * nbp;
+    // ldmatrix row addresses: B -- token (lane & 7), K half (lane >> 3) & 1;
+    // A -- row `lane` of the tile (q4_0: its 16 nibble bytes; q8_0: first or
+    // second 16 bytes of rows (lane & 15) + 16 * mt, half lane >> 4)
+    const int8_t* xrow = xs.q + (lane & 7) * xstage_stride(cols) + ((lane >> 3) & 1) * 16;
+    const int2* a0row = xs.a + (2 * t) * xaux_stride(nbp);
+    const int2* a1row = xs.a + (2 * t + 1) * xaux_stride(nbp);
     bool ok = true;
     for (int st = 0; st < nst; st++) {
         int slot = st % rg.S;
@@ -392,28 +413,29 @@ __device__ bool tile_dot_mma(Ring& rg, const uint8_t* __restrict__ gtile, int nb
         for (int bi = 0; bi < nblk; bi++) {
             const int b = st * kStageBlocks + bi;
             const uint8_t* rec = sbuf + bi * REC;
-            const uint32_t bf0 = *reinterpret_cast<const uint32_t*>(xrow + b * kQK);
-            const uint32_t bf1 = *reinterpret_cast<const uint32_t*>(xrow + b * kQK + 16);
+            uint32_t bf[2];
+            ldsm_x2(bf, xrow + b * kQK);
+            const uint32_t bf0 = bf[0], bf1 = bf[1];
             const int2 x0 = a0row[b], x1 = a1row[b];
             const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
             const float xs0 = __int_as_float(x0.x), xs1 = __int_as_float(x1.x);
+            // words t of rows g, g+8, g+16, g+24 (q4_0) -- byte j of a row holds
+            // element j (low nibble) and j + 16 (high)
+            uint32_t w4[4];
+            if (QT == 0) ldsm_x4(w4, rec + lane * QB);
 #pragma unroll
             for (int mt = 0; mt < 2; mt++) {
                 const int r0 = mt * 16 + g, r1 = r0 + 8;
                 uint32_t a[4];
                 if (QT == 0) {
-                    // byte j of a row holds element j (low nibble) and j + 16 (high)
-                    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 4 * t);
-                    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 4 * t);
-                    a[0] = w0 & 0x0F0F0F0Fu;
-                    a[1] = w1 & 0x0F0F0F0Fu;
-                    a[2] = (w0 >> 4) & 0x0F0F0F0Fu;
-                    a[3] = (w1 >> 4) & 0x0F0F0F0Fu;
+                    a[0] = w4[2 * mt] & 0x0F0F0F0Fu;
+                    a[1] = w4[2 * mt + 1] & 0x0F0F0F0Fu;
+                    a[2] = (w4[2 * mt] >> 4) & 0x0F0F0F0Fu;
+                    a[3] = (w4[2 * mt + 1] >> 4) & 0x0F0F0F0Fu;
                 } else {
-                    a[0] = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 4 * t);
-                    a[1] = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 4 * t);
-                    a[2] = *reinterpret_cast<const uint32_t*>(rec + r0 * QB + 16 + 4 * t);
-                    a[3] = *reinterpret_cast<const uint32_t*>(rec + r1 * QB + 16 + 4 * t);
+                    // matrices (rows 0-7, K 0-15), (rows 8-15, K 0-15), (rows 0-7,
+                    // K 16-31), (rows 8-15, K 16-31) of this half: a0 .. a3
+                    ldsm_x4(a, rec + (mt * 16 + (lane & 15)) * QB + (lane >> 4) * 16);
                 }
                 int d[4];
                 mma_s8_16832(d, a, bf0, bf1, c0, c1);
@@ -503,7 +525,7 @@ __host__ __device__ inline SmemPlan smem_plan(int BB, int S, int warps, int cols
     p.xq_off = warps * p.ring_bytes;
     int nbp = aux_stride(cols / kQK);
     p.xa_off = p.xq_off + kPassRows * xstage_stride(cols);
-    p.bars_off = p.xa_off + kPassRows * nbp * 8;
+    p.bars_off = p.xa_off + kPassRows * xaux_stride(nbp) * 8;
     p.total = p.bars_off + (warps * S + 1) * 8;
     return p;
 }

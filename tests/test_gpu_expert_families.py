@@ -1,10 +1,11 @@
-"""GPU parity of the tensor-core (tcgen05 kind::i8) expert kernels.
+"""GPU parity of the expert-kernel families.
 
-Contexts here force a kernel family: "tc" runs the tensor-core kernels at
-every batch size the shapes allow, "dp4a" the CUDA-core kernels. Both must
-equal the oracle (MoeLayer::forward, src/moe.rs:56-70, with dot_q4_0 /
-dot_q8_0 of src/tensor/quant.rs:115-144) bit for bit, and each other on whole
-batches too large for the oracle to check every token.
+Contexts here force a family at every batch size the shapes allow: "tc" the
+tcgen05 kind::i8 kernels, "ps" the persistent streaming warp-MMA kernels,
+"dp4a" the per-CTA kernels. Each must equal the oracle (MoeLayer::forward,
+src/moe.rs:56-70, with dot_q4_0 / dot_q8_0 of src/tensor/quant.rs:115-144)
+bit for bit, and the per-CTA kernels on whole batches too large for the
+oracle to check every token.
 """
 import importlib
 
@@ -20,14 +21,16 @@ hale = importlib.import_module("hale-token_b200")
 fmt = importlib.import_module("hale-token_b200.formats")
 
 
+FAMILIES = ["tc", "ps"]
+
+
 @pytest.fixture(scope="module")
 def ctxs():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    tc = hale.Context(0, expert_kernel="tc")
-    dp = hale.Context(0, expert_kernel="dp4a")
-    yield tc, dp
-    for c in (tc, dp):
+    cs = {name: hale.Context(0, expert_kernel=name) for name in FAMILIES + ["dp4a"]}
+    yield cs
+    for c in cs.values():
         c.check()
         c.close()
 
@@ -68,12 +71,13 @@ def forward(ctx, pool, ld, x, k):
     return out.cpu().numpy(), idx.cpu().numpy(), renc
 
 
+@pytest.mark.parametrize("family", FAMILIES)
 @pytest.mark.parametrize("dtype", [fmt.Q4_0, fmt.Q8_0])
 @pytest.mark.parametrize("m", [1, 3, 16, 40, 64, 100])
-def test_tc_tiny_layer_matches_oracle(ctxs, dtype, m):
-    """16 experts top-4, H=256, I=128: one to several passes per expert, both
-    pass widths (8 tokens below M*k = 16*E, 16 from there)."""
-    tc, _ = ctxs
+def test_tiny_layer_matches_oracle(ctxs, family, dtype, m):
+    """16 experts top-4, H=256, I=128: one to several passes per expert (for
+    tc both pass widths: 8 tokens below M*k = 16*E, 16 from there)."""
+    tc = ctxs[family]
     ld = fmt.SyntheticLayer(300 + m, 16, 256, 128, dtype)
     pool = make_pool(tc, ld)
     x = ld.tokens(m)
@@ -83,11 +87,12 @@ def test_tc_tiny_layer_matches_oracle(ctxs, dtype, m):
     assert_bit_equal(out, want, "layer output")
 
 
+@pytest.mark.parametrize("family", FAMILIES)
 @pytest.mark.parametrize("m", [8, 64, 512])
-def test_tc_qwen3_shape_matches_oracle_and_dp4a(ctxs, m):
+def test_qwen3_shape_matches_oracle_and_dp4a(ctxs, family, m):
     """H=2048, 128 experts top-8, I=768, q4_0: sampled tokens against the
-    oracle, the whole batch against the dp4a kernels."""
-    tc, dp = ctxs
+    oracle, the whole batch against the per-CTA kernels."""
+    tc, dp = ctxs[family], ctxs["dp4a"]
     ld = fmt.SyntheticLayer(11, 128, 2048, 768, fmt.Q4_0)
     x = ld.tokens(m)
     out_tc, idx, renc = forward(tc, make_pool(tc, ld), ld, x, 8)
@@ -99,10 +104,11 @@ def test_tc_qwen3_shape_matches_oracle_and_dp4a(ctxs, m):
     assert_bit_equal(out_tc[toks], want, "sampled tokens")
 
 
-def test_tc_q8_wide_hidden_with_shallow_ring(ctxs):
-    """q8_0, H=4096 (Mixtral hidden size): the activation operand takes most of
-    shared memory, leaving the weight ring its minimum depth."""
-    tc, dp = ctxs
+@pytest.mark.parametrize("family", FAMILIES)
+def test_q8_wide_hidden_with_shallow_ring(ctxs, family):
+    """q8_0, H=4096 (Mixtral hidden size): the activation stage takes much of
+    shared memory, leaving the weight ring a shallow depth."""
+    tc, dp = ctxs[family], ctxs["dp4a"]
     ld = fmt.SyntheticLayer(23, 8, 4096, 1024, fmt.Q8_0)
     x = ld.tokens(24)
     out_tc, idx, renc = forward(tc, make_pool(tc, ld), ld, x, 2)
@@ -112,10 +118,11 @@ def test_tc_q8_wide_hidden_with_shallow_ring(ctxs):
     assert_bit_equal(out_tc[:4], want, "first tokens")
 
 
-def test_tc_repeated_calls_are_deterministic(ctxs):
+@pytest.mark.parametrize("family", FAMILIES)
+def test_repeated_calls_are_deterministic(ctxs, family):
     """The persistent kernels reset their combine counters: two calls in a row
     give identical bits."""
-    tc, _ = ctxs
+    tc = ctxs[family]
     ld = fmt.SyntheticLayer(5, 32, 512, 256, fmt.Q4_0)
     pool = make_pool(tc, ld)
     x = ld.tokens(200)
