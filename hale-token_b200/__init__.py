@@ -86,6 +86,10 @@ SIGNATURES = {
     "hale_moe_forward_host": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_route": (I32, [P, C.POINTER(MoeLayer), U32, P, U32, P, P, P, P]),
     "hale_moe_route_noalloc": (I32, [P, C.c_int, U32, U32, I32, U32, P, U32, P, P, P, P]),
+    "hale_q8_aux_pairs": (I32, [U32]),
+    "hale_ep_dispatch": (I32, [P, P, U32, P, U32, U32, P, P, P, C.POINTER(U64), P, P, P]),
+    "hale_ep_experts": (I32, [P, P, U32, U32, P, P, P, U32, P, P]),
+    "hale_ep_combine": (I32, [P, P, P, U32, U32, U32, P, P]),
     "hale_lm_head": (I32, [P, P, P, U32, P, P]),
     "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
     "hale_expf_host": (None, [P, P, U64]),
@@ -312,6 +316,33 @@ def moe_route_noalloc(router, router_dtype, n_experts, top_k, normalize, hidden,
     _check(lib().hale_moe_route_noalloc(ptr(router), router_dtype, n_experts, top_k, int(normalize),
                                         hidden, ptr(x), x.shape[0], ptr(topk_idx), ptr(topk_w),
                                         ptr(probs), _stream(stream)))
+
+
+def q8_aux_pairs(cols):
+    """int2 entries per Q8Activations aux row: (cols / 32) rounded up to even."""
+    return lib().hale_q8_aux_pairs(cols)
+
+
+def ep_dispatch(ctx, layer, hidden, x, n_ranks, send_q, send_aux, send_meta, topk_idx=None, topk_w=None,
+                stream=None):
+    """hale_ep_dispatch: route x [M, hidden], pack one record per route in
+    owner-rank order. Returns the record count per owner rank (list)."""
+    counts = (U64 * n_ranks)()
+    ctx.call("hale_ep_dispatch", ctx.h, C.byref(layer), hidden, ptr(x), x.shape[0], n_ranks, ptr(send_q),
+             ptr(send_aux), ptr(send_meta), counts, ptr(topk_idx), ptr(topk_w), _stream(stream))
+    return [int(c) for c in counts]
+
+
+def ep_experts(ctx, pool, layer, expert0, recv_q, recv_aux, recv_meta, y, stream=None):
+    """hale_ep_experts: y[j] = Expert(record j) for the received records."""
+    ctx.call("hale_ep_experts", ctx.h, pool.h, layer, expert0, ptr(recv_q), ptr(recv_aux), ptr(recv_meta),
+             recv_meta.shape[0], ptr(y), _stream(stream))
+
+
+def ep_combine(ctx, send_meta, y_back, m_tokens, top_k, hidden, out, stream=None):
+    """hale_ep_combine: out[t] = best-first weighted sum of the token's y rows."""
+    ctx.call("hale_ep_combine", ctx.h, ptr(send_meta), ptr(y_back), m_tokens, top_k, hidden, ptr(out),
+             _stream(stream))
 
 
 def quantize_q8(ctx, x, scales, quants, stream=None):

@@ -20,6 +20,7 @@
 #include "hale_kernels.cuh"
 #include "hale_tc.cuh"
 #include "hale_stream.cuh"
+#include "hale_ep.cuh"
 
 using namespace hale;
 
@@ -904,6 +905,9 @@ static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_ac
     return check_launch(ctx, "expert_down");
 }
 
+static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, uint32_t M, int k, int E,
+                                  cudaStream_t st);
+
 extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
                                         uint32_t M, float* out, int32_t* topk_idx, float* topk_w, void* stream) {
     if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL ctx or pool");
@@ -947,23 +951,31 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
     a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
     a.out = out;
-    // ring depth, capped at the stages one tile has
-    a.S1 = std::min(ring_stages(p->dtype, M), (H / 32 + kStageBlocks - 1) / kStageBlocks);
-    a.S2 = std::min(ring_stages(p->dtype, M), (I / 32 + kStageBlocks - 1) / kStageBlocks);
     a.err = ctx->d_err;
+    return launch_experts(ctx, p->dtype, a, M, k, E, st);
+}
+
+// The expert kernels over the routes in a (expert lists built, activations
+// quantized): the family by context setting and batch shape.
+static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, uint32_t M, int k, int E,
+                                  cudaStream_t st) {
+    const int H = a.H, I = a.I;
+    // ring depth, capped at the stages one tile has
+    a.S1 = std::min(ring_stages(dt, M), (H / 32 + kStageBlocks - 1) / kStageBlocks);
+    a.S2 = std::min(ring_stages(dt, M), (I / 32 + kStageBlocks - 1) / kStageBlocks);
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
-    if (use_tc(ctx, p->dtype, M, H, I)) {
+    if (use_tc(ctx, dt, M, H, I)) {
         // 16-token passes once experts average ~16 tokens; 8-token passes below
         const bool wide = (long long)M * k >= 16LL * E;
-        if (p->dtype == HALE_Q4_0)
+        if (dt == HALE_Q4_0)
             return wide ? expert_go_tc<0, 16>(ctx, a, max_active, st) : expert_go_tc<0, 8>(ctx, a, max_active, st);
         return wide ? expert_go_tc<1, 16>(ctx, a, max_active, st) : expert_go_tc<1, 8>(ctx, a, max_active, st);
     }
-    if (use_ps(ctx, p->dtype, M, H, I))
-        return p->dtype == HALE_Q4_0 ? expert_go_ps<0>(ctx, a, max_active, st) : expert_go_ps<1>(ctx, a, max_active, st);
+    if (use_ps(ctx, dt, M, H, I))
+        return dt == HALE_Q4_0 ? expert_go_ps<0>(ctx, a, max_active, st) : expert_go_ps<1>(ctx, a, max_active, st);
     // small batches: one row tile per CTA pair of warps, for more CTAs
     bool small = M <= 2;
-    if (p->dtype == HALE_Q4_0)
+    if (dt == HALE_Q4_0)
         return small ? expert_go<0, 1>(ctx, a, max_active, st) : expert_go<0, 2>(ctx, a, max_active, st);
     return small ? expert_go<1, 1>(ctx, a, max_active, st) : expert_go<1, 2>(ctx, a, max_active, st);
 }
@@ -998,6 +1010,142 @@ extern "C" hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* p, const 
 // ---------------------------------------------------------------------------
 // sampling tail
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Expert parallelism (hale_ep.cuh): the device work on either side of the
+// two all-to-all-v exchanges the host performs.
+// ---------------------------------------------------------------------------
+extern "C" int32_t hale_q8_aux_pairs(uint32_t cols) { return aux_stride((int)(cols / 32)); }
+
+extern "C" hale_status hale_ep_dispatch(hale_ctx* ctx, const hale_moe_layer* ly, uint32_t hidden, const float* x,
+                                        uint32_t M, uint32_t n_ranks, int8_t* send_q, int32_t* send_aux,
+                                        int32_t* send_meta, uint64_t* counts_host, int32_t* topk_idx, float* topk_w,
+                                        void* stream) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ep_dispatch: ctx is NULL");
+    hale_status r = check_layer(ctx, ly, hidden);
+    if (r) return r;
+    if (hidden % 32 != 0) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hidden (%u) must be a multiple of 32", hidden);
+    if (n_ranks == 0 || ly->n_experts % n_ranks != 0)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "%u experts do not split evenly over %u ranks", ly->n_experts,
+                    n_ranks);
+    if (!counts_host) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_dispatch: counts is NULL");
+    if (M == 0) {
+        for (uint32_t i = 0; i < n_ranks; i++) counts_host[i] = 0;
+        return HALE_OK;
+    }
+    if (!x || !send_q || !send_aux || !send_meta)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_dispatch: NULL buffer");
+    if (!aligned16(x) || !aligned16(send_q) || !aligned16(send_aux) || !aligned16(send_meta))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_dispatch: buffers must be 16-byte aligned");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int E = (int)ly->n_experts, k = (int)ly->top_k, H = (int)hidden;
+    MoeLayout L;
+    if ((r = ensure_moe_ws(ctx, (int)M, E, k, H, ctx->capI > 0 ? ctx->capI : 32, stream, &L))) return r;
+    if ((r = ensure_scratch(ctx, (size_t)n_ranks * 8, stream))) return r;
+    cudaStream_t st = S(stream);
+    if ((r = launch_router(ctx, ly, hidden, x, M, L, true, topk_idx, topk_w, nullptr, nullptr, st))) return r;
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    const int n = (int)M * k, nbp = aux_stride(H / 32);
+    {
+        ProfScope ps_(ctx, "ep_pack", st);
+        ep_pack_kernel<<<(n + 7) / 8, 256, 0, st>>>(
+            reinterpret_cast<const int*>(ws + L.elist), reinterpret_cast<const int*>(ws + L.topk_idx),
+            reinterpret_cast<const float*>(ws + L.topk_w), reinterpret_cast<const int8_t*>(ws + L.xq),
+            reinterpret_cast<const int2*>(ws + L.xaux), n, k, H, nbp, send_q, reinterpret_cast<int2*>(send_aux),
+            reinterpret_cast<EpMeta*>(send_meta));
+    }
+    if ((r = check_launch(ctx, "ep_pack"))) return r;
+    auto* d_counts = static_cast<unsigned long long*>(ctx->scratch);
+    ep_rank_counts_kernel<<<1, 256, 0, st>>>(reinterpret_cast<const int*>(ws + L.elist_off), (int)n_ranks,
+                                             E / (int)n_ranks, d_counts);
+    if ((r = check_launch(ctx, "ep_rank_counts"))) return r;
+    CUDA_TRY(ctx, cudaMemcpyAsync(counts_host, d_counts, (size_t)n_ranks * 8, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(ctx, cudaStreamSynchronize(st));
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* p, uint32_t layer, uint32_t expert0,
+                                       const int8_t* recv_q, const int32_t* recv_aux, const int32_t* recv_meta,
+                                       uint32_t n, float* y, void* stream) {
+    if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_experts: NULL ctx or pool");
+    if (p->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "pool belongs to another context");
+    if (layer >= p->L) return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u has no experts in the pool", layer);
+    if (p->layer_resident[layer] != p->E)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: only %u of %u experts are resident", layer,
+                    p->layer_resident[layer], p->E);
+    if (n == 0) return HALE_OK;
+    if (!recv_q || !recv_aux || !recv_meta || !y)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_experts: NULL buffer");
+    if (!aligned16(recv_q) || !aligned16(recv_aux) || !aligned16(recv_meta))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_experts: buffers must be 16-byte aligned");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int El = (int)p->E, H = (int)p->H, I = (int)p->I;
+    MoeLayout L;
+    hale_status r;
+    if ((r = ensure_moe_ws(ctx, (int)n, El, 1, H, I, stream, &L))) return r;
+    cudaStream_t st = S(stream);
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    const EpMeta* meta = reinterpret_cast<const EpMeta*>(recv_meta);
+    int* cursor = reinterpret_cast<int*>(ws + L.logits);  // [El], free on this side
+    ep_count_kernel<<<1, 1024, (size_t)El * 4, st>>>(meta, (int)n, (int)expert0, El,
+                                                      reinterpret_cast<int*>(ws + L.elist_off), cursor,
+                                                      reinterpret_cast<int*>(ws + L.active),
+                                                      reinterpret_cast<int*>(ws + L.n_active), ctx->d_err);
+    if ((r = check_launch(ctx, "ep_count"))) return r;
+    ep_scatter_kernel<<<(n + 255) / 256, 256, 0, st>>>(meta, (int)n, (int)expert0, El,
+                                                        reinterpret_cast<const int*>(ws + L.elist_off), cursor,
+                                                        reinterpret_cast<int*>(ws + L.elist),
+                                                        reinterpret_cast<float*>(ws + L.topk_w));
+    if ((r = check_launch(ctx, "ep_scatter"))) return r;
+    // every record is one token with one route of weight 1: the combine of
+    // the expert kernels then writes y itself (0 + 1 * y == y)
+    ExpertArgs a{};
+    a.experts = p->data + (size_t)layer * p->E * p->expert_stride;
+    a.expert_stride = p->expert_stride;
+    a.H = H;
+    a.I = I;
+    a.k = 1;
+    a.M = (int)n;
+    a.elist_off = reinterpret_cast<int*>(ws + L.elist_off);
+    a.elist = reinterpret_cast<int*>(ws + L.elist);
+    a.active = reinterpret_cast<int*>(ws + L.active);
+    a.n_active = reinterpret_cast<int*>(ws + L.n_active);
+    a.xq = recv_q;
+    a.xaux = reinterpret_cast<const int2*>(recv_aux);
+    a.hq = reinterpret_cast<int8_t*>(ws + L.hq);
+    a.haux = reinterpret_cast<int2*>(ws + L.haux);
+    a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+    a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
+    a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+    a.out = y;
+    a.err = ctx->d_err;
+    return launch_experts(ctx, p->dtype, a, n, 1, El, st);
+}
+
+extern "C" hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, const float* y_back, uint32_t M,
+                                       uint32_t top_k, uint32_t hidden, float* out, void* stream) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ep_combine: ctx is NULL");
+    if (M == 0) return HALE_OK;
+    if (!send_meta || !y_back || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_combine: NULL buffer");
+    if (top_k == 0 || top_k > 32 || hidden == 0)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_combine: top_k %u / hidden %u out of range", top_k, hidden);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_status r;
+    const size_t n = (size_t)M * top_k;
+    if ((r = ensure_scratch(ctx, n * 4, stream))) return r;
+    cudaStream_t st = S(stream);
+    int* pos = static_cast<int*>(ctx->scratch);
+    CUDA_TRY(ctx, cudaMemsetAsync(pos, 0xFF, n * 4, st));
+    const EpMeta* meta = reinterpret_cast<const EpMeta*>(send_meta);
+    ep_pos_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(meta, (int)n, (int)M, (int)top_k, pos, ctx->d_err);
+    if ((r = check_launch(ctx, "ep_pos"))) return r;
+    {
+        ProfScope ps_(ctx, "ep_combine", st);
+        ep_combine_kernel<<<dim3((hidden + 255) / 256, M), 256, 0, st>>>(meta, pos, y_back, (int)n, (int)M,
+                                                                          (int)top_k, (int)hidden, out, ctx->d_err);
+    }
+    return check_launch(ctx, "ep_combine");
+}
+
 extern "C" hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, const float* hidden, uint32_t batch,
                                     float* logits, void* stream) {
     if (!ctx || !lm_head) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_lm_head: NULL argument");

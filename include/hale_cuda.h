@@ -244,6 +244,53 @@ HALE_API hale_status hale_moe_route_noalloc(const void* router, hale_dtype route
                                             const float* x, uint32_t m_tokens, int32_t* topk_idx,
                                             float* topk_w, float* probs, void* stream);
 
+/* ---- expert parallelism ----------------------------------------------------
+ * MoeLayer::forward (moe.rs:56-70) over n_ranks ranks, each owning a
+ * contiguous block of n_experts / n_ranks experts per layer (rank r owns
+ * [r * E/R, (r+1) * E/R)). The reference runs on one host and has no such
+ * split; these three calls are the device work around the two all-to-all-v
+ * exchanges the host performs with its own communicator:
+ *   1. hale_ep_dispatch (home): route m_tokens tokens, quantize each once,
+ *      pack one record per route, grouped by owner rank;
+ *   2. send the records; hale_ep_experts (owner) on what arrived; send the
+ *      y rows back in the order they came;
+ *   3. hale_ep_combine (home): best-first weighted sum per token.
+ * The result is bit-identical to hale_moe_forward on one GPU. Records:
+ *   q    [n, hidden] int8      -- Q8Activations quants of the home token
+ *   aux  [n, 2 * hale_q8_aux_pairs(hidden)] int32 -- per block: f32 scale bits,
+ *                                -8 * sum of the block's quants
+ *   meta [n, 4] int32          -- home token, route slot (0 = best), global
+ *                                expert, routing weight (f32 bits)
+ * Device buffers must be 16-byte aligned. */
+
+/* Pairs of int32 per aux row: (cols / 32) rounded up to even. */
+HALE_API int32_t hale_q8_aux_pairs(uint32_t cols);
+
+/* Home side. Records for all m_tokens * top_k routes in send order (owner
+ * rank ascending, then expert ascending); counts_host[r] = records for rank
+ * r (host memory; the call synchronizes the stream). topk_idx / topk_w
+ * (nullable): as hale_moe_forward. */
+HALE_API hale_status hale_ep_dispatch(hale_ctx* ctx, const hale_moe_layer* layer, uint32_t hidden,
+                                      const float* x, uint32_t m_tokens, uint32_t n_ranks, int8_t* send_q,
+                                      int32_t* send_aux, int32_t* send_meta, uint64_t* counts_host,
+                                      int32_t* topk_idx, float* topk_w, void* stream);
+
+/* Owner side: y[j, :] = Expert(record j) for the n received records (any
+ * source order), with this rank's experts in `pool` as local ids
+ * 0 .. pool experts - 1 = global ids expert0 .. ; a record naming another
+ * expert raises HALE_E_DEVICE_CHECK at the next hale_ctx_check. */
+HALE_API hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* pool, uint32_t layer, uint32_t expert0,
+                                     const int8_t* recv_q, const int32_t* recv_aux, const int32_t* recv_meta,
+                                     uint32_t n, float* y, void* stream);
+
+/* Home side: out[t, :] = sum over s = 0 .. top_k-1 of w * y_back[record of
+ * (t, s)], starting from 0 (moe.rs:63-68). send_meta: as packed by
+ * hale_ep_dispatch; y_back [m_tokens * top_k, hidden]: y of each record in
+ * send order. */
+HALE_API hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, const float* y_back,
+                                     uint32_t m_tokens, uint32_t top_k, uint32_t hidden, float* out,
+                                     void* stream);
+
 /* ---- sampling tail -------------------------------------------------------- */
 
 /* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .
