@@ -12,7 +12,9 @@ q4_0 MoE GEMV achieved HBM GB/s").
 
 Multi-GPU (torchrun): each rank runs its own batch against its own copy of
 the layer (per-GPU work fixed -> weak scaling); the step time is the max
-over ranks.
+over ranks. The line also carries "ep": the same layer split over the N
+ranks by expert parallelism (each rank E/N experts and its own M tokens,
+records and y rows exchanged by NCCL all-to-all-v), timed the same way.
 """
 import argparse
 import json
@@ -41,6 +43,7 @@ def parse():
     p.add_argument("--impl", default="hale", choices=["hale", "reference"])
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel measurement at N > 1")
     return p.parse_args()
 
 
@@ -150,6 +153,45 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
+def measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush, barrier, max_over_ranks):
+    """The layer split over `world` ranks by expert parallelism: this rank
+    holds experts [rank*E/world, (rank+1)*E/world) and its own m tokens; a step
+    is one ep.moe_forward_ep (dispatch, NCCL all-to-all-v of the records,
+    local experts, y rows back, combine). Device time per step by CUDA events
+    on the current stream, L2 flushed before each step, max over ranks."""
+    import importlib
+
+    import torch
+    ep = importlib.import_module("hale-token_b200.ep")
+    epr = E // world
+    pool = hale.Pool(ctx, fmt.Q4_0, H, I, 1, epr)
+    for le in range(epr):
+        pool.upload(0, le, fmt.pack_record(*encoded[rank * epr + le]))
+    layer = hale.moe_layer(0, router, fmt.F32, E, K_TOP, True)
+    backend = ep.CudaEpBackend(ctx, pool, layer, H, rank, world)
+    exch = ep.Exchange(device=f"cuda:{torch.cuda.current_device()}")
+    x = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).cuda()
+    for _ in range(max(args.warmup, 3)):
+        ep.moe_forward_ep(backend, exch, x)
+    ctx.check()
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        ep.moe_forward_ep(backend, exch, x)
+        b.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ctx.check()
+    ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+    return {"tok_s": world * m / (ms / 1e3), "ms_per_step": ms, "n_ranks": world, "experts_per_rank": epr,
+            "tokens_per_rank": m, "exchange": "NCCL all-to-all-v via torch.distributed (counts, q8 rows, "
+            "scales, route metadata; y rows back)", "bit_exact_vs_1gpu": "tests/test_gpu_ep*.py"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -177,7 +219,7 @@ def run_reference(args):
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "Rust reference cannot be built here (no cargo); the C restatement of its CPU path stands in",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -346,6 +388,12 @@ def main():
                               "distinct_experts": s_distinct,
                               "layer_hbm_gbs": lb / (s_ms / 1e3) / 1e9}
 
+    # ---- expert parallelism over the N ranks (N > 1) --------------------------
+    ep_line = None
+    if world > 1 and not args.no_ep:
+        ep_line = measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush, barrier,
+                             max_over_ranks)
+
     # ---- CPU baseline (rank 0, N=1 only) --------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -365,11 +413,25 @@ def main():
             "ms_per_step_eager": ms_eager, "timing": "device: CUDA events around CUDA-graph replays of hale_moe_forward",
             "clocks": clk, "sweep": sweep,
         }
-        print(json.dumps(line), flush=True)
+        if ep_line is not None:
+            line["ep"] = ep_line
+        emit(line)
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
 
 
+def emit(line):
+    """The one JSON line, on the process's original stdout."""
+    os.write(_JSON_FD, (json.dumps(line) + "\n").encode())
+
+
+_JSON_FD = 1
+
 if __name__ == "__main__":
+    # stdout carries exactly one JSON line: everything else written to fd 1
+    # (library banners such as NCCL's version line, warnings) goes to stderr
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     main()

@@ -185,7 +185,7 @@ __device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bit) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk async copy (TMA engine, no multicast)
+// mbarrier + bulk async copy (TMA engine, plain per-CTA loads)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
