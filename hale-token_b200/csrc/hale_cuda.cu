@@ -854,32 +854,35 @@ static hale_status expert_go_tc(hale_ctx* ctx, const ExpertArgs& a, unsigned max
     return check_launch(ctx, "expert_down_tc");
 }
 
-// Persistent streaming kernels (hale_stream.cuh): one CTA per SM.
-static constexpr int kPsBudget = 219 * 1024;
+// Persistent streaming kernels (hale_stream.cuh): kPsCtas CTAs per SM, each
+// with its share of shared memory, so one CTA's per-pass epilogue overlaps
+// another's streaming.
+static constexpr int kPsCtas = 2;
+static constexpr int kPsBudget = (kPsCtas == 1 ? 219 : 104) * 1024;
 static bool use_ps(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
     if (ctx->expert_kernel != 3 || I % 64 != 0 || H % 128 != 0) return false;
-    const int bb = block_bytes(dt), sb = dt == HALE_Q4_0 ? PsStage<0>::SB : PsStage<1>::SB;
+    const int bb = block_bytes(dt), sb = ps_stage_blocks(dt == HALE_Q4_0 ? 0 : 1, kPsCtas);
     return ps_plan_ok(ps_plan(bb, sb, H, kPsBudget), kPsBudget) && ps_plan_ok(ps_plan(bb, sb, I, kPsBudget), kPsBudget);
 }
 
 template <int QT>
 static hale_status expert_go_ps(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
-    const int TI = a.I / 32, TH = a.H / 32;
-    const PsPlan P1 = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.H, kPsBudget);
-    const PsPlan P2 = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.I, kPsBudget);
+    const int TI = a.I / 32, TH = a.H / 32, sb = ps_stage_blocks(QT, kPsCtas);
+    const PsPlan P1 = ps_plan(QFmt<QT>::BB, sb, a.H, kPsBudget);
+    const PsPlan P2 = ps_plan(QFmt<QT>::BB, sb, a.I, kPsBudget);
     CUDA_TRY(ctx, allow_smem(expert_gate_up_ps_kernel<QT>, (size_t)P1.total));
     CUDA_TRY(ctx, allow_smem(expert_down_ps_kernel<QT>, (size_t)P2.total));
-    const unsigned sms = (unsigned)ctx->sm_count;
-    unsigned g1 = std::min(max_active * (unsigned)(TI / 2), sms), g2 = std::min(max_active * (unsigned)(TH / 4), sms);
+    const unsigned slots = (unsigned)(ctx->sm_count * kPsCtas);
+    unsigned g1 = std::min(max_active * (unsigned)(TI / 2), slots), g2 = std::min(max_active * (unsigned)(TH / 4), slots);
     {
         ProfScope ps_(ctx, "expert_gate_up", st);
-        expert_gate_up_ps_kernel<QT><<<g1, kPsThreads, P1.total, st>>>(a, kPsBudget);
+        expert_gate_up_ps_kernel<QT><<<g1, kPsThreads, P1.total, st>>>(a, kPsBudget, sb);
     }
     hale_status r = check_launch(ctx, "expert_gate_up_ps");
     if (r) return r;
     {
         ProfScope ps_(ctx, "expert_down", st);
-        expert_down_ps_kernel<QT><<<g2, kPsThreads, P2.total, st>>>(a, kPsBudget);
+        expert_down_ps_kernel<QT><<<g2, kPsThreads, P2.total, st>>>(a, kPsBudget, sb);
     }
     return check_launch(ctx, "expert_down_ps");
 }

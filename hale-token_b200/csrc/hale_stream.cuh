@@ -31,16 +31,9 @@ constexpr int kPsComputeWarps = 8;
 constexpr int kPsThreads = (kPsComputeWarps + 1) * 32;  // + the producer warp
 constexpr int kPsMaxStages = 8;
 
-template <int QT>
-struct PsStage;
-template <>
-struct PsStage<0> {
-    static constexpr int SB = 16;  // 16 x 576 B = 9216 B per tile copy
-};
-template <>
-struct PsStage<1> {
-    static constexpr int SB = 8;  // 8 x 1088 B = 8704 B per tile copy
-};
+// Blocks per tile per ring stage for `ctas` CTAs per SM: ~9 KB copies with
+// one CTA per SM, ~4.5 KB with two (each then has half the shared memory).
+__host__ __device__ inline int ps_stage_blocks(int qt, int ctas) { return (qt == 0 ? 16 : 8) / ctas; }
 
 struct PsPlan {
     int stages, stage_bytes, xstride, xq_bytes, nbp, xa_bytes;
@@ -264,7 +257,7 @@ __device__ void ps_pass(PsCtx& c, int nb, int tile, int half, int& gs, int q, fl
 // matching up rows -- so h = silu(g) * u and its q8 quantization are formed
 // per pass in-CTA, as in expert_gate_up_kernel, and written in slot order.
 template <int QT>
-__global__ void __launch_bounds__(kPsThreads, 1) expert_gate_up_ps_kernel(ExpertArgs a, int budget) {
+__global__ void __launch_bounds__(kPsThreads, 2) expert_gate_up_ps_kernel(ExpertArgs a, int budget, int sb) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_out[4][kPassRows][kTileRows];
     constexpr int REC = kTileRows * QFmt<QT>::BB;
@@ -272,9 +265,9 @@ __global__ void __launch_bounds__(kPsThreads, 1) expert_gate_up_ps_kernel(Expert
     const int upe = TI / 2;
     const int n_units = *a.n_active * upe;
     if ((int)blockIdx.x >= n_units) return;
-    const PsPlan P = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.H, budget);
+    const PsPlan P = ps_plan(QFmt<QT>::BB, sb, a.H, budget);
     PsCtx c;
-    ps_setup(c, smem, P, PsStage<QT>::SB);
+    ps_setup(c, smem, P, sb);
     const size_t tile_bytes = (size_t)nbh * REC;
     auto unit_of = [&](int u) {
         PsUnit U;
@@ -336,7 +329,7 @@ __global__ void __launch_bounds__(kPsThreads, 1) expert_gate_up_ps_kernel(Expert
 // Phase 2: units of 128 rows of the down projection; y for every route, then
 // the best-first combine of expert_down_kernel.
 template <int QT>
-__global__ void __launch_bounds__(kPsThreads, 1) expert_down_ps_kernel(ExpertArgs a, int budget) {
+__global__ void __launch_bounds__(kPsThreads, 2) expert_down_ps_kernel(ExpertArgs a, int budget, int sb) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_last[kPassRows];
     constexpr int REC = kTileRows * QFmt<QT>::BB;
@@ -344,9 +337,9 @@ __global__ void __launch_bounds__(kPsThreads, 1) expert_down_ps_kernel(ExpertArg
     const int upe = TH / 4;
     const int n_units = *a.n_active * upe;
     if ((int)blockIdx.x >= n_units) return;
-    const PsPlan P = ps_plan(QFmt<QT>::BB, PsStage<QT>::SB, a.I, budget);
+    const PsPlan P = ps_plan(QFmt<QT>::BB, sb, a.I, budget);
     PsCtx c;
-    ps_setup(c, smem, P, PsStage<QT>::SB);
+    ps_setup(c, smem, P, sb);
     const size_t gu_tile = (size_t)nbh * REC, d_tile = (size_t)nbi * REC;
     auto unit_of = [&](int u) {
         PsUnit U;
