@@ -61,6 +61,24 @@ class SamplingParams(C.Structure):
                 ("repetition_penalty", C.c_float)]
 
 
+class HostMatrix(C.Structure):
+    _fields_ = [("dtype", I32), ("rows", U32), ("cols", U32), ("data", P)]
+
+
+class DecoderLayer(C.Structure):
+    _fields_ = [("input_norm", P), ("post_norm", P), ("q_norm", P), ("k_norm", P),
+                ("q", HostMatrix), ("k", HostMatrix), ("v", HostMatrix), ("o", HostMatrix),
+                ("is_moe", I32), ("router", HostMatrix),
+                ("dense_gate", HostMatrix), ("dense_up", HostMatrix), ("dense_down", HostMatrix)]
+
+
+class DecoderDesc(C.Structure):
+    _fields_ = [("hidden", U32), ("n_layers", U32), ("n_heads", U32), ("n_kv_heads", U32),
+                ("head_dim", U32), ("vocab", U32), ("n_experts", U32), ("top_k", U32),
+                ("normalize_topk", I32), ("eps", C.c_float), ("rope_theta", C.c_float),
+                ("embed", HostMatrix), ("lm_head", HostMatrix), ("final_norm", P)]
+
+
 SIGNATURES = {
     "hale_ctx_create": (I32, [C.c_int, C.POINTER(P)]),
     "hale_ctx_destroy": (None, [P]),
@@ -90,6 +108,9 @@ SIGNATURES = {
     "hale_ep_dispatch": (I32, [P, P, U32, P, U32, U32, P, P, P, C.POINTER(U64), P, P, P]),
     "hale_ep_experts": (I32, [P, P, U32, U32, P, P, P, U32, P, P]),
     "hale_ep_combine": (I32, [P, P, P, U32, U32, U32, P, P]),
+    "hale_decoder_create": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, C.POINTER(P)]),
+    "hale_decoder_destroy": (None, [P]),
+    "hale_decoder_forward": (I32, [P, P, U32, U32, P, P, P]),
     "hale_lm_head": (I32, [P, P, P, U32, P, P]),
     "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
     "hale_expf_host": (None, [P, P, U64]),
@@ -316,6 +337,71 @@ def moe_route_noalloc(router, router_dtype, n_experts, top_k, normalize, hidden,
     _check(lib().hale_moe_route_noalloc(ptr(router), router_dtype, n_experts, top_k, int(normalize),
                                         hidden, ptr(x), x.shape[0], ptr(topk_idx), ptr(topk_w),
                                         ptr(probs), _stream(stream)))
+
+
+class Decoder:
+    """hale_decoder: Transformer::forward (transformer.rs:168-227) on the GPU.
+
+    dims: hidden, n_layers, n_heads, n_kv_heads, head_dim, vocab, n_experts,
+    top_k, normalize_topk, eps, rope_theta. layers: one dict per layer with
+    input_norm, post_norm, q_norm / k_norm (or None) as float32 arrays; q, k,
+    v, o and router (MoE layers) or dense_gate / dense_up / dense_down as
+    (dtype, rows, cols, encoded uint8 rows). embed, lm_head: (dtype, rows,
+    cols, bytes); final_norm: float32 array. pool: the routed experts of the
+    MoE layers in order (pool layer j = j-th MoE layer), or None.
+    """
+
+    def __init__(self, ctx, dims, layers, embed, lm_head, final_norm, pool, max_len):
+        import numpy as np
+        self.ctx, self.dims, self._keep = ctx, dict(dims), []
+
+        def vec(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        def mat(m):
+            if m is None:
+                return HostMatrix(0, 0, 0, None)
+            dt, rows, cols, data = m
+            data = np.ascontiguousarray(data, dtype=np.uint8)
+            self._keep.append(data)
+            return HostMatrix(dt, rows, cols, data.ctypes.data)
+
+        arr = (DecoderLayer * len(layers))()
+        for i, L in enumerate(layers):
+            moe = L.get("router") is not None
+            arr[i] = DecoderLayer(vec(L["input_norm"]), vec(L["post_norm"]), vec(L.get("q_norm")),
+                                  vec(L.get("k_norm")), mat(L["q"]), mat(L["k"]), mat(L["v"]), mat(L["o"]),
+                                  int(moe), mat(L.get("router")), mat(L.get("dense_gate")),
+                                  mat(L.get("dense_up")), mat(L.get("dense_down")))
+        d = dims
+        desc = DecoderDesc(d["hidden"], d["n_layers"], d["n_heads"], d["n_kv_heads"], d["head_dim"], d["vocab"],
+                           d.get("n_experts", 0), d.get("top_k", 0), int(d.get("normalize_topk", 0)), d["eps"],
+                           d["rope_theta"], mat(embed), mat(lm_head), vec(final_norm))
+        h = P()
+        ctx.call("hale_decoder_create", ctx.h, C.byref(desc), arr, pool.h if pool is not None else None,
+                 max_len, C.byref(h))
+        self.h = h
+        self.pool = pool
+
+    def forward(self, token, position, logits=None, hidden=None, stream=None):
+        """One decode step; logits / hidden: device tensors or None."""
+        self.ctx.call("hale_decoder_forward", self.ctx.h, self.h, int(token), int(position), ptr(logits),
+                      ptr(hidden), _stream(stream))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hale_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def q8_aux_pairs(cols):

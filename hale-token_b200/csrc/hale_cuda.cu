@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -21,6 +22,7 @@
 #include "hale_tc.cuh"
 #include "hale_stream.cuh"
 #include "hale_ep.cuh"
+#include "hale_decoder.cuh"
 
 using namespace hale;
 
@@ -1147,6 +1149,243 @@ extern "C" hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, 
                                                                           (int)top_k, (int)hidden, out, ctx->d_err);
     }
     return check_launch(ctx, "ep_combine");
+}
+
+// ---------------------------------------------------------------------------
+// Decode step of the whole model (hale_decoder.cuh)
+// ---------------------------------------------------------------------------
+struct hale_decoder {
+    struct Layer {
+        float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+        hale_matrix *qkv = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+        int is_moe = 0;
+        void* router = nullptr;
+        hale_dtype router_dtype = HALE_F32;
+        uint32_t pool_layer = 0, inter = 0;
+    };
+    hale_ctx* ctx = nullptr;
+    hale_pool* pool = nullptr;
+    uint32_t H = 0, L = 0, nh = 0, nkv = 0, hd = 0, V = 0, E = 0, k = 0, max_len = 0;
+    int normalize = 0;
+    float eps = 0.0f, scale = 0.0f;
+    std::vector<Layer> layers;
+    void* embed = nullptr;
+    hale_dtype embed_dtype = HALE_F32;
+    hale_matrix* lm_head = nullptr;
+    float* final_norm = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr, *kcache = nullptr, *vcache = nullptr;
+    float *x = nullptr, *normed = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr;
+    float *g = nullptr, *u = nullptr, *h = nullptr, *scores = nullptr;
+    std::vector<void*> allocs;
+};
+
+extern "C" void hale_decoder_destroy(hale_decoder* d) {
+    if (!d) return;
+    cudaSetDevice(d->ctx->device);
+    for (auto& ly : d->layers)
+        for (hale_matrix* m : {ly.qkv, ly.o, ly.gate, ly.up, ly.down})
+            if (m) hale_matrix_destroy(m);
+    if (d->lm_head) hale_matrix_destroy(d->lm_head);
+    for (void* p : d->allocs) cudaFree(p);
+    delete d;
+}
+
+static hale_status dec_alloc(hale_ctx* ctx, hale_decoder* d, size_t bytes, void** out) {
+    if (cudaMalloc(out, std::max(bytes, (size_t)16)) != cudaSuccess)
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "decoder: cannot allocate %zu bytes", bytes);
+    d->allocs.push_back(*out);
+    CUDA_TRY(ctx, cudaMemset(*out, 0, bytes));
+    return HALE_OK;
+}
+
+static hale_status dec_upload(hale_ctx* ctx, hale_decoder* d, const void* host, size_t bytes, void** out) {
+    hale_status r = dec_alloc(ctx, d, bytes, out);
+    if (r) return r;
+    CUDA_TRY(ctx, cudaMemcpy(*out, host, bytes, cudaMemcpyHostToDevice));
+    return HALE_OK;
+}
+
+static hale_status dec_matrix(hale_ctx* ctx, const hale_host_matrix& m, uint32_t rows, uint32_t cols,
+                              const char* what, hale_matrix** out) {
+    if (!is_float((hale_dtype)m.dtype))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: %s must be f32, f16 or bf16", what);
+    if (m.rows != rows || m.cols != cols || !m.data)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: %s is %ux%u, expected %ux%u", what, m.rows, m.cols, rows,
+                    cols);
+    const int64_t rb = hale_row_bytes((hale_dtype)m.dtype, cols);
+    return hale_matrix_create(ctx, (hale_dtype)m.dtype, rows, cols, m.data, (uint64_t)rows * rb, 0, out);
+}
+
+extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_desc* ds, const hale_decoder_layer* lys,
+                                           hale_pool* pool, uint32_t max_len, hale_decoder** out) {
+    if (!ctx || !ds || !lys || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_create: NULL argument");
+    *out = nullptr;
+    const uint32_t H = ds->hidden, nh = ds->n_heads, nkv = ds->n_kv_heads, hd = ds->head_dim;
+    if (!H || !ds->n_layers || !nh || !nkv || !hd || !ds->vocab || !max_len || nh % nkv || hd % 2 || hd > 1024)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT,
+                    "decoder: bad shape (hidden %u, layers %u, heads %u/%u, head_dim %u, vocab %u, max_len %u)", H,
+                    ds->n_layers, nh, nkv, hd, ds->vocab, max_len);
+    if (!ds->final_norm) return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: final_norm is NULL");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_decoder* d = new hale_decoder();
+    d->ctx = ctx;
+    d->pool = pool;
+    d->H = H;
+    d->L = ds->n_layers;
+    d->nh = nh;
+    d->nkv = nkv;
+    d->hd = hd;
+    d->V = ds->vocab;
+    d->E = ds->n_experts;
+    d->k = ds->top_k;
+    d->normalize = ds->normalize_topk;
+    d->eps = ds->eps;
+    d->max_len = max_len;
+    d->scale = 1.0f / sqrtf((float)hd);  // attention.rs: 1 / sqrt(head_dim)
+    hale_status r = HALE_OK;
+    auto bail = [&](hale_status st) {
+        hale_decoder_destroy(d);
+        return st;
+    };
+    const uint32_t kvd = nkv * hd, qkv_rows = (nh + 2 * nkv) * hd;
+    uint32_t moe_layers = 0, max_inter = 1;
+    d->layers.resize(d->L);
+    for (uint32_t l = 0; l < d->L; l++) {
+        const hale_decoder_layer& s = lys[l];
+        auto& ly = d->layers[l];
+        if (!s.input_norm || !s.post_norm) return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: norm is NULL", l));
+        // q, k, v rows of one dtype go into one fused projection (rows are independent dots)
+        if (s.q.dtype != s.k.dtype || s.q.dtype != s.v.dtype)
+            return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: q/k/v dtypes differ", l));
+        if (s.q.rows != nh * hd || s.k.rows != kvd || s.v.rows != kvd || s.q.cols != H || s.k.cols != H ||
+            s.v.cols != H || !s.q.data || !s.k.data || !s.v.data)
+            return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: q/k/v shapes", l));
+        if (!is_float((hale_dtype)s.q.dtype))
+            return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: q/k/v must be float", l));
+        const size_t rb = (size_t)hale_row_bytes((hale_dtype)s.q.dtype, H);
+        std::vector<uint8_t> cat((size_t)qkv_rows * rb);
+        std::memcpy(cat.data(), s.q.data, (size_t)nh * hd * rb);
+        std::memcpy(cat.data() + (size_t)nh * hd * rb, s.k.data, (size_t)kvd * rb);
+        std::memcpy(cat.data() + (size_t)(nh + nkv) * hd * rb, s.v.data, (size_t)kvd * rb);
+        if ((r = hale_matrix_create(ctx, (hale_dtype)s.q.dtype, qkv_rows, H, cat.data(), cat.size(), 0, &ly.qkv)))
+            return bail(r);
+        if ((r = dec_matrix(ctx, s.o, H, nh * hd, "o_proj", &ly.o))) return bail(r);
+        if ((r = dec_upload(ctx, d, s.input_norm, H * 4, reinterpret_cast<void**>(&ly.in_norm)))) return bail(r);
+        if ((r = dec_upload(ctx, d, s.post_norm, H * 4, reinterpret_cast<void**>(&ly.post_norm)))) return bail(r);
+        if (s.q_norm && (r = dec_upload(ctx, d, s.q_norm, hd * 4, reinterpret_cast<void**>(&ly.q_norm)))) return bail(r);
+        if (s.k_norm && (r = dec_upload(ctx, d, s.k_norm, hd * 4, reinterpret_cast<void**>(&ly.k_norm)))) return bail(r);
+        ly.is_moe = s.is_moe ? 1 : 0;
+        if (ly.is_moe) {
+            if (!pool || pool->ctx != ctx || pool->H != H || pool->E != d->E || moe_layers >= pool->L)
+                return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: the expert pool does not hold MoE layer %u "
+                                 "(%u experts of hidden %u)", l, moe_layers, d->E, H));
+            if (!is_float((hale_dtype)s.router.dtype) || s.router.rows != d->E || s.router.cols != H || !s.router.data)
+                return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: router must be float [%u, %u]", l, d->E, H));
+            ly.router_dtype = (hale_dtype)s.router.dtype;
+            if ((r = dec_upload(ctx, d, s.router.data, (size_t)d->E * hale_row_bytes(ly.router_dtype, H), &ly.router)))
+                return bail(r);
+            ly.pool_layer = moe_layers++;
+        } else {
+            const uint32_t I = s.dense_gate.rows;
+            if ((r = dec_matrix(ctx, s.dense_gate, I, H, "dense gate", &ly.gate))) return bail(r);
+            if ((r = dec_matrix(ctx, s.dense_up, I, H, "dense up", &ly.up))) return bail(r);
+            if ((r = dec_matrix(ctx, s.dense_down, H, I, "dense down", &ly.down))) return bail(r);
+            ly.inter = I;
+            max_inter = std::max(max_inter, I);
+        }
+    }
+    const hale_dtype edt = (hale_dtype)ds->embed.dtype;
+    if (!is_float(edt) || ds->embed.rows != d->V || ds->embed.cols != H || !ds->embed.data)
+        return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: embedding must be float [%u, %u]", d->V, H));
+    d->embed_dtype = edt;
+    if ((r = dec_upload(ctx, d, ds->embed.data, (size_t)d->V * hale_row_bytes(edt, H), &d->embed))) return bail(r);
+    if ((r = dec_matrix(ctx, ds->lm_head, d->V, H, "lm_head", &d->lm_head))) return bail(r);
+    if ((r = dec_upload(ctx, d, ds->final_norm, H * 4, reinterpret_cast<void**>(&d->final_norm)))) return bail(r);
+    // RoPE tables with the host libm (rope.rs:15-30): inv_freq_i = 1 / theta^(2i / hd),
+    // angle = position * inv_freq_i
+    const uint32_t half = hd / 2;
+    std::vector<float> inv(half), cs((size_t)max_len * half), sn((size_t)max_len * half);
+    for (uint32_t i = 0; i < half; i++) inv[i] = 1.0f / powf(ds->rope_theta, (float)(2 * i) / (float)hd);
+    for (uint32_t p = 0; p < max_len; p++)
+        for (uint32_t i = 0; i < half; i++) {
+            const float angle = (float)p * inv[i];
+            cs[(size_t)p * half + i] = cosf(angle);
+            sn[(size_t)p * half + i] = sinf(angle);
+        }
+    if ((r = dec_upload(ctx, d, cs.data(), cs.size() * 4, reinterpret_cast<void**>(&d->rope_cos)))) return bail(r);
+    if ((r = dec_upload(ctx, d, sn.data(), sn.size() * 4, reinterpret_cast<void**>(&d->rope_sin)))) return bail(r);
+    const size_t cache = (size_t)d->L * max_len * kvd * 4;
+    if ((r = dec_alloc(ctx, d, cache, reinterpret_cast<void**>(&d->kcache)))) return bail(r);
+    if ((r = dec_alloc(ctx, d, cache, reinterpret_cast<void**>(&d->vcache)))) return bail(r);
+    struct { float** p; size_t n; } bufs[] = {{&d->x, H}, {&d->normed, H}, {&d->delta, H}, {&d->qkv, qkv_rows},
+                                               {&d->attn, (size_t)nh * hd}, {&d->g, max_inter}, {&d->u, max_inter},
+                                               {&d->h, max_inter}, {&d->scores, (size_t)nh * max_len}};
+    for (auto& b : bufs)
+        if ((r = dec_alloc(ctx, d, b.n * 4, reinterpret_cast<void**>(b.p)))) return bail(r);
+    *out = d;
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint32_t token, uint32_t position,
+                                            float* logits, float* hidden, void* stream) {
+    if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_forward: bad handle");
+    if (token >= d->V) return fail(ctx, HALE_E_INVALID_ARGUMENT, "token %u out of vocabulary (%u)", token, d->V);
+    if (position >= d->max_len)
+        return fail(ctx, HALE_E_CONTEXT_OVERFLOW, "position %u exceeds the KV cache (%u positions)", position,
+                    d->max_len);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    hale_status r;
+    const int H = (int)d->H, hb = (H + 255) / 256;
+    const size_t kvd = (size_t)d->nkv * d->hd;
+    switch (d->embed_dtype) {
+    case HALE_F32: embed_kernel<0><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
+    case HALE_F16: embed_kernel<1><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
+    default: embed_kernel<2><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
+    }
+    if ((r = check_launch(ctx, "embed"))) return r;
+    for (uint32_t l = 0; l < d->L; l++) {
+        const auto& ly = d->layers[l];
+        float* kc = d->kcache + (size_t)l * d->max_len * kvd;
+        float* vc = d->vcache + (size_t)l * d->max_len * kvd;
+        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, ly.in_norm, d->eps, H, d->normed);
+        if ((r = check_launch(ctx, "rmsnorm"))) return r;
+        if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, 1, d->qkv, nullptr, stream))) return r;
+        qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
+                                                          ly.k_norm, d->eps, d->rope_cos, d->rope_sin, position, kc,
+                                                          vc);
+        if ((r = check_launch(ctx, "qk_rope"))) return r;
+        attn_decode_kernel<<<d->nh, 256, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, position,
+                                                  (int)d->max_len, d->scale, d->scores, d->attn);
+        if ((r = check_launch(ctx, "attn_decode"))) return r;
+        if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, 1, d->delta, nullptr, stream))) return r;
+        add_kernel<<<hb, 256, 0, st>>>(d->x, d->delta, H);
+        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, ly.post_norm, d->eps, H, d->normed);
+        if ((r = check_launch(ctx, "rmsnorm"))) return r;
+        if (ly.is_moe) {
+            hale_moe_layer m{};
+            m.layer = ly.pool_layer;
+            m.router = ly.router;
+            m.router_dtype = ly.router_dtype;
+            m.n_experts = d->E;
+            m.top_k = d->k;
+            m.normalize_topk = d->normalize;
+            if ((r = hale_moe_forward(ctx, d->pool, &m, d->normed, 1, d->delta, nullptr, nullptr, stream))) return r;
+        } else {
+            if ((r = hale_matrix_matvec(ctx, ly.gate, d->normed, 1, d->g, nullptr, stream))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.up, d->normed, 1, d->u, nullptr, stream))) return r;
+            silu_mul_kernel<<<(ly.inter + 255) / 256, 256, 0, st>>>(d->g, d->u, (int)ly.inter, d->h);
+            if ((r = check_launch(ctx, "silu_mul"))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.down, d->h, 1, d->delta, nullptr, stream))) return r;
+        }
+        add_kernel<<<hb, 256, 0, st>>>(d->x, d->delta, H);
+        if ((r = check_launch(ctx, "residual"))) return r;
+    }
+    rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->final_norm, d->eps, H, d->normed);
+    if ((r = check_launch(ctx, "rmsnorm"))) return r;
+    if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)H * 4, cudaMemcpyDeviceToDevice, st));
+    if (logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed, 1, logits, nullptr, stream);
+    return HALE_OK;
 }
 
 extern "C" hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, const float* hidden, uint32_t batch,

@@ -1,0 +1,160 @@
+// hale_decoder.cuh -- the dense pieces of one decode step of the reference's
+// Transformer::forward (src/model/transformer.rs:168-227), around the MoE
+// layer: embedding row, RMSNorm, per-head QK-norm and RoPE with the KV-cache
+// append, GQA attention over the cache, residual adds, and the float SwiGLU
+// of dense layers. Every f32 operation keeps the reference's order, so a
+// decode step equals the oracle's bit for bit:
+//   - sums that the reference folds left to right (sum of squares in
+//     RMSNorm, the softmax denominator, each score's q.k, each context
+//     element) run as one sequential chain per output;
+//   - order-independent steps (max, elementwise) run in parallel.
+// The RoPE cos/sin tables come from the host's libm (the one the reference
+// calls), computed once per decoder.
+#pragma once
+
+#include "hale_kernels.cuh"
+
+namespace hale {
+
+// x[c] = embed[token][c] decoded to f32 (row-major source rows; DT 0 f32,
+// 1 f16, 2 bf16).
+template <int DT>
+__global__ void embed_kernel(const void* __restrict__ embed, int H, uint32_t token, float* __restrict__ x) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= H) return;
+    const size_t i = (size_t)token * H + c;
+    if (DT == 0) x[c] = reinterpret_cast<const float*>(embed)[i];
+    else if (DT == 1) x[c] = half_bits_to_float(reinterpret_cast<const uint16_t*>(embed)[i]);
+    else x[c] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(embed)[i] << 16);
+}
+
+// RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
+// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps, int n,
+                               float* __restrict__ out) {
+    __shared__ float s_scale;
+    if (threadIdx.x == 0) {
+        float s = -0.0f;
+        for (int i = 0; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
+        s_scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)n), eps)));
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fmul(fmul(x[i], scale), w[i]);
+}
+
+// Per head (one warp each; q heads, then k heads, then v heads): the in-place
+// RMSNorm of q/k heads, x = x * (scale * w) (norm.rs:30-37, attention.rs:49-56),
+// when the model has it; RoPE (rope.rs:15-43) a' = a c - b s, b' = b c + a s on
+// the pairs (i, i + hd/2); k and v rows appended to the cache at `pos`.
+// qkv: [nh*hd | nkv*hd | nkv*hd] as the fused projection wrote it.
+__global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd, const float* __restrict__ q_norm,
+                               const float* __restrict__ k_norm, float eps, const float* __restrict__ rope_cos,
+                               const float* __restrict__ rope_sin, uint32_t pos, float* __restrict__ kcache,
+                               float* __restrict__ vcache) {
+    const int head = blockIdx.x, lane = threadIdx.x, half = hd / 2;
+    const int kvd = nkv * hd;
+    if (head >= nh + 2 * nkv) return;
+    if (head >= nh + nkv) {  // v head: straight into the cache
+        const int vh = head - nh - nkv;
+        const float* v = qkv + (size_t)(nh + nkv) * hd + (size_t)vh * hd;
+        for (int i = lane; i < hd; i += 32) vcache[(size_t)pos * kvd + vh * hd + i] = v[i];
+        return;
+    }
+    const bool is_k = head >= nh;
+    float* x = qkv + (size_t)head * hd;
+    const float* w = is_k ? k_norm : q_norm;
+    if (w) {
+        float scale = 0.0f;
+        if (lane == 0) {
+            float s = -0.0f;
+            for (int i = 0; i < hd; i++) s = fadd(s, fmul(x[i], x[i]));
+            scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)hd), eps)));
+        }
+        scale = __shfl_sync(0xffffffffu, scale, 0);
+        __syncwarp();
+        for (int i = lane; i < hd; i += 32) x[i] = fmul(x[i], fmul(scale, w[i]));
+        __syncwarp();
+    }
+    const float* c = rope_cos + (size_t)pos * half;
+    const float* s = rope_sin + (size_t)pos * half;
+    for (int i = lane; i < half; i += 32) {
+        const float a = x[i], b = x[half + i];
+        x[i] = fsub(fmul(a, c[i]), fmul(b, s[i]));
+        x[half + i] = fadd(fmul(b, c[i]), fmul(a, s[i]));
+    }
+    __syncwarp();
+    if (is_k) {
+        const int kh = head - nh;
+        for (int i = lane; i < hd; i += 32) kcache[(size_t)pos * kvd + kh * hd + i] = x[i];
+    }
+}
+
+// Attention::forward for the token at pos (attention.rs:59-85), one CTA per
+// q head h (kv head h / (nh / nkv)): scores[t] = (sum_i q_i k_ti from -0) *
+// scale; softmax over t = 0..pos (activation.rs:11-21); ctx_i = sum_t
+// scores[t] v_ti from 0, t ascending. scores: [nh][max_len] scratch.
+__global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
+                                                          const float* __restrict__ kcache,
+                                                          const float* __restrict__ vcache,
+                                                          uint32_t pos, int max_len, float scale,
+                                                          float* __restrict__ scores, float* __restrict__ ctx) {
+    __shared__ float s_red[32];
+    __shared__ float s_bc[2];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int seq = (int)pos + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
+    const float* q = qkv + (size_t)h * hd;
+    float* sc = scores + (size_t)h * max_len;
+    float mx = -__int_as_float(0x7f800000);
+    for (int t = tid; t < seq; t += blockDim.x) {
+        const float* key = kcache + (size_t)t * kvd + off;
+        float s = -0.0f;
+        for (int i = 0; i < hd; i++) s = fadd(s, fmul(q[i], key[i]));
+        s = fmul(s, scale);
+        sc[t] = s;
+        mx = fmaxf(mx, s);
+    }
+    // max is order-independent
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) s_red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = -__int_as_float(0x7f800000);
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, s_red[w]);
+        s_bc[0] = m;
+    }
+    __syncthreads();
+    mx = s_bc[0];
+    for (int t = tid; t < seq; t += blockDim.x) sc[t] = hale_expf(fsub(sc[t], mx));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+        for (int t = 0; t < seq; t++) sum = fadd(sum, sc[t]);
+        s_bc[1] = sum;
+    }
+    __syncthreads();
+    const float sum = s_bc[1];
+    for (int t = tid; t < seq; t += blockDim.x) sc[t] = fdiv(sc[t], sum);
+    __syncthreads();
+    for (int i = tid; i < hd; i += blockDim.x) {
+        float c = 0.0f;
+        for (int t = 0; t < seq; t++) c = fadd(c, fmul(sc[t], vcache[(size_t)t * kvd + off + i]));
+        ctx[(size_t)h * hd + i] = c;
+    }
+}
+
+// x[i] = x[i] + d[i] (transformer.rs residual adds).
+__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ d, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = fadd(x[i], d[i]);
+}
+
+// h[j] = silu(g[j]) * u[j] (expert/mod.rs:100 for float dense layers).
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, int n,
+                                float* __restrict__ h) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) h[j] = fmul(silu(g[j]), u[j]);
+}
+
+}  // namespace hale

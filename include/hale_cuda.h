@@ -291,6 +291,55 @@ HALE_API hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, co
                                      uint32_t m_tokens, uint32_t top_k, uint32_t hidden, float* out,
                                      void* stream);
 
+/* ---- decode step of the whole model ----------------------------------------
+ * Transformer::forward (transformer.rs:168-227) for one token: embedding
+ * row, then per layer RMSNorm -> attention (q/k/v projections, per-head
+ * q/k RMSNorm when present, RoPE, KV-cache append, GQA softmax attention,
+ * o projection) -> residual -> RMSNorm -> MoE layer or dense SwiGLU ->
+ * residual; final RMSNorm and lm_head. Bit-identical to the reference's
+ * arithmetic (the RoPE tables come from the host libm the reference calls).
+ * Matrices are given as host row-major buffers in the reference's encodings
+ * (tensor/dtype.rs); dense matrices must be float (f32, f16, bf16). */
+typedef struct {
+    int32_t dtype;       /* hale_dtype */
+    uint32_t rows, cols;
+    const void* data;    /* rows * hale_row_bytes(dtype, cols) bytes, host memory */
+} hale_host_matrix;
+
+typedef struct {
+    const float* input_norm;   /* [hidden], host */
+    const float* post_norm;    /* [hidden] */
+    const float* q_norm;       /* [head_dim] or NULL (Mixtral) */
+    const float* k_norm;       /* [head_dim] or NULL */
+    hale_host_matrix q, k, v, o;                 /* [nh*hd, H], [nkv*hd, H] x2, [H, nh*hd] */
+    int32_t is_moe;
+    hale_host_matrix router;                     /* is_moe: [n_experts, H], float */
+    hale_host_matrix dense_gate, dense_up, dense_down;  /* !is_moe: [I, H], [I, H], [H, I] */
+} hale_decoder_layer;
+
+typedef struct {
+    uint32_t hidden, n_layers, n_heads, n_kv_heads, head_dim, vocab, n_experts, top_k;
+    int32_t normalize_topk;
+    float eps, rope_theta;
+    hale_host_matrix embed;    /* [vocab, hidden], float */
+    hale_host_matrix lm_head;  /* [vocab, hidden], float */
+    const float* final_norm;   /* [hidden], host */
+} hale_decoder_desc;
+
+typedef struct hale_decoder hale_decoder;
+
+/* Builds the decoder on ctx's GPU. experts: the routed experts of the MoE
+ * layers in order (pool layer j = the j-th MoE layer), already uploaded;
+ * NULL when the model has no MoE layer. max_len: KV-cache positions. */
+HALE_API hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_desc* desc,
+                                         const hale_decoder_layer* layers, hale_pool* experts,
+                                         uint32_t max_len, hale_decoder** out);
+HALE_API void hale_decoder_destroy(hale_decoder* dec);
+/* One step for `token` at `position` (KV cache appended there). logits
+ * [vocab] / hidden [hidden] (the final-normed state): device, nullable. */
+HALE_API hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* dec, uint32_t token, uint32_t position,
+                                          float* logits, float* hidden, void* stream);
+
 /* ---- sampling tail -------------------------------------------------------- */
 
 /* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .
