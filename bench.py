@@ -44,6 +44,10 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel measurement at N > 1")
+    p.add_argument("--decode", action="store_true",
+                   help="whole-model decode tok/s at batch 1 (BASELINE config 2 shapes) instead of the layer")
+    p.add_argument("--layers", type=int, default=48, help="--decode: decoder layers")
+    p.add_argument("--prompt", type=int, default=64, help="--decode: positions filled before timing")
     return p.parse_args()
 
 
@@ -192,6 +196,91 @@ def measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush,
             "scales, route metadata; y rows back)", "bit_exact_vs_1gpu": "tests/test_gpu_ep*.py"}
 
 
+def run_decode(args):
+    """Whole-model decode at batch 1 with BASELINE config 2's shapes
+    (Qwen3-30B-A3B: hidden 2048, 32 q / 4 kv heads of 128, q/k norms, 128
+    experts top-8 of intermediate 768 in q4_0, vocab 151936, bf16 attention,
+    embedding and lm_head). Synthetic weights: one layer's 128 expert records
+    uploaded to every layer (each layer its own copy in HBM), random bf16
+    dense weights N(0, 0.02), norms 1.0. A step is one hale_decoder_forward
+    (token -> logits); `prompt` positions are filled first, then `steps`
+    timed with CUDA events (device time, no L2 flush: the per-token working
+    set is ~3.5 GB)."""
+    import importlib
+
+    import torch
+    hale = importlib.import_module("hale-token_b200")
+    fmt = importlib.import_module("hale-token_b200.formats")
+    torch.cuda.set_device(0)
+    ctx = hale.Context(0)
+    L, Hd, nh, nkv, hd, V = args.layers, 2048, 32, 4, 128, 151936
+    rng = np.random.default_rng(SEED)
+
+    def bf16(rows, cols):
+        a = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02).view(np.uint32)
+        return (fmt.BF16, rows, cols, ((a + 0x7FFF + ((a >> 16) & 1)) >> 16).astype(np.uint16).view(np.uint8))
+
+    ld = make_layer(fmt)
+    encoded = encode_all(ld)
+    pool = hale.Pool(ctx, fmt.Q4_0, Hd, I, L, E)
+    records = [fmt.pack_record(*encoded[e]) for e in range(E)]
+    for l in range(L):
+        for e in range(E):
+            pool.upload(l, e, records[e])
+    ones_h, ones_d = np.ones(Hd, np.float32), np.ones(hd, np.float32)
+    router = (fmt.F32, E, Hd, fmt.encode(fmt.F32, ld.router))
+    layers = []
+    for l in range(L):
+        layers.append(dict(input_norm=ones_h, post_norm=ones_h, q_norm=ones_d, k_norm=ones_d,
+                           q=bf16(nh * hd, Hd), k=bf16(nkv * hd, Hd), v=bf16(nkv * hd, Hd), o=bf16(Hd, nh * hd),
+                           router=router))
+    dims = dict(hidden=Hd, n_layers=L, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, n_experts=E, top_k=K_TOP,
+                normalize_topk=1, eps=1e-6, rope_theta=1e6)
+    max_len = args.prompt + args.steps + args.warmup + 1
+    dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len)
+    logits = torch.empty(V, dtype=torch.float32, device="cuda")
+    toks = rng.integers(0, V, size=max_len)
+    pos = 0
+    for _ in range(args.prompt + args.warmup):
+        dec.forward(int(toks[pos]), pos, logits)
+        pos += 1
+    ctx.check()
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches0 = ctx.launches
+    torch.cuda.synchronize()
+    ctx.profile(True)
+    for a, b in evs:
+        a.record(stream)
+        dec.forward(int(toks[pos]), pos, logits)
+        b.record(stream)
+        pos += 1
+    torch.cuda.synchronize()
+    ctx.profile(False)
+    ctx.check()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    names = ("router", "expert_gate_up", "expert_down")
+    kern = {k: {"launches_per_token": n / args.steps, "ms_per_token": t / args.steps}
+            for k in names for n, t in [ctx.profile_read(k)]}
+    q4r_h, q4r_i = fmt.row_bytes(fmt.Q4_0, Hd), fmt.row_bytes(fmt.Q4_0, I)
+    expert_bytes = 2 * I * q4r_h + Hd * q4r_i
+    attn_bytes = ((nh + 2 * nkv) * hd * Hd + Hd * nh * hd) * 2
+    per_token_bytes = L * (K_TOP * expert_bytes + attn_bytes + E * Hd * 4) + V * Hd * 2
+    line = {"metric": "decode_tok_s_full_model", "value": 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 experts, bf16 dense, f32 activations",
+            "data": "synthetic",
+            "config": {"workload": "qwen3_30b_a3b_decode_b1", "layers": L, "hidden": Hd, "heads": nh,
+                       "kv_heads": nkv, "head_dim": hd, "vocab": V, "experts": E, "top_k": K_TOP,
+                       "moe_intermediate": I, "batch": 1, "positions_before_timing": args.prompt},
+            "gpu_launches_per_token": (ctx.launches - launches0) / args.steps, "kernels": kern,
+            "algorithmic_bytes_per_token": per_token_bytes,
+            "achieved_gbs": per_token_bytes / (ms / 1e3) / 1e9}
+    emit(line)
+    dec.close()
+    ctx.close()
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -227,6 +316,9 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 def main():
     args = parse()
+    if args.decode:
+        run_decode(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
