@@ -71,6 +71,7 @@ struct hale_matrix {
     uint32_t nb;     // quantized: blocks per row; float: steps of 8
     uint8_t* data;
     size_t bytes;
+    bool lanes = false;  // float, lane-major layout (fgemv_lanes_kernel); rows_pad = rows rounded to 4
 };
 
 struct hale_pool {
@@ -528,8 +529,22 @@ static void fgemv_dispatch(const hale_matrix* m, const float* x, uint32_t M, flo
 
 static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float* x, uint32_t M, float* out,
                                 cudaStream_t st) {
-    int vec = (m->cols % 4 == 0) && (((uintptr_t)x & 15) == 0);
     ProfScope ps_(ctx, "fgemv", st);
+    if (m->lanes) {
+        const unsigned grid = (m->rows_pad / 4 + 7) / 8;
+        const size_t smem = (size_t)m->cols * 4;
+        for (uint32_t t = 0; t < M; t++) {
+            const float* xt = x + (size_t)t * m->cols;
+            float* ot = out + (size_t)t * m->rows;
+            switch (m->dtype) {
+            case HALE_F32: fgemv_lanes_kernel<0><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            case HALE_F16: fgemv_lanes_kernel<1><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            default: fgemv_lanes_kernel<2><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            }
+        }
+        return check_launch(ctx, "fgemv_lanes");
+    }
+    int vec = (m->cols % 4 == 0) && (((uintptr_t)x & 15) == 0);
     switch (m->dtype) {
     case HALE_F32: fgemv_dispatch<0>(m, x, M, out, vec, st); break;
     case HALE_F16: fgemv_dispatch<1>(m, x, M, out, vec, st); break;
@@ -1154,6 +1169,47 @@ extern "C" hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, 
 // ---------------------------------------------------------------------------
 // Decode step of the whole model (hale_decoder.cuh)
 // ---------------------------------------------------------------------------
+// A float matrix in the lane-major layout (fgemv_lanes_kernel): cols a
+// multiple of 64, at most 12288 (its activation row is staged in shared
+// memory). Host row-major data in.
+static hale_status matrix_create_lanes(hale_ctx* ctx, hale_dtype dt, uint32_t rows, uint32_t cols, const void* host,
+                                       hale_matrix** out) {
+    *out = nullptr;
+    const int es = dt == HALE_F32 ? 4 : 2;
+    hale_matrix* m = new hale_matrix();
+    m->ctx = ctx;
+    m->dtype = dt;
+    m->rows = rows;
+    m->cols = cols;
+    m->rows_pad = (rows + 3) / 4 * 4;
+    m->nb = cols / 8;
+    m->lanes = true;
+    m->bytes = (size_t)m->rows_pad * cols * es;
+    uint8_t* tmp = nullptr;
+    const size_t src_bytes = (size_t)rows * cols * es;
+    if (cudaMalloc(&m->data, m->bytes) != cudaSuccess || cudaMalloc(&tmp, src_bytes) != cudaSuccess ||
+        cudaMemcpy(tmp, host, src_bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(tmp);
+        cudaFree(m->data);
+        delete m;
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "cannot stage a %ux%u float matrix", rows, cols);
+    }
+    const unsigned grid = (unsigned)std::min<size_t>((m->bytes / es + 255) / 256, 65535);
+    if (es == 4) repack_lanes_kernel<4><<<grid, 256>>>(tmp, m->data, (int)rows, (int)m->rows_pad, (int)cols);
+    else repack_lanes_kernel<2><<<grid, 256>>>(tmp, m->data, (int)rows, (int)m->rows_pad, (int)cols);
+    const cudaError_t e1 = cudaGetLastError(), e2 = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) {
+        cudaFree(m->data);
+        delete m;
+        return fail(ctx, HALE_E_CUDA, "lane-major repack failed: %s", cudaGetErrorString(e1 ? e1 : e2));
+    }
+    *out = m;
+    return HALE_OK;
+}
+
+static bool lanes_ok(hale_dtype dt, uint32_t cols) { return is_float(dt) && cols % 64 == 0 && cols <= 12288; }
+
 struct hale_decoder {
     struct Layer {
         float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
@@ -1212,6 +1268,7 @@ static hale_status dec_matrix(hale_ctx* ctx, const hale_host_matrix& m, uint32_t
     if (m.rows != rows || m.cols != cols || !m.data)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: %s is %ux%u, expected %ux%u", what, m.rows, m.cols, rows,
                     cols);
+    if (lanes_ok((hale_dtype)m.dtype, cols)) return matrix_create_lanes(ctx, (hale_dtype)m.dtype, rows, cols, m.data, out);
     const int64_t rb = hale_row_bytes((hale_dtype)m.dtype, cols);
     return hale_matrix_create(ctx, (hale_dtype)m.dtype, rows, cols, m.data, (uint64_t)rows * rb, 0, out);
 }
@@ -1267,8 +1324,10 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
         std::memcpy(cat.data(), s.q.data, (size_t)nh * hd * rb);
         std::memcpy(cat.data() + (size_t)nh * hd * rb, s.k.data, (size_t)kvd * rb);
         std::memcpy(cat.data() + (size_t)(nh + nkv) * hd * rb, s.v.data, (size_t)kvd * rb);
-        if ((r = hale_matrix_create(ctx, (hale_dtype)s.q.dtype, qkv_rows, H, cat.data(), cat.size(), 0, &ly.qkv)))
-            return bail(r);
+        r = lanes_ok((hale_dtype)s.q.dtype, H)
+                ? matrix_create_lanes(ctx, (hale_dtype)s.q.dtype, qkv_rows, H, cat.data(), &ly.qkv)
+                : hale_matrix_create(ctx, (hale_dtype)s.q.dtype, qkv_rows, H, cat.data(), cat.size(), 0, &ly.qkv);
+        if (r) return bail(r);
         if ((r = dec_matrix(ctx, s.o, H, nh * hd, "o_proj", &ly.o))) return bail(r);
         if ((r = dec_upload(ctx, d, s.input_norm, H * 4, reinterpret_cast<void**>(&ly.in_norm)))) return bail(r);
         if ((r = dec_upload(ctx, d, s.post_norm, H * 4, reinterpret_cast<void**>(&ly.post_norm)))) return bail(r);
@@ -1348,7 +1407,8 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
         const auto& ly = d->layers[l];
         float* kc = d->kcache + (size_t)l * d->max_len * kvd;
         float* vc = d->vcache + (size_t)l * d->max_len * kvd;
-        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, ly.in_norm, d->eps, H, d->normed);
+        // the previous layer's FFN residual folds into this norm
+        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, 1, d->qkv, nullptr, stream))) return r;
         qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
@@ -1359,8 +1419,7 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
                                                   (int)d->max_len, d->scale, d->scores, d->attn);
         if ((r = check_launch(ctx, "attn_decode"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, 1, d->delta, nullptr, stream))) return r;
-        add_kernel<<<hb, 256, 0, st>>>(d->x, d->delta, H);
-        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, ly.post_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
             hale_moe_layer m{};
@@ -1378,10 +1437,8 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
             if ((r = check_launch(ctx, "silu_mul"))) return r;
             if ((r = hale_matrix_matvec(ctx, ly.down, d->h, 1, d->delta, nullptr, stream))) return r;
         }
-        add_kernel<<<hb, 256, 0, st>>>(d->x, d->delta, H);
-        if ((r = check_launch(ctx, "residual"))) return r;
     }
-    rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->final_norm, d->eps, H, d->normed);
+    rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)H * 4, cudaMemcpyDeviceToDevice, st));
     if (logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed, 1, logits, nullptr, stream);

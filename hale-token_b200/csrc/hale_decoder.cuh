@@ -28,11 +28,16 @@ __global__ void embed_kernel(const void* __restrict__ embed, int H, uint32_t tok
     else x[c] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(embed)[i] << 16);
 }
 
+// The residual add x += delta (transformer.rs residual; delta nullable), then
 // RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
 // -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps, int n,
-                               float* __restrict__ out) {
+__global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
+                               float eps, int n, float* __restrict__ out) {
     __shared__ float s_scale;
+    if (delta) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = fadd(x[i], delta[i]);
+        __syncthreads();
+    }
     if (threadIdx.x == 0) {
         float s = -0.0f;
         for (int i = 0; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
@@ -142,12 +147,6 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
         for (int t = 0; t < seq; t++) c = fadd(c, fmul(sc[t], vcache[(size_t)t * kvd + off + i]));
         ctx[(size_t)h * hd + i] = c;
     }
-}
-
-// x[i] = x[i] + d[i] (transformer.rs residual adds).
-__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ d, int n) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) x[i] = fadd(x[i], d[i]);
 }
 
 // h[j] = silu(g[j]) * u[j] (expert/mod.rs:100 for float dense layers).

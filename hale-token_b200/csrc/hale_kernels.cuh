@@ -91,12 +91,15 @@ __host__ __device__ __forceinline__ int aux_stride(int nb) { return (nb + 1) & ~
 // One block of Q8Activations::quantize by one thread: the 32 values come in
 // with eight 16-byte loads and leave with two 16-byte stores (xb, q 16-byte
 // aligned: rows of a multiple of 32 elements).
+// SMEM: xb points into shared memory (plain loads instead of the read-only
+// global path).
+template <bool SMEM = false>
 __device__ __forceinline__ void quantize_block(const float* __restrict__ xb, int8_t* __restrict__ q,
                                                float* scale_out, int* sum_out) {
     float v[kQK];
 #pragma unroll
     for (int j = 0; j < kQK / 4; j++) {
-        float4 f = __ldg(reinterpret_cast<const float4*>(xb) + j);
+        float4 f = SMEM ? reinterpret_cast<const float4*>(xb)[j] : __ldg(reinterpret_cast<const float4*>(xb) + j);
         v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
     }
     float amax = 0.0f;
@@ -1092,6 +1095,63 @@ __global__ void __launch_bounds__(128) fgemv_kernel(const uint8_t* __restrict__ 
             float a0 = fadd(fadd(acc[j][0], acc[j][4]), fadd(acc[j][1], acc[j][5]));
             float a1 = fadd(fadd(acc[j][2], acc[j][6]), fadd(acc[j][3], acc[j][7]));
             if (row < rows) out[(size_t)(t0 + j) * rows + row] = fadd(fadd(a0, a1), tail);
+        }
+    }
+}
+
+// Float matvec for one activation row in the lane-major layout (cols a
+// multiple of 64): in each group of 4 rows, for each group of 8 steps (a step
+// = 8 columns), row rr's lane l holds its 8 consecutive step values
+// contiguously -- offset ((q * S8 + s) * 4 + rr) * 64 + l * 8 + j elements for
+// row 4q + rr, column 8 (8 s + j) + l. A warp covers 4 rows x 8 lanes: thread
+// (rr, l) runs the reference's accumulator lane l of row 4q + rr
+// (acc += w * x over the steps in order, quant.rs:152-160), and reduce()
+// ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) (quant.rs:37-41) combines the 8
+// threads; the (empty) tail adds -0. 8x the row parallelism of
+// fgemv_kernel, with 512-byte warp loads.
+template <int DT>
+__global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restrict__ W, int rows, int cols,
+                                                          const float* __restrict__ x, float* __restrict__ out) {
+    extern __shared__ float s_x[];  // [cols]
+    constexpr int ES = DT == 0 ? 4 : 2;
+    for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[i] = x[i];
+    __syncthreads();
+    const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (q * 4 >= rows) return;
+    const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
+    const uint8_t* base = W + (((size_t)q * S8 * 4 + rr) * 64 + l * 8) * ES;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int s = 0; s < S8; s++) {
+        float w[8];
+        load8<DT>(base + (size_t)s * 4 * 64 * ES, w);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc = fadd(acc, fmul(w[j], s_x[(8 * s + j) * 8 + l]));
+    }
+    const float s1 = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
+    const float p = fadd(s1, __shfl_down_sync(0xffffffffu, s1, 1, 8));
+    const float r = fadd(p, __shfl_down_sync(0xffffffffu, p, 2, 8));
+    const int row = q * 4 + rr;
+    if (l == 0 && row < rows) out[row] = fadd(r, -0.0f);
+}
+
+// Row-major float rows -> the lane-major layout (rows padded to 4 with 0).
+template <int ES>
+__global__ void repack_lanes_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+                                    int rows_pad, int cols) {
+    const size_t n = (size_t)rows_pad * cols;
+    const int S8 = cols / 64;
+    for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < n; o += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(o & 7), l = (int)((o >> 3) & 7), rr = (int)((o >> 6) & 3);
+        const size_t qs = o >> 8;
+        const int s = (int)(qs % S8), q = (int)(qs / S8);
+        const int r = q * 4 + rr, c = 8 * (8 * s + j) + l;
+        uint8_t* d = dst + o * ES;
+        if (r < rows) {
+            const uint8_t* sp = src + ((size_t)r * cols + c) * ES;
+            for (int b = 0; b < ES; b++) d[b] = sp[b];
+        } else {
+            for (int b = 0; b < ES; b++) d[b] = 0;
         }
     }
 }
