@@ -1233,11 +1233,25 @@ struct hale_decoder {
     float *x = nullptr, *normed = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr;
     float *g = nullptr, *u = nullptr, *h = nullptr, *scores = nullptr;
     std::vector<void*> allocs;
+    // step replay: token/position through device memory from a pinned slot
+    uint32_t* d_tp = nullptr;
+    uint32_t* h_tp = nullptr;
+    cudaEvent_t ev_copied = nullptr;
+    bool copied_recorded = false;
+    cudaStream_t cap = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    float *g_logits = nullptr, *g_hidden = nullptr;
+    bool no_graph = false;
 };
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
     if (!d) return;
     cudaSetDevice(d->ctx->device);
+    cudaDeviceSynchronize();
+    if (d->exec) cudaGraphExecDestroy(d->exec);
+    if (d->cap) cudaStreamDestroy(d->cap);
+    if (d->ev_copied) cudaEventDestroy(d->ev_copied);
+    if (d->h_tp) cudaFreeHost(d->h_tp);
     for (auto& ly : d->layers)
         for (hale_matrix* m : {ly.qkv, ly.o, ly.gate, ly.up, ly.down})
             if (m) hale_matrix_destroy(m);
@@ -1381,26 +1395,27 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
                                                {&d->h, max_inter}, {&d->scores, (size_t)nh * max_len}};
     for (auto& b : bufs)
         if ((r = dec_alloc(ctx, d, b.n * 4, reinterpret_cast<void**>(b.p)))) return bail(r);
+    if ((r = dec_alloc(ctx, d, 8, reinterpret_cast<void**>(&d->d_tp)))) return bail(r);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_tp), 8, cudaHostAllocDefault) != cudaSuccess ||
+        cudaEventCreateWithFlags(&d->ev_copied, cudaEventDisableTiming) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(ctx, HALE_E_CUDA, "decoder: cannot create its step resources"));
     *out = d;
     return HALE_OK;
 }
 
-extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint32_t token, uint32_t position,
-                                            float* logits, float* hidden, void* stream) {
-    if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_forward: bad handle");
-    if (token >= d->V) return fail(ctx, HALE_E_INVALID_ARGUMENT, "token %u out of vocabulary (%u)", token, d->V);
-    if (position >= d->max_len)
-        return fail(ctx, HALE_E_CONTEXT_OVERFLOW, "position %u exceeds the KV cache (%u positions)", position,
-                    d->max_len);
-    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-    cudaStream_t st = S(stream);
+// One step on stream st: the token/position copy from the pinned slot, then
+// every kernel of the step.
+static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, float* logits, float* hidden, cudaStream_t st) {
+    void* stream = st;
+    CUDA_TRY(ctx, cudaMemcpyAsync(d->d_tp, d->h_tp, 8, cudaMemcpyHostToDevice, st));
     hale_status r;
     const int H = (int)d->H, hb = (H + 255) / 256;
     const size_t kvd = (size_t)d->nkv * d->hd;
     switch (d->embed_dtype) {
-    case HALE_F32: embed_kernel<0><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
-    case HALE_F16: embed_kernel<1><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
-    default: embed_kernel<2><<<hb, 256, 0, st>>>(d->embed, H, token, d->x); break;
+    case HALE_F32: embed_kernel<0><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
+    case HALE_F16: embed_kernel<1><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
+    default: embed_kernel<2><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
     }
     if ((r = check_launch(ctx, "embed"))) return r;
     for (uint32_t l = 0; l < d->L; l++) {
@@ -1412,10 +1427,10 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, 1, d->qkv, nullptr, stream))) return r;
         qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
-                                                          ly.k_norm, d->eps, d->rope_cos, d->rope_sin, position, kc,
+                                                          ly.k_norm, d->eps, d->rope_cos, d->rope_sin, d->d_tp, kc,
                                                           vc);
         if ((r = check_launch(ctx, "qk_rope"))) return r;
-        attn_decode_kernel<<<d->nh, 256, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, position,
+        attn_decode_kernel<<<d->nh, 256, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_tp,
                                                   (int)d->max_len, d->scale, d->scores, d->attn);
         if ((r = check_launch(ctx, "attn_decode"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, 1, d->delta, nullptr, stream))) return r;
@@ -1442,6 +1457,54 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)H * 4, cudaMemcpyDeviceToDevice, st));
     if (logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed, 1, logits, nullptr, stream);
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint32_t token, uint32_t position,
+                                            float* logits, float* hidden, void* stream) {
+    if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_forward: bad handle");
+    if (token >= d->V) return fail(ctx, HALE_E_INVALID_ARGUMENT, "token %u out of vocabulary (%u)", token, d->V);
+    if (position >= d->max_len)
+        return fail(ctx, HALE_E_CONTEXT_OVERFLOW, "position %u exceeds the KV cache (%u positions)", position,
+                    d->max_len);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    // the previous step must have read the slot before it is rewritten
+    if (d->copied_recorded) CUDA_TRY(ctx, cudaEventSynchronize(d->ev_copied));
+    d->h_tp[0] = token;
+    d->h_tp[1] = position;
+    const bool capturing = stream_capturing(stream);
+    d->copied_recorded = !capturing;
+    if (d->exec && d->g_logits == logits && d->g_hidden == hidden && !capturing) {
+        CUDA_TRY(ctx, cudaGraphLaunch(d->exec, st));
+        CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
+        return HALE_OK;
+    }
+    hale_status r = decoder_enqueue(ctx, d, logits, hidden, st);
+    if (!r && !capturing) CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
+    if (r || capturing || d->no_graph) return r;
+    // capture the step for the following calls with these outputs
+    if (d->exec) {
+        cudaGraphExecDestroy(d->exec);
+        d->exec = nullptr;
+    }
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        d->no_graph = true;
+        return HALE_OK;
+    }
+    r = decoder_enqueue(ctx, d, logits, hidden, d->cap);
+    const cudaError_t ec = cudaStreamEndCapture(d->cap, &graph);
+    if (r || ec != cudaSuccess || !graph || cudaGraphInstantiate(&d->exec, graph, 0) != cudaSuccess) {
+        cudaGetLastError();
+        d->exec = nullptr;
+        d->no_graph = true;  // keep launching step by step
+        g_thread_status = HALE_OK;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    d->g_logits = logits;
+    d->g_hidden = hidden;
     return HALE_OK;
 }
 

@@ -16,13 +16,17 @@
 
 namespace hale {
 
+// tp[0] = token, tp[1] = position of the step, in device memory so that a
+// captured step replays for any token.
+
 // x[c] = embed[token][c] decoded to f32 (row-major source rows; DT 0 f32,
 // 1 f16, 2 bf16).
 template <int DT>
-__global__ void embed_kernel(const void* __restrict__ embed, int H, uint32_t token, float* __restrict__ x) {
+__global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32_t* __restrict__ tp,
+                             float* __restrict__ x) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= H) return;
-    const size_t i = (size_t)token * H + c;
+    const size_t i = (size_t)tp[0] * H + c;
     if (DT == 0) x[c] = reinterpret_cast<const float*>(embed)[i];
     else if (DT == 1) x[c] = half_bits_to_float(reinterpret_cast<const uint16_t*>(embed)[i]);
     else x[c] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(embed)[i] << 16);
@@ -55,9 +59,10 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
 // qkv: [nh*hd | nkv*hd | nkv*hd] as the fused projection wrote it.
 __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd, const float* __restrict__ q_norm,
                                const float* __restrict__ k_norm, float eps, const float* __restrict__ rope_cos,
-                               const float* __restrict__ rope_sin, uint32_t pos, float* __restrict__ kcache,
-                               float* __restrict__ vcache) {
+                               const float* __restrict__ rope_sin, const uint32_t* __restrict__ tp,
+                               float* __restrict__ kcache, float* __restrict__ vcache) {
     const int head = blockIdx.x, lane = threadIdx.x, half = hd / 2;
+    const uint32_t pos = tp[1];
     const int kvd = nkv * hd;
     if (head >= nh + 2 * nkv) return;
     if (head >= nh + nkv) {  // v head: straight into the cache
@@ -102,12 +107,13 @@ __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd,
 __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
                                                           const float* __restrict__ kcache,
                                                           const float* __restrict__ vcache,
-                                                          uint32_t pos, int max_len, float scale,
-                                                          float* __restrict__ scores, float* __restrict__ ctx) {
+                                                          const uint32_t* __restrict__ tp, int max_len,
+                                                          float scale, float* __restrict__ scores,
+                                                          float* __restrict__ ctx) {
     __shared__ float s_red[32];
     __shared__ float s_bc[2];
     const int h = blockIdx.x, tid = threadIdx.x;
-    const int seq = (int)pos + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
+    const int seq = (int)tp[1] + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
     const float* q = qkv + (size_t)h * hd;
     float* sc = scores + (size_t)h * max_len;
     float mx = -__int_as_float(0x7f800000);
