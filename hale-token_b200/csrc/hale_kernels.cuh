@@ -728,7 +728,23 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     __threadfence();
 
     // ---- last CTA of this token tile: softmax, top-k, quantize ----------
+    // warps 0 .. kRouterTT-1: softmax and top-k of one token each; the other
+    // warps quantize the tile's activation rows meanwhile
     const int warp = tid >> 5, lane = tid & 31;
+    static_assert(kRouterTT < 8, "the router tail needs warps left for quantization");
+    if (warp >= kRouterTT && a.xq) {
+        // Q8Activations::quantize of the tile's tokens (quant.rs:77-93)
+        const int nb = a.H / kQK, nbp = aux_stride(nb);
+        const int nt = min(kRouterTT, a.M - (int)blockIdx.x * kRouterTT);
+        for (int i = tid - kRouterTT * 32; i < nt * nb; i += (8 - kRouterTT) * 32) {
+            const int tt = i / nb, b = i - tt * nb;
+            const int tok = blockIdx.x * kRouterTT + tt;
+            float sc;
+            int sm;
+            quantize_block(a.x + (size_t)tok * a.H + b * kQK, a.xq + (size_t)tok * a.H + b * kQK, &sc, &sm);
+            a.xaux[(size_t)tok * nbp + b] = make_int2(__float_as_int(sc), -8 * sm);
+        }
+    }
     for (int tt = warp; tt < kRouterTT; tt += 8) {
         const int tok = blockIdx.x * kRouterTT + tt;
         if (tok >= a.M) break;
@@ -790,16 +806,6 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             a.topk_w[(size_t)tok * a.k + lane] = wv;
             if (a.user_idx) a.user_idx[(size_t)tok * a.k + lane] = chosen_idx;
             if (a.user_w) a.user_w[(size_t)tok * a.k + lane] = wv;
-        }
-        // Q8Activations::quantize of this token (quant.rs:77-93)
-        if (a.xq) {
-            const int nb = a.H / kQK, nbp = aux_stride(nb);
-            for (int b = lane; b < nb; b += 32) {
-                float sc;
-                int sm;
-                quantize_block(a.x + (size_t)tok * a.H + b * kQK, a.xq + (size_t)tok * a.H + b * kQK, &sc, &sm);
-                a.xaux[(size_t)tok * nbp + b] = make_int2(__float_as_int(sc), -8 * sm);
-            }
         }
         __syncwarp();
     }
