@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const uint8_t* __restrict__ 
 // activation rows. The last such CTA of the grid groups the routes by
 // expert for the expert kernels.
 // ---------------------------------------------------------------------------
-constexpr int kRouterTT = 4, kRouterET = 8, kRouterCH = 512, kRouterPad = 8;  // pad: 8-bank row skew
+constexpr int kRouterTT = 4, kRouterET = 8, kRouterCH = 1024, kRouterPad = 8;  // pad: 8-bank row skew
 constexpr int kRouterSlots = 4;
 
 struct RouterArgs {
