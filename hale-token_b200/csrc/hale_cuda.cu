@@ -1242,6 +1242,7 @@ struct hale_decoder {
     cudaGraphExec_t exec = nullptr;
     float *g_logits = nullptr, *g_hidden = nullptr;
     bool no_graph = false;
+    uint32_t smem_scores = 0;  // attention scores kept in shared memory up to this many positions
 };
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
@@ -1292,7 +1293,7 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
     if (!ctx || !ds || !lys || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_create: NULL argument");
     *out = nullptr;
     const uint32_t H = ds->hidden, nh = ds->n_heads, nkv = ds->n_kv_heads, hd = ds->head_dim;
-    if (!H || !ds->n_layers || !nh || !nkv || !hd || !ds->vocab || !max_len || nh % nkv || hd % 2 || hd > 1024)
+    if (!H || !ds->n_layers || !nh || !nkv || !hd || !ds->vocab || !max_len || nh % nkv || hd % 4 || hd > 1024)
         return fail(ctx, HALE_E_INVALID_ARGUMENT,
                     "decoder: bad shape (hidden %u, layers %u, heads %u/%u, head_dim %u, vocab %u, max_len %u)", H,
                     ds->n_layers, nh, nkv, hd, ds->vocab, max_len);
@@ -1396,6 +1397,9 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
     for (auto& b : bufs)
         if ((r = dec_alloc(ctx, d, b.n * 4, reinterpret_cast<void**>(b.p)))) return bail(r);
     if ((r = dec_alloc(ctx, d, 8, reinterpret_cast<void**>(&d->d_tp)))) return bail(r);
+    // attention keeps q and up to 8192 scores in shared memory (below 48 KB)
+    d->smem_scores = std::min<uint32_t>(max_len, 8192u);
+    if (H > 12000) return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: hidden %u above 12000", H));
     if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_tp), 8, cudaHostAllocDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&d->ev_copied, cudaEventDisableTiming) != cudaSuccess ||
         cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
@@ -1423,18 +1427,19 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, float* logits
         float* kc = d->kcache + (size_t)l * d->max_len * kvd;
         float* vc = d->vcache + (size_t)l * d->max_len * kvd;
         // the previous layer's FFN residual folds into this norm
-        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, 1, d->qkv, nullptr, stream))) return r;
-        qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
+        qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, (size_t)d->hd * 4, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
                                                           ly.k_norm, d->eps, d->rope_cos, d->rope_sin, d->d_tp, kc,
                                                           vc);
         if ((r = check_launch(ctx, "qk_rope"))) return r;
-        attn_decode_kernel<<<d->nh, 256, 0, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_tp,
-                                                  (int)d->max_len, d->scale, d->scores, d->attn);
+        attn_decode_kernel<<<d->nh, 256, ((size_t)d->hd + d->smem_scores) * 4, st>>>(
+            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_tp, (int)d->max_len, d->scale, d->scores,
+            d->attn, (int)d->smem_scores);
         if ((r = check_launch(ctx, "attn_decode"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, 1, d->delta, nullptr, stream))) return r;
-        rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
             hale_moe_layer m{};
@@ -1453,7 +1458,7 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, float* logits
             if ((r = hale_matrix_matvec(ctx, ly.down, d->h, 1, d->delta, nullptr, stream))) return r;
         }
     }
-    rmsnorm_kernel<<<1, 256, 0, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+    rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)H * 4, cudaMemcpyDeviceToDevice, st));
     if (logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed, 1, logits, nullptr, stream);

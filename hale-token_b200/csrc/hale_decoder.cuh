@@ -34,22 +34,28 @@ __global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32
 
 // The residual add x += delta (transformer.rs residual; delta nullable), then
 // RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
-// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA.
+// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA; x is
+// staged in shared memory by all threads so the one sequential chain runs
+// at the add's latency, not a global load's. Dynamic shared memory: n floats.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                float eps, int n, float* __restrict__ out) {
+    extern __shared__ float s_v[];
     __shared__ float s_scale;
-    if (delta) {
-        for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = fadd(x[i], delta[i]);
-        __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = delta ? fadd(x[i], delta[i]) : x[i];
+        if (delta) x[i] = v;
+        s_v[i] = v;
     }
+    __syncthreads();
     if (threadIdx.x == 0) {
         float s = -0.0f;
-        for (int i = 0; i < n; i++) s = fadd(s, fmul(x[i], x[i]));
+#pragma unroll 16
+        for (int i = 0; i < n; i++) s = fadd(s, fmul(s_v[i], s_v[i]));
         s_scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)n), eps)));
     }
     __syncthreads();
     const float scale = s_scale;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fmul(fmul(x[i], scale), w[i]);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fmul(fmul(s_v[i], scale), w[i]);
 }
 
 // Per head (one warp each; q heads, then k heads, then v heads): the in-place
@@ -75,10 +81,14 @@ __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd,
     float* x = qkv + (size_t)head * hd;
     const float* w = is_k ? k_norm : q_norm;
     if (w) {
+        extern __shared__ float s_h[];  // [hd]: the head, staged for lane 0's chain
+        for (int i = lane; i < hd; i += 32) s_h[i] = x[i];
+        __syncwarp();
         float scale = 0.0f;
         if (lane == 0) {
             float s = -0.0f;
-            for (int i = 0; i < hd; i++) s = fadd(s, fmul(x[i], x[i]));
+#pragma unroll 16
+            for (int i = 0; i < hd; i++) s = fadd(s, fmul(s_h[i], s_h[i]));
             scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)hd), eps)));
         }
         scale = __shfl_sync(0xffffffffu, scale, 0);
@@ -103,24 +113,37 @@ __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd,
 // Attention::forward for the token at pos (attention.rs:59-85), one CTA per
 // q head h (kv head h / (nh / nkv)): scores[t] = (sum_i q_i k_ti from -0) *
 // scale; softmax over t = 0..pos (activation.rs:11-21); ctx_i = sum_t
-// scores[t] v_ti from 0, t ascending. scores: [nh][max_len] scratch.
+// scores[t] v_ti from 0, t ascending. q sits in shared memory and each key
+// row is read 16 bytes at a time ahead of its chain; scores live in shared
+// memory when pos + 1 <= smem_scores (dynamic shared memory: hd +
+// smem_scores floats), else in the [nh][max_len] scratch.
 __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
                                                           const float* __restrict__ kcache,
                                                           const float* __restrict__ vcache,
                                                           const uint32_t* __restrict__ tp, int max_len,
                                                           float scale, float* __restrict__ scores,
-                                                          float* __restrict__ ctx) {
+                                                          float* __restrict__ ctx, int smem_scores) {
+    extern __shared__ __align__(16) float s_att[];  // [hd] q, then [smem_scores] scores
     __shared__ float s_red[32];
     __shared__ float s_bc[2];
     const int h = blockIdx.x, tid = threadIdx.x;
     const int seq = (int)tp[1] + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
-    const float* q = qkv + (size_t)h * hd;
-    float* sc = scores + (size_t)h * max_len;
+    float* s_q = s_att;
+    for (int i = tid; i < hd; i += blockDim.x) s_q[i] = qkv[(size_t)h * hd + i];
+    float* sc = seq <= smem_scores ? s_att + hd : scores + (size_t)h * max_len;
+    __syncthreads();
     float mx = -__int_as_float(0x7f800000);
     for (int t = tid; t < seq; t += blockDim.x) {
-        const float* key = kcache + (size_t)t * kvd + off;
+        const float4* key = reinterpret_cast<const float4*>(kcache + (size_t)t * kvd + off);
         float s = -0.0f;
-        for (int i = 0; i < hd; i++) s = fadd(s, fmul(q[i], key[i]));
+#pragma unroll 8
+        for (int i4 = 0; i4 < hd / 4; i4++) {
+            const float4 k4 = key[i4];
+            s = fadd(s, fmul(s_q[4 * i4], k4.x));
+            s = fadd(s, fmul(s_q[4 * i4 + 1], k4.y));
+            s = fadd(s, fmul(s_q[4 * i4 + 2], k4.z));
+            s = fadd(s, fmul(s_q[4 * i4 + 3], k4.w));
+        }
         s = fmul(s, scale);
         sc[t] = s;
         mx = fmaxf(mx, s);
