@@ -137,3 +137,25 @@ def test_decoder_rejects_positions_beyond_its_cache(ctx):
         dec.forward(om.cfg["vocab"], 0)
     assert ei.value.status == hale.E_INVALID_ARGUMENT
     dec.close()
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3-moe", "tiny-mixtral"])
+def test_checkpoint_loader_builds_a_bit_exact_decoder(ctx, name):
+    """load_decoder reads config.json + safetensors itself (config.rs,
+    safetensors.rs, arch.rs naming) and converts the experts to q4_0; its
+    logits equal the oracle's on the same checkpoint bit for bit."""
+    loader = importlib.import_module("hale-token_b200.loader")
+    d = os.path.join(GOLDEN, name)
+    with open(os.path.join(d, "expected.json")) as f:
+        tokens = json.load(f)["tokens"]
+    want = OM.OracleModel(d, expert_dtype=fmt.Q4_0).teacher_forced_logits(tokens)
+    dec, pool, cfg = loader.load_decoder(ctx, d, fmt.Q4_0, max_len=len(tokens))
+    logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device="cuda")
+    got = []
+    for i, t in enumerate(tokens):
+        dec.forward(t, i, logits)
+        got.append(logits.cpu().numpy().copy())
+    ctx.check()
+    got = np.stack(got)
+    assert (got.view(np.uint32) == want.view(np.uint32)).all()
+    dec.close()
