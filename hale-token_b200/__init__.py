@@ -51,6 +51,10 @@ class ExpertView(C.Structure):
     _fields_ = [("gate", P), ("up", P), ("down", P)]
 
 
+class CachePolicyStruct(C.Structure):
+    _fields_ = [("pinned", P), ("n_pinned", U64), ("lru_bytes", U64)]
+
+
 class MoeLayer(C.Structure):
     _fields_ = [("layer", U32), ("router", P), ("router_dtype", C.c_int), ("n_experts", U32),
                 ("top_k", U32), ("normalize_topk", I32)]
@@ -100,6 +104,8 @@ SIGNATURES = {
     "hale_pool_stats": (I32, [P, C.POINTER(CacheStats)]),
     "hale_pool_routing_counts": (I32, [P, P, U64]),
     "hale_pool_expert_bytes": (U64, [P]),
+    "hale_pool_create_tiered": (I32, [P, C.c_int, U32, U32, U32, U32, C.POINTER(CachePolicyStruct), C.POINTER(P)]),
+    "hale_pool_hbm_slots": (U64, [P]),
     "hale_moe_forward": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_forward_host": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_route": (I32, [P, C.POINTER(MoeLayer), U32, P, U32, P, P, P, P]),
@@ -260,13 +266,38 @@ class Matrix:
                       ptr(logits), _stream(stream))
 
 
-class Pool:
-    """hale_pool: HBM-resident ExpertProvider."""
+class CachePolicy:
+    """CachePolicy (src/expert/cache.rs:58-64): `pinned` keys (pool layer,
+    expert) kept in HBM for good, `lru_bytes` the HBM LRU tier's budget in
+    expert-record bytes."""
 
-    def __init__(self, ctx, dtype, hidden, inter, n_layers, n_experts):
+    def __init__(self, pinned=(), lru_bytes=0):
+        self.pinned = [(int(l), int(e)) for l, e in pinned]
+        self.lru_bytes = int(lru_bytes)
+
+    def __repr__(self):
+        return f"CachePolicy(pinned={len(self.pinned)} experts, lru_bytes={self.lru_bytes})"
+
+
+class Pool:
+    """hale_pool: the ExpertProvider of the MoE layers.
+
+    Without a policy every expert is HBM-resident. With a CachePolicy the
+    pool is tiered (ExpertCache, cache.rs:66-194): uploads fill a page-locked
+    host tier, HBM holds the pinned experts plus an LRU, and misses are
+    copied in as each forward's routes are resolved; results are identical.
+    """
+
+    def __init__(self, ctx, dtype, hidden, inter, n_layers, n_experts, policy=None):
         h = P()
-        ctx.call("hale_pool_create", ctx.h, dtype, hidden, inter, n_layers, n_experts, C.byref(h))
-        self.ctx, self.h = ctx, h
+        if policy is None:
+            ctx.call("hale_pool_create", ctx.h, dtype, hidden, inter, n_layers, n_experts, C.byref(h))
+        else:
+            keys = (ExpertKey * max(1, len(policy.pinned)))(*[ExpertKey(l, e) for l, e in policy.pinned])
+            pol = CachePolicyStruct(C.cast(keys, P), len(policy.pinned), policy.lru_bytes)
+            ctx.call("hale_pool_create_tiered", ctx.h, dtype, hidden, inter, n_layers, n_experts, C.byref(pol),
+                     C.byref(h))
+        self.ctx, self.h, self.policy = ctx, h, policy
         self.dtype, self.hidden, self.inter, self.n_layers, self.n_experts = (
             dtype, hidden, inter, n_layers, n_experts)
 
@@ -281,6 +312,11 @@ class Pool:
     @property
     def expert_bytes(self):
         return lib().hale_pool_expert_bytes(self.h)
+
+    @property
+    def hbm_slots(self):
+        """Experts HBM holds at once (n_layers * n_experts when resident)."""
+        return lib().hale_pool_hbm_slots(self.h)
 
     def upload(self, layer, expert, record, stream=None):
         on_dev = hasattr(record, "is_cuda") and record.is_cuda

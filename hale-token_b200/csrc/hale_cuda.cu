@@ -74,19 +74,105 @@ struct hale_matrix {
     bool lanes = false;  // float, lane-major layout (fgemv_lanes_kernel); rows_pad = rows rounded to 4
 };
 
+// LruCache (src/expert/lru.rs:40-160) over expert keys 0 .. n-1 (layer * E +
+// expert): a doubly linked recency list in index arrays, every entry of the
+// same weight (one expert record).
+struct KeyLru {
+    std::vector<int64_t> prev, next;
+    std::vector<uint8_t> in;
+    int64_t head = -1, tail = -1;
+    uint64_t used = 0, cap = 0, weight = 0;
+    size_t count = 0;
+
+    void init(size_t n, uint64_t cap_bytes, uint64_t w) {
+        prev.assign(n, -1);
+        next.assign(n, -1);
+        in.assign(n, 0);
+        head = tail = -1;
+        used = 0;
+        cap = cap_bytes;
+        weight = w;
+        count = 0;
+    }
+    void unlink(int64_t k) {
+        if (prev[k] >= 0) next[prev[k]] = next[k]; else head = next[k];
+        if (next[k] >= 0) prev[next[k]] = prev[k]; else tail = prev[k];
+        prev[k] = next[k] = -1;
+    }
+    void push_front(int64_t k) {
+        prev[k] = -1;
+        next[k] = head;
+        if (head >= 0) prev[head] = k;
+        head = k;
+        if (tail < 0) tail = k;
+    }
+    void remove(int64_t k) {
+        unlink(k);
+        in[k] = 0;
+        used -= weight;
+        count--;
+    }
+    // get(): a hit becomes the most recently used entry
+    bool get(int64_t k) {
+        if (!in[k]) return false;
+        unlink(k);
+        push_front(k);
+        return true;
+    }
+    // insert(): evicts from the tail until the entry fits; an entry heavier
+    // than the whole budget is not stored and comes back as evicted
+    void insert(int64_t k, std::vector<int64_t>& evicted) {
+        if (in[k]) remove(k);
+        if (weight > cap) {
+            evicted.push_back(k);
+            return;
+        }
+        while (used + weight > cap) {
+            const int64_t t = tail;
+            remove(t);
+            evicted.push_back(t);
+        }
+        push_front(k);
+        in[k] = 1;
+        used += weight;
+        count++;
+    }
+};
+
 struct hale_pool {
     hale_ctx* ctx;
     hale_dtype dtype;
     uint32_t H, I, L, E;
     size_t expert_stride;   // tiled bytes per expert
     size_t record_bytes;    // reference pack record bytes per expert
-    uint8_t* data = nullptr;
+    uint8_t* data = nullptr;                   // resident: [L * E] experts; tiered: [n_slots]
     uint8_t* staging = nullptr;
     unsigned long long* d_routing = nullptr;  // [L * E]
-    std::vector<uint8_t> resident;             // [L * E]
+    std::vector<uint8_t> resident;             // [L * E] uploaded
     std::vector<uint32_t> layer_resident;      // count per layer
     std::vector<uint64_t> host_routing;        // fetch() records
     hale_cache_stats stats{};
+    // tiered pools (hale_pool_create_tiered)
+    bool tiered = false;
+    uint8_t* host_tier = nullptr;          // [L * E] tiled experts, page-locked host memory
+    uint8_t* scratch = nullptr;            // one tiled expert (upload of an unpinned key)
+    uint32_t n_slots = 0;
+    std::vector<int32_t> slot_of;          // [L * E] HBM slot or -1
+    std::vector<int64_t> slot_key;         // [n_slots] key or -1
+    std::vector<int32_t> free_slots;
+    std::vector<uint8_t> pinned_key;       // [L * E]
+    KeyLru lru;
+    std::vector<int64_t> held;             // unpinned keys of the request in flight
+    std::vector<uint8_t> held_mark;        // [L * E]
+    int32_t* d_slot = nullptr;             // [L * E] slot table read by the expert kernels
+    int32_t* h_slot = nullptr;             // page-locked staging of one layer's row [E]
+    int32_t* h_routes = nullptr;           // page-locked read-back of a forward's routes
+    size_t h_routes_cap = 0;
+    cudaStream_t copy_st = nullptr;
+    cudaEvent_t ev_issue = nullptr, ev_t0 = nullptr, ev_t1 = nullptr;
+    cudaEvent_t ev_done = nullptr;         // after the last tiered forward's expert kernels
+    bool done_recorded = false;
+    bool timing_pending = false;
 };
 
 static hale_status fail(hale_ctx* ctx, hale_status st, const char* fmt, ...) {
@@ -662,10 +748,212 @@ extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_
 extern "C" void hale_pool_destroy(hale_pool* p) {
     if (!p) return;
     cudaSetDevice(p->ctx->device);
+    if (p->copy_st) cudaStreamSynchronize(p->copy_st);
     cudaFree(p->data);
     cudaFree(p->staging);
     cudaFree(p->d_routing);
+    cudaFree(p->scratch);
+    cudaFree(p->d_slot);
+    cudaFreeHost(p->host_tier);
+    cudaFreeHost(p->h_slot);
+    cudaFreeHost(p->h_routes);
+    if (p->copy_st) cudaStreamDestroy(p->copy_st);
+    if (p->ev_issue) cudaEventDestroy(p->ev_issue);
+    if (p->ev_t0) cudaEventDestroy(p->ev_t0);
+    if (p->ev_t1) cudaEventDestroy(p->ev_t1);
+    if (p->ev_done) cudaEventDestroy(p->ev_done);
     delete p;
+}
+
+extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
+                                               uint32_t n_layers, uint32_t n_experts, const hale_cache_policy* policy,
+                                               hale_pool** out) {
+    if (!ctx || !out || !policy) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_pool_create_tiered: NULL argument");
+    *out = nullptr;
+    if (policy->n_pinned && !policy->pinned)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "policy lists %llu pinned keys but no key array",
+                    (unsigned long long)policy->n_pinned);
+    if (!is_quant(dtype)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert pool dtype must be q8_0 or q4_0");
+    if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hidden (%u) and intermediate (%u) must be non-zero multiples of 32",
+                    hidden, inter);
+    if (n_layers == 0 || n_experts == 0 || n_experts > 256)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "need 1..256 experts and >= 1 layer (got %u, %u)", n_experts, n_layers);
+    const size_t nk = (size_t)n_layers * n_experts;
+    for (uint64_t i = 0; i < policy->n_pinned; i++)
+        if (policy->pinned[i].layer >= n_layers || policy->pinned[i].expert >= n_experts)
+            return fail(ctx, HALE_E_INVALID_ARGUMENT, "pinned expert L%uE%u out of range", policy->pinned[i].layer,
+                        policy->pinned[i].expert);
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_pool* p = new hale_pool();
+    p->ctx = ctx;
+    p->dtype = dtype;
+    p->H = hidden;
+    p->I = inter;
+    p->L = n_layers;
+    p->E = n_experts;
+    p->tiered = true;
+    p->expert_stride = 2 * tiled_bytes(dtype, inter, hidden) + tiled_bytes(dtype, hidden, inter);
+    p->record_bytes = 2 * (size_t)inter * hale_row_bytes(dtype, hidden) + (size_t)hidden * hale_row_bytes(dtype, inter);
+    p->pinned_key.assign(nk, 0);
+    uint64_t n_pinned = 0;
+    for (uint64_t i = 0; i < policy->n_pinned; i++) {
+        const size_t key = (size_t)policy->pinned[i].layer * n_experts + policy->pinned[i].expert;
+        if (!p->pinned_key[key]) n_pinned++;
+        p->pinned_key[key] = 1;
+    }
+    // slots: the pinned tier, the LRU at full budget, and one forward's
+    // distinct experts (at most one layer's E) held while the LRU evicts them
+    const uint64_t lru_cap = policy->lru_bytes / p->record_bytes;
+    p->n_slots = (uint32_t)std::min<uint64_t>(nk, n_pinned + lru_cap + n_experts);
+    const size_t dev_bytes = p->expert_stride * p->n_slots;
+    bool ok = cudaMalloc(&p->data, dev_bytes) == cudaSuccess &&
+              cudaMalloc(&p->staging, p->record_bytes) == cudaSuccess &&
+              cudaMalloc(&p->scratch, p->expert_stride) == cudaSuccess &&
+              cudaMalloc(&p->d_routing, nk * 8) == cudaSuccess && cudaMemset(p->d_routing, 0, nk * 8) == cudaSuccess &&
+              cudaMalloc(&p->d_slot, nk * 4) == cudaSuccess && cudaMemset(p->d_slot, 0xff, nk * 4) == cudaSuccess &&
+              cudaHostAlloc(&p->host_tier, p->expert_stride * nk, cudaHostAllocPortable) == cudaSuccess &&
+              cudaHostAlloc(&p->h_slot, (size_t)n_experts * 4, cudaHostAllocPortable) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&p->copy_st, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p->ev_issue, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreate(&p->ev_t0) == cudaSuccess && cudaEventCreate(&p->ev_t1) == cudaSuccess &&
+              cudaEventCreateWithFlags(&p->ev_done, cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        const size_t host_bytes = p->expert_stride * nk;
+        hale_pool_destroy(p);
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "cannot allocate a tiered pool (%zu bytes of HBM, %zu of host memory)",
+                    dev_bytes, host_bytes);
+    }
+    p->resident.assign(nk, 0);
+    p->layer_resident.assign(n_layers, 0);
+    p->host_routing.assign(nk, 0);
+    p->slot_of.assign(nk, -1);
+    p->slot_key.assign(p->n_slots, -1);
+    p->held_mark.assign(nk, 0);
+    p->lru.init(nk, policy->lru_bytes, p->record_bytes);
+    // pinned keys take the first slots for good
+    uint32_t next = 0;
+    for (size_t key = 0; key < nk; key++)
+        if (p->pinned_key[key]) {
+            p->slot_of[key] = (int32_t)next;
+            p->slot_key[next] = (int64_t)key;
+            next++;
+        }
+    for (int32_t sl = (int32_t)p->n_slots - 1; sl >= (int32_t)next; sl--) p->free_slots.push_back(sl);
+    // CacheStats at construction (cache.rs:96-103)
+    p->stats.pinned_experts = n_pinned;
+    p->stats.pinned_bytes = n_pinned * p->record_bytes;
+    p->stats.lru_capacity_bytes = policy->lru_bytes;
+    *out = p;
+    return HALE_OK;
+}
+
+extern "C" uint64_t hale_pool_hbm_slots(const hale_pool* p) {
+    return p ? (p->tiered ? p->n_slots : (uint64_t)p->L * p->E) : 0;
+}
+
+// ---- tier bookkeeping (host) ------------------------------------------------
+
+static void tier_free_slot(hale_pool* p, int64_t key) {
+    const int32_t sl = p->slot_of[key];
+    if (sl < 0) return;
+    p->slot_of[key] = -1;
+    p->slot_key[sl] = -1;
+    p->free_slots.push_back(sl);
+}
+
+// Folds the device-timed duration of the last batch of tier loads into
+// load_seconds once it has completed.
+static void tier_collect_timing(hale_pool* p) {
+    if (!p->timing_pending) return;
+    float ms = 0.f;
+    if (cudaEventSynchronize(p->ev_t1) == cudaSuccess && cudaEventElapsedTime(&ms, p->ev_t0, p->ev_t1) == cudaSuccess)
+        p->stats.load_seconds += ms * 1e-3;
+    cudaGetLastError();
+    p->timing_pending = false;
+}
+
+// The previous request's kernels have completed (the caller synchronised):
+// slots of its experts that no tier keeps become free.
+static void tier_release(hale_pool* p) {
+    if (p->done_recorded) {
+        cudaEventSynchronize(p->ev_done);  // the previous forward may have run on another stream
+        p->done_recorded = false;
+    }
+    for (int64_t key : p->held) {
+        p->held_mark[key] = 0;
+        if (!p->pinned_key[key] && !p->lru.in[key]) tier_free_slot(p, key);
+    }
+    p->held.clear();
+    tier_collect_timing(p);
+}
+
+// ExpertCache::fetch (cache.rs:124-194) for one request: routing recorded,
+// pass 1 serves pinned and LRU hits (a hit refreshes recency), pass 2 loads
+// the misses in request order and inserts them into the LRU. Every expert of
+// the request keeps its slot until the next release, even if a later insert
+// evicts it from the LRU. A miss whose bytes are still in a held slot needs
+// no copy (it counts as a miss all the same). Copies to issue go to `loads`.
+static hale_status tier_request(hale_pool* p, const int64_t* keys, size_t n,
+                                std::vector<std::pair<int32_t, int64_t>>& loads) {
+    for (size_t i = 0; i < n; i++) p->host_routing[keys[i]]++;
+    uint64_t pinned_hits = 0, lru_hits = 0;
+    std::vector<int64_t> missing;
+    for (size_t i = 0; i < n; i++) {
+        const int64_t key = keys[i];
+        if (p->pinned_key[key]) {
+            pinned_hits++;
+            continue;
+        }
+        if (!p->held_mark[key]) {
+            p->held_mark[key] = 1;
+            p->held.push_back(key);
+        }
+        if (p->lru.get(key)) lru_hits++;
+        else missing.push_back(key);
+    }
+    std::vector<int64_t> evicted;
+    for (int64_t key : missing) {
+        if (p->slot_of[key] < 0) {
+            if (p->free_slots.empty())
+                return fail(p->ctx, HALE_E_OUT_OF_MEMORY, "tiered pool ran out of HBM slots (%u)", p->n_slots);
+            const int32_t sl = p->free_slots.back();
+            p->free_slots.pop_back();
+            p->slot_of[key] = sl;
+            p->slot_key[sl] = key;
+            loads.emplace_back(sl, key);
+        }
+        evicted.clear();
+        p->lru.insert(key, evicted);
+        for (int64_t ev : evicted)
+            if (!p->held_mark[ev]) tier_free_slot(p, ev);
+    }
+    p->stats.pinned_hits += pinned_hits;
+    p->stats.lru_hits += lru_hits;
+    p->stats.misses += missing.size();
+    p->stats.bytes_loaded += (uint64_t)missing.size() * p->record_bytes;
+    p->stats.lru_experts = p->lru.count;
+    p->stats.lru_bytes = p->lru.used;
+    return HALE_OK;
+}
+
+// Host tier -> HBM slots on the copy stream, after the work already queued on
+// `st`; `st` waits for the copies.
+static hale_status tier_issue(hale_pool* p, const std::vector<std::pair<int32_t, int64_t>>& loads, cudaStream_t st) {
+    hale_ctx* ctx = p->ctx;
+    if (loads.empty()) return HALE_OK;
+    CUDA_TRY(ctx, cudaEventRecord(p->ev_issue, st));
+    CUDA_TRY(ctx, cudaStreamWaitEvent(p->copy_st, p->ev_issue, 0));
+    CUDA_TRY(ctx, cudaEventRecord(p->ev_t0, p->copy_st));
+    for (const auto& ld : loads)
+        CUDA_TRY(ctx, cudaMemcpyAsync(p->data + (size_t)ld.first * p->expert_stride,
+                                      p->host_tier + (size_t)ld.second * p->expert_stride, p->expert_stride,
+                                      cudaMemcpyHostToDevice, p->copy_st));
+    CUDA_TRY(ctx, cudaEventRecord(p->ev_t1, p->copy_st));
+    CUDA_TRY(ctx, cudaStreamWaitEvent(st, p->ev_t1, 0));
+    p->timing_pending = true;
+    return HALE_OK;
 }
 
 extern "C" uint64_t hale_pool_expert_bytes(const hale_pool* p) { return p ? p->record_bytes : 0; }
@@ -688,15 +976,34 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
         CUDA_TRY(ctx, cudaMemcpyAsync(p->staging, record, record_bytes, cudaMemcpyHostToDevice, st));
         src = p->staging;
     }
-    uint8_t* dst = p->data + ((size_t)layer * p->E + expert) * p->expert_stride;
+    const size_t i = (size_t)layer * p->E + expert;
+    // tiered: a pinned key is tiled straight into its slot, any other through
+    // the scratch expert; both then land in the host tier
+    uint8_t* dst = !p->tiered ? p->data + i * p->expert_stride
+                              : (p->pinned_key[i] ? p->data + (size_t)p->slot_of[i] * p->expert_stride : p->scratch);
     size_t proj = (size_t)p->I * hale_row_bytes(p->dtype, p->H);
     size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
     hale_status r;
     if ((r = launch_repack(ctx, p->dtype, src, dst, p->I, p->H, st))) return r;
     if ((r = launch_repack(ctx, p->dtype, src + proj, dst + gu_tiled, p->I, p->H, st))) return r;
     if ((r = launch_repack(ctx, p->dtype, src + 2 * proj, dst + 2 * gu_tiled, p->H, p->I, st))) return r;
+    if (p->tiered) {
+        CUDA_TRY(ctx, cudaMemcpyAsync(p->host_tier + i * p->expert_stride, dst, p->expert_stride,
+                                      cudaMemcpyDeviceToHost, st));
+        if (!p->pinned_key[i] && p->slot_of[i] >= 0)
+            CUDA_TRY(ctx, cudaMemcpyAsync(p->data + (size_t)p->slot_of[i] * p->expert_stride, dst, p->expert_stride,
+                                          cudaMemcpyDeviceToDevice, st));
+    }
     CUDA_TRY(ctx, cudaStreamSynchronize(st));
-    size_t i = (size_t)layer * p->E + expert;
+    if (p->tiered) {
+        // the cold tier is filled before serving; CacheStats counts only the
+        // loads of fetch() (cache.rs:185-188)
+        if (!p->resident[i]) {
+            p->resident[i] = 1;
+            p->layer_resident[layer]++;
+        }
+        return HALE_OK;
+    }
     if (!p->resident[i]) {
         p->resident[i] = 1;
         p->layer_resident[layer]++;
@@ -712,6 +1019,34 @@ extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys
     if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: pool is NULL");
     hale_ctx* ctx = p->ctx;
     if (n && (!keys || !out)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: NULL buffer");
+    if (p->tiered) {
+        std::vector<int64_t> ks(n);
+        for (uint64_t i = 0; i < n; i++) {
+            if (keys[i].layer >= p->L || keys[i].expert >= p->E)
+                return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u out of range", keys[i].layer, keys[i].expert);
+            ks[i] = (int64_t)keys[i].layer * p->E + keys[i].expert;
+            if (!p->resident[ks[i]])
+                return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u was never uploaded", keys[i].layer,
+                            keys[i].expert);
+        }
+        CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+        // the slots of the previous request may still be read by queued work
+        CUDA_TRY(ctx, cudaDeviceSynchronize());
+        tier_release(p);
+        std::vector<std::pair<int32_t, int64_t>> loads;
+        hale_status r = tier_request(p, ks.data(), n, loads);
+        if (r) return r;
+        if ((r = tier_issue(p, loads, p->copy_st))) return r;
+        CUDA_TRY(ctx, cudaStreamSynchronize(p->copy_st));
+        const size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
+        for (uint64_t i = 0; i < n; i++) {
+            const uint8_t* base = p->data + (size_t)p->slot_of[ks[i]] * p->expert_stride;
+            out[i].gate = base;
+            out[i].up = base + gu_tiled;
+            out[i].down = base + 2 * gu_tiled;
+        }
+        return HALE_OK;
+    }
     // routing is recorded before lookup, like ExpertCache::fetch (cache.rs:125-128)
     for (uint64_t i = 0; i < n; i++)
         if (keys[i].layer < p->L && keys[i].expert < p->E) p->host_routing[(size_t)keys[i].layer * p->E + keys[i].expert]++;
@@ -757,6 +1092,12 @@ extern "C" hale_status hale_pool_stats(hale_pool* p, hale_cache_stats* out) {
     CUDA_TRY(p->ctx, cudaSetDevice(p->ctx->device));
     CUDA_TRY(p->ctx, cudaDeviceSynchronize());
     CUDA_TRY(p->ctx, cudaMemcpy(dev.data(), p->d_routing, total * 8, cudaMemcpyDeviceToHost));
+    if (p->tiered) {
+        // routes were counted on the host as they were resolved
+        tier_collect_timing(p);
+        *out = p->stats;
+        return HALE_OK;
+    }
     *out = p->stats;
     for (size_t i = 0; i < total; i++) out->pinned_hits += dev[i];
     return HALE_OK;
@@ -928,6 +1269,44 @@ static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_ac
 static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, uint32_t M, int k, int E,
                                   cudaStream_t st);
 
+// A tiered pool's forward: read the routes back (the calling thread waits for
+// the router), resolve them one token at a time in top-k order, copy the
+// misses into HBM slots on the side stream and publish this layer's slot row
+// for the expert kernels, which `st` orders after the copies.
+static hale_status tier_forward(hale_pool* p, uint32_t layer, const int* d_routes, uint32_t M, int k,
+                                cudaStream_t st) {
+    hale_ctx* ctx = p->ctx;
+    const size_t n = (size_t)M * k;
+    if (n > p->h_routes_cap) {
+        cudaFreeHost(p->h_routes);
+        p->h_routes = nullptr;
+        p->h_routes_cap = 0;
+        CUDA_TRY(ctx, cudaHostAlloc(&p->h_routes, n * 4, cudaHostAllocPortable));
+        p->h_routes_cap = n;
+    }
+    CUDA_TRY(ctx, cudaMemcpyAsync(p->h_routes, d_routes, n * 4, cudaMemcpyDeviceToHost, st));
+    // also completes every earlier forward's kernels, so held slots can go
+    CUDA_TRY(ctx, cudaStreamSynchronize(st));
+    tier_release(p);
+    std::vector<std::pair<int32_t, int64_t>> loads;
+    std::vector<int64_t> keys(k);
+    for (uint32_t t = 0; t < M; t++) {
+        for (int j = 0; j < k; j++) {
+            const int e = p->h_routes[(size_t)t * k + j];
+            if (e < 0 || (uint32_t)e >= p->E) return fail(ctx, HALE_E_DEVICE_CHECK, "route %d out of range", e);
+            keys[j] = (int64_t)layer * p->E + e;
+        }
+        hale_status r = tier_request(p, keys.data(), (size_t)k, loads);
+        if (r) return r;
+    }
+    hale_status r = tier_issue(p, loads, st);
+    if (r) return r;
+    for (uint32_t e = 0; e < p->E; e++) p->h_slot[e] = p->slot_of[(size_t)layer * p->E + e];
+    CUDA_TRY(ctx, cudaMemcpyAsync(p->d_slot + (size_t)layer * p->E, p->h_slot, (size_t)p->E * 4,
+                                  cudaMemcpyHostToDevice, st));
+    return HALE_OK;
+}
+
 extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
                                         uint32_t M, float* out, int32_t* topk_idx, float* topk_w, void* stream) {
     if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL ctx or pool");
@@ -948,12 +1327,20 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     MoeLayout L;
     if ((r = ensure_moe_ws(ctx, (int)M, E, k, H, I, stream, &L))) return r;
     cudaStream_t st = S(stream);
+    if (p->tiered && stream_capturing(stream))
+        return fail(ctx, HALE_E_UNSUPPORTED, "a tiered pool resolves routes on the host; its forward cannot be captured");
     if ((r = launch_router(ctx, ly, p->H, x, M, L, true, topk_idx, topk_w, nullptr,
-                           p->d_routing + (size_t)ly->layer * p->E, st)))
+                           p->tiered ? nullptr : p->d_routing + (size_t)ly->layer * p->E, st)))
         return r;
     uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
     ExpertArgs a{};
-    a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+    if (p->tiered) {
+        if ((r = tier_forward(p, ly->layer, reinterpret_cast<const int*>(ws + L.topk_idx), M, k, st))) return r;
+        a.experts = p->data;
+        a.slot = p->d_slot + (size_t)ly->layer * p->E;
+    } else {
+        a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+    }
     a.expert_stride = p->expert_stride;
     a.H = H;
     a.I = I;
@@ -972,7 +1359,12 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
     a.out = out;
     a.err = ctx->d_err;
-    return launch_experts(ctx, p->dtype, a, M, k, E, st);
+    r = launch_experts(ctx, p->dtype, a, M, k, E, st);
+    if (!r && p->tiered) {
+        CUDA_TRY(ctx, cudaEventRecord(p->ev_done, st));
+        p->done_recorded = true;
+    }
+    return r;
 }
 
 // The expert kernels over the routes in a (expert lists built, activations
@@ -1088,6 +1480,7 @@ extern "C" hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* p, uint32_t lay
                                        uint32_t n, float* y, void* stream) {
     if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ep_experts: NULL ctx or pool");
     if (p->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "pool belongs to another context");
+    if (p->tiered) return fail(ctx, HALE_E_UNSUPPORTED, "hale_ep_experts needs an HBM-resident pool");
     if (layer >= p->L) return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u has no experts in the pool", layer);
     if (p->layer_resident[layer] != p->E)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: only %u of %u experts are resident", layer,
@@ -1302,6 +1695,8 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
     hale_decoder* d = new hale_decoder();
     d->ctx = ctx;
     d->pool = pool;
+    // a tiered pool resolves each MoE layer's routes on the host mid-step
+    d->no_graph = pool && pool->tiered;
     d->H = H;
     d->L = ds->n_layers;
     d->nh = nh;

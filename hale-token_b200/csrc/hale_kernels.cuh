@@ -874,6 +874,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 struct ExpertArgs {
     const uint8_t* experts;   // layer base: E experts, each [gate tiles][up tiles][down tiles]
     size_t expert_stride;     // bytes per expert
+    const int* slot;          // nullable [E]: expert e lives at experts + slot[e] * stride (tiered pools)
     int H, I, k, M;
     const int* elist_off;     // [E + 1]: routes of expert e are slots off[e] .. off[e+1]-1
     const int* elist;         // [M * k]: route id (token * k + s) of each slot
@@ -890,6 +891,12 @@ struct ExpertArgs {
     int S1, S2;               // ring depths of the gate/up and down kernels
     uint32_t* err;
 };
+
+// Tiled weights of expert e: its own position in a resident pool's layer, or
+// the HBM slot a tiered pool placed it in for this forward.
+__device__ __forceinline__ const uint8_t* expert_base(const ExpertArgs& a, int e) {
+    return a.experts + (size_t)(a.slot ? __ldg(a.slot + e) : e) * a.expert_stride;
+}
 
 // Phase 1: one CTA per (active expert, RT consecutive 32-row tiles of the
 // intermediate dimension). Warps 0..RT-1 take the gate tiles, RT..2RT-1 the
@@ -922,7 +929,7 @@ __global__ void __launch_bounds__(64 * RT) expert_gate_up_kernel(ExpertArgs a) {
     xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
                 bars + W * a.S1);
     const size_t tile_bytes = (size_t)nbh * REC;
-    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)(m * TI + tile) * tile_bytes;
+    const uint8_t* gtile = expert_base(a, e) + (size_t)(m * TI + tile) * tile_bytes;
     const int* routes = a.elist + beg;
     const int k = a.k;
     const bool live = tile < TI;
@@ -986,7 +993,7 @@ __global__ void __launch_bounds__(128) expert_down_kernel(ExpertArgs a) {
     xstage_init(xs, reinterpret_cast<int8_t*>(smem + P.xq_off), reinterpret_cast<int2*>(smem + P.xa_off),
                 bars + 4 * a.S2);
     const size_t gu_tile = (size_t)nbh * REC, d_tile = (size_t)nbi * REC;
-    const uint8_t* gtile = a.experts + (size_t)e * a.expert_stride + (size_t)2 * TI * gu_tile + (size_t)tile * d_tile;
+    const uint8_t* gtile = expert_base(a, e) + (size_t)2 * TI * gu_tile + (size_t)tile * d_tile;
     const int* routes = a.elist + beg;
     const int k = a.k;
     for (int base = 0; base < T; base += kPassRows) {

@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kPsThreads, 2) expert_gate_up_ps_kernel(Expert
         U.e = a.active[ai];
         U.beg = a.elist_off[U.e];
         U.T = a.elist_off[U.e + 1] - U.beg;
-        const uint8_t* eb = a.experts + (size_t)U.e * a.expert_stride;
+        const uint8_t* eb = expert_base(a, U.e);
         U.tiles[0] = eb + (size_t)(2 * jj) * tile_bytes;
         U.tiles[1] = eb + (size_t)(2 * jj + 1) * tile_bytes;
         U.tiles[2] = eb + (size_t)(TI + 2 * jj) * tile_bytes;
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kPsThreads, 2) expert_down_ps_kernel(ExpertArg
         U.e = a.active[ai];
         U.beg = a.elist_off[U.e];
         U.T = a.elist_off[U.e + 1] - U.beg;
-        const uint8_t* db = a.experts + (size_t)U.e * a.expert_stride + (size_t)2 * TI * gu_tile;
+        const uint8_t* db = expert_base(a, U.e) + (size_t)2 * TI * gu_tile;
         for (int w = 0; w < 4; w++) U.tiles[w] = db + (size_t)(4 * grp + w) * d_tile;
         U.tile0 = 4 * grp;
         return U;

@@ -104,6 +104,30 @@ def encode(dtype, values):
     raise ValueError(f"unknown dtype {dtype}")
 
 
+def decode(dtype, rows, cols):
+    """decode_row per row (quant.rs:236-269): [rows, row_bytes] uint8 -> f32
+    [rows, cols]; quantized values are scale * q in f32."""
+    r = np.ascontiguousarray(rows, dtype=np.uint8)
+    r = r.reshape(-1, row_bytes(dtype, cols))
+    n = r.shape[0]
+    if dtype == F32:
+        return r.view(np.float32).reshape(n, cols).copy()
+    if dtype == F16:
+        return r.view(np.float16).astype(np.float32).reshape(n, cols)
+    if dtype == BF16:
+        return (r.view(np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(n, cols)
+    b = r.reshape(n, cols // QK, BLOCK_BYTES[dtype])
+    scale = b[..., :2].copy().view(np.float16).astype(np.float32)  # [n, nb, 1]
+    if dtype == Q8_0:
+        q = b[..., 2:].view(np.int8).astype(np.float32)
+    elif dtype == Q4_0:
+        nib = b[..., 2:]
+        q = np.concatenate([(nib & 0x0F), (nib >> 4)], axis=-1).astype(np.float32) - np.float32(8.0)
+    else:
+        raise ValueError(f"unknown dtype {dtype}")
+    return (scale * q).astype(np.float32).reshape(n, cols)
+
+
 def pack_record(gate, up, down):
     """One expert-pack record: gate | up | down encoded rows (pack.rs:15-16)."""
     return np.concatenate([np.ascontiguousarray(m, dtype=np.uint8).reshape(-1) for m in (gate, up, down)])

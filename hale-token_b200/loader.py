@@ -328,18 +328,37 @@ def write_safetensors(path, tensors):
 
 
 class ModelWeights:
-    """A checkpoint's tensors arranged for hale_decoder (the reference's
-    Transformer::load, transformer.rs:58-150): per-layer norms as f32,
-    projections, routers, dense MLPs, embedding and head as stored
-    (dtype, rows, cols, bytes); routed experts produced on demand as pack
-    records re-encoded to expert_dtype (MoE layer j = j-th MoE layer)."""
+    """A model directory's tensors arranged for hale_decoder (the reference's
+    Transformer::load, transformer.rs:58-150, and Engine::load's expert
+    source choice, engine.rs:78-86): per-layer norms as f32; projections,
+    routers, dense MLPs, embedding and head as stored (dtype, rows, cols,
+    bytes); routed experts as pack records (MoE layer j = j-th MoE layer),
+    read from experts.hpk when the directory holds one (a converted model),
+    else re-encoded from the checkpoint's tensors to expert_dtype.
 
-    def __init__(self, directory, expert_dtype=fmt.Q8_0):
+    expert_dtype: the pool's format (q8_0 / q4_0). Default: the pack's dtype,
+    or q8_0 for a plain checkpoint. A pack in another dtype is re-encoded
+    from its decoded values (matrix.rs:103-109)."""
+
+    def __init__(self, directory, expert_dtype=None):
+        pack = importlib.import_module("hale-token_b200.pack")
         cfg = self.config = ModelConfig.from_dir(directory)
         ck = self.checkpoint = Checkpoint.open_dir(directory)
         names = self.naming = Naming(cfg.architecture)
-        self.expert_dtype = expert_dtype
         self.moe_layers = [l for l in range(cfg.num_layers) if cfg.is_moe_layer(l)]
+        pack_path = os.path.join(directory, pack.PACK_FILE_NAME)
+        self.pack = pack.PackSource(pack_path) if os.path.exists(pack_path) else None
+        if self.pack is not None:
+            hd = self.pack.header
+            got = (hd.hidden_size, hd.intermediate_size, hd.num_experts, hd.moe_layers)
+            want = (cfg.hidden_size, cfg.expert_intermediate_size, cfg.num_experts, self.moe_layers)
+            if got != want:
+                raise LoadError(f"{pack_path}: pack shape {got} does not match config.json {want}")
+            self.expert_dtype = hd.dtype if expert_dtype is None else expert_dtype
+        else:
+            self.expert_dtype = fmt.Q8_0 if expert_dtype is None else expert_dtype
+        if self.expert_dtype not in (fmt.Q8_0, fmt.Q4_0):
+            raise LoadError("the expert pool stores q8_0 or q4_0 experts; pass expert_dtype to convert")
         self.layers = []
         for l in range(cfg.num_layers):
             L = dict(input_norm=ck.vector(names.input_norm(l)), post_norm=ck.vector(names.post_attention_norm(l)),
@@ -350,10 +369,11 @@ class ModelWeights:
                 L["k_norm"] = ck.vector(names.attention(l, "k_norm"))
             if cfg.is_moe_layer(l):
                 L["router"] = ck.matrix(names.router(l))
-                for e in range(cfg.num_experts):
-                    for p in ("gate", "up", "down"):
-                        if not ck.contains(names.expert(l, e, p)):
-                            raise MissingTensor(f"missing tensor `{names.expert(l, e, p)}`")
+                if self.pack is None:
+                    for e in range(cfg.num_experts):
+                        for p in ("gate", "up", "down"):
+                            if not ck.contains(names.expert(l, e, p)):
+                                raise MissingTensor(f"missing tensor `{names.expert(l, e, p)}`")
             else:
                 for p in ("gate", "up", "down"):
                     L[f"dense_{p}"] = ck.matrix(names.dense_mlp(l, p))
@@ -367,11 +387,27 @@ class ModelWeights:
                          n_experts=cfg.num_experts, top_k=cfg.experts_per_token,
                          normalize_topk=cfg.normalize_topk, eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta)
 
+    @property
+    def record_bytes(self):
+        c, d = self.config, self.expert_dtype
+        return 2 * c.expert_intermediate_size * fmt.row_bytes(d, c.hidden_size) + \
+            c.hidden_size * fmt.row_bytes(d, c.expert_intermediate_size)
+
+    def _values(self, l, e):
+        """gate, up, down of expert e of model layer l as f32."""
+        if self.pack is None:
+            return [self.checkpoint.f32(self.naming.expert(l, e, p)) for p in ("gate", "up", "down")]
+        hd = self.pack.header
+        parts = self.pack.split(self.pack.record(l, e))
+        shapes = [(hd.intermediate_size, hd.hidden_size)] * 2 + [(hd.hidden_size, hd.intermediate_size)]
+        return [fmt.decode(hd.dtype, m, sh[1]).reshape(sh) for m, sh in zip(parts, shapes)]
+
     def expert_record(self, j, e):
         """Expert e of MoE layer j as one pack record gate | up | down."""
         l = self.moe_layers[j]
-        enc = [fmt.encode(self.expert_dtype, self.checkpoint.f32(self.naming.expert(l, e, p)))
-               for p in ("gate", "up", "down")]
+        if self.pack is not None and self.pack.header.dtype == self.expert_dtype:
+            return np.asarray(self.pack.record(l, e))
+        enc = [fmt.encode(self.expert_dtype, v) for v in self._values(l, e)]
         for m, p in zip(enc, ("gate", "up", "down")):
             want = (self.config.expert_intermediate_size, self.config.hidden_size) if p != "down" else \
                 (self.config.hidden_size, self.config.expert_intermediate_size)
@@ -380,17 +416,74 @@ class ModelWeights:
         return fmt.pack_record(*enc)
 
 
-def load_decoder(ctx, directory, expert_dtype=fmt.Q8_0, max_len=None):
-    """Builds (decoder, pool, config) from a checkpoint directory: every
-    routed expert re-encoded to expert_dtype and uploaded into an HBM pool;
-    dense weights as stored. max_len: KV-cache positions (default the
-    config's max_position_embeddings)."""
+def split_budget(experts_in_ram, total_experts, per_token_experts):
+    """planner::split_budget (src/expert/planner.rs:253-267) -> (pinned, lru)
+    expert counts: below twice one token's working set an LRU only thrashes
+    on the cyclic layer walk, so every slot is pinned."""
+    n = min(experts_in_ram, total_experts)
+    if n == total_experts or n < 2 * per_token_experts:
+        return n, 0
+    return n // 2, n - n // 2
+
+
+def hottest(counts, n):
+    """RoutingStats::hottest (src/expert/stats.rs:77-95): the n most routed
+    (layer, expert) keys of a [layers, experts] count array, hotter first,
+    ties by index; never-routed keys are left out."""
+    flat = np.asarray(counts, dtype=np.uint64).reshape(-1)
+    E = np.asarray(counts).shape[-1]
+    used = np.flatnonzero(flat)
+    order = sorted(used.tolist(), key=lambda i: (-int(flat[i]), i))[:n]
+    return [(i // E, i % E) for i in order]
+
+
+def choose_pinned(counts, n_layers, n_experts, n):
+    """choose_pinned (src/engine.rs:266-292): the hottest keys of past runs
+    first, then keys expert-major across the layers so every layer gets the
+    same share."""
+    if n >= n_layers * n_experts:
+        return [(l, e) for l in range(n_layers) for e in range(n_experts)]
+    chosen = hottest(counts, n) if counts is not None else []
+    taken = set(chosen)
+    for e in range(n_experts):
+        for l in range(n_layers):
+            if len(chosen) == n:
+                return chosen
+            if (l, e) not in taken:
+                taken.add((l, e))
+                chosen.append((l, e))
+    return chosen
+
+
+def cache_policy(config, record_bytes, budget_bytes, routing_counts=None):
+    """cache_policy (src/engine.rs:294-318) for pool layers = MoE ordinals:
+    an HBM budget for experts turned into pinned keys plus an LRU budget."""
+    hale_mod = hale
+    n_moe = config.num_moe_layers()
+    total = n_moe * config.num_experts
+    per_token = n_moe * config.experts_per_token
+    pinned, lru = split_budget(budget_bytes // max(record_bytes, 1), total, per_token)
+    keys = choose_pinned(routing_counts, n_moe, config.num_experts, pinned)
+    return hale_mod.CachePolicy(keys, lru * record_bytes)
+
+
+def load_decoder(ctx, directory, expert_dtype=None, max_len=None, policy=None, expert_hbm_bytes=None,
+                 routing_counts=None):
+    """Builds (decoder, pool, config) from a model directory: a Hugging Face
+    checkpoint (config.json + safetensors) or a converted one (config.json,
+    dense.safetensors, experts.hpk). Dense weights as stored; experts into an
+    HBM-resident pool, or a tiered one when `policy` (a CachePolicy) or
+    `expert_hbm_bytes` (planned like the reference's RAM budget, hottest
+    experts of `routing_counts` pinned first) is given. max_len: KV-cache
+    positions (default the config's max_position_embeddings)."""
     w = ModelWeights(directory, expert_dtype)
     cfg = w.config
+    if policy is None and expert_hbm_bytes is not None:
+        policy = cache_policy(cfg, w.record_bytes, expert_hbm_bytes, routing_counts)
     pool = None
     if w.moe_layers:
-        pool = hale.Pool(ctx, expert_dtype, cfg.hidden_size, cfg.expert_intermediate_size, len(w.moe_layers),
-                         cfg.num_experts)
+        pool = hale.Pool(ctx, w.expert_dtype, cfg.hidden_size, cfg.expert_intermediate_size, len(w.moe_layers),
+                         cfg.num_experts, policy=policy)
         for j in range(len(w.moe_layers)):
             for e in range(cfg.num_experts):
                 pool.upload(j, e, w.expert_record(j, e))

@@ -193,6 +193,36 @@ HALE_API hale_status hale_pool_routing_counts(hale_pool* pool, uint64_t* counts,
 /* Bytes of one expert record (ExpertSource::expert_bytes). */
 HALE_API uint64_t hale_pool_expert_bytes(const hale_pool* pool);
 
+/* ---- tiered expert pool: ExpertCache (src/expert/cache.rs:66-194) --------- */
+
+/* CachePolicy (cache.rs:58-64): keys kept in HBM for the pool's life (tier 0)
+ * and the byte budget of the HBM LRU tier (tier 1), counted in record bytes
+ * like LruCache's weights (cache.rs:178, lru.rs:97-125). */
+typedef struct {
+    const hale_expert_key* pinned;
+    uint64_t n_pinned;
+    uint64_t lru_bytes;
+} hale_cache_policy;
+
+/* A pool for experts that do not all fit in HBM. hale_pool_upload_expert
+ * fills the cold tier: every expert's tiled bytes in pinned host memory (the
+ * pack read once into page-locked RAM; PackExpertSource, pack.rs:211-271, is
+ * the reference's tier 2). HBM holds the policy's pinned experts, an LRU of
+ * the others, and one forward's working set. hale_moe_forward then reads the
+ * routes back, resolves them through the tiers with ExpertCache::fetch's
+ * counters (one request per token, top-k order) and brings misses in with
+ * asynchronous host-to-device copies on a side stream before the expert
+ * kernels, which read every expert through a slot table: results are
+ * identical to a resident pool's. Tiered forwards block the calling thread
+ * until the routes are known and cannot be captured into a CUDA graph.
+ * Device views from hale_pool_fetch stay valid until the next fetch or
+ * forward on the pool. */
+HALE_API hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
+                                    uint32_t n_layers, uint32_t n_experts, const hale_cache_policy* policy,
+                                    hale_pool** out);
+/* Number of HBM expert slots of a pool (n_layers * n_experts when resident). */
+HALE_API uint64_t hale_pool_hbm_slots(const hale_pool* pool);
+
 /* ---- the MoE layer (src/model/moe.rs:25-70) ---------------------------- */
 
 /* Router description for MoeLayer (moe.rs:25-32): `router` is the [E, H]
