@@ -45,9 +45,11 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel measurement at N > 1")
     p.add_argument("--decode", action="store_true",
-                   help="whole-model decode tok/s at batch 1 (BASELINE config 2 shapes) instead of the layer")
+                   help="whole-model decode tok/s (BASELINE config 2 shapes; --batch sequences) instead of the layer")
     p.add_argument("--layers", type=int, default=48, help="--decode: decoder layers")
     p.add_argument("--prompt", type=int, default=64, help="--decode: positions filled before timing")
+    p.add_argument("--batch", type=int, default=1,
+                   help="--decode: sequences decoded together (one row each per hale_decoder_step)")
     return p.parse_args()
 
 
@@ -197,15 +199,17 @@ def measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush,
 
 
 def run_decode(args):
-    """Whole-model decode at batch 1 with BASELINE config 2's shapes
-    (Qwen3-30B-A3B: hidden 2048, 32 q / 4 kv heads of 128, q/k norms, 128
-    experts top-8 of intermediate 768 in q4_0, vocab 151936, bf16 attention,
-    embedding and lm_head). Synthetic weights: one layer's 128 expert records
-    uploaded to every layer (each layer its own copy in HBM), random bf16
-    dense weights N(0, 0.02), norms 1.0. A step is one hale_decoder_forward
-    (token -> logits); `prompt` positions are filled first, then `steps`
-    timed with CUDA events (device time, no L2 flush: the per-token working
-    set is ~3.5 GB)."""
+    """Whole-model decode with BASELINE config 2's shapes (Qwen3-30B-A3B:
+    hidden 2048, 32 q / 4 kv heads of 128, q/k norms, 128 experts top-8 of
+    intermediate 768 in q4_0, vocab 151936, bf16 attention, embedding and
+    lm_head). Synthetic weights: one layer's 128 expert records uploaded to
+    every layer (each layer its own copy in HBM), random bf16 dense weights
+    N(0, 0.02), norms 1.0. Each of `batch` sequences first prefills a
+    `prompt`-token random prompt in batched steps (timed: prefill tok/s);
+    then a step is one token of every sequence -> logits for each, timed
+    with CUDA events (device time, no L2 flush: the per-step working set is
+    3.5 GB and up). Batch 1 steps go through hale_decoder_forward (one
+    captured CUDA graph replayed), batch B through hale_decoder_step."""
     import importlib
 
     import torch
@@ -214,6 +218,7 @@ def run_decode(args):
     torch.cuda.set_device(0)
     ctx = hale.Context(0)
     L, Hd, nh, nkv, hd, V = args.layers, 2048, 32, 4, 128, 151936
+    B = max(1, args.batch)
     rng = np.random.default_rng(SEED)
 
     def bf16(rows, cols):
@@ -237,20 +242,44 @@ def run_decode(args):
     dims = dict(hidden=Hd, n_layers=L, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, n_experts=E, top_k=K_TOP,
                 normalize_topk=1, eps=1e-6, rope_theta=1e6)
     max_len = args.prompt + args.steps + args.warmup + 1
-    dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len)
-    logits = torch.empty(V, dtype=torch.float32, device="cuda")
-    toks = rng.integers(0, V, size=max_len)
-    pos = 0
-    for _ in range(args.prompt + args.warmup):
-        dec.forward(int(toks[pos]), pos, logits)
+    chunk = max(B, min(args.prompt, 512))
+    dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len, n_seqs=B,
+                       max_batch=chunk)
+    logits = torch.empty((B, V), dtype=torch.float32, device="cuda")
+    toks = rng.integers(0, V, size=(B, max_len))
+    stream = torch.cuda.current_stream()
+    # prefill: each sequence's prompt in steps of up to `chunk` consecutive positions
+    pre_ms = 0.0
+    for b in range(B):
+        for s0 in range(0, args.prompt, chunk):
+            s1 = min(args.prompt, s0 + chunk)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dec.step(toks[b, s0:s1], np.arange(s0, s1), np.full(s1 - s0, b), logits=logits[:1],
+                     last_logits_only=True)
+            e.record(stream)
+            torch.cuda.synchronize()
+            if b > 0 or s0 > 0 or B == 1:   # the very first step warms the kernels
+                pre_ms += a.elapsed_time(e)
+    pre_tokens = args.prompt * B - (0 if B == 1 else min(chunk, args.prompt))
+    pos = args.prompt
+    seq_ids = np.arange(B)
+
+    def one_step(p):
+        if B == 1:
+            dec.forward(int(toks[0, p]), p, logits[0])
+        else:
+            dec.step(toks[:, p], np.full(B, p), seq_ids, logits=logits)
+
+    for _ in range(args.warmup):
+        one_step(pos)
         pos += 1
     ctx.check()
-    stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
     for a, b in evs:
         a.record(stream)
-        dec.forward(int(toks[pos]), pos, logits)
+        one_step(pos)
         b.record(stream)
         pos += 1
     torch.cuda.synchronize()
@@ -259,19 +288,25 @@ def run_decode(args):
     q4r_h, q4r_i = fmt.row_bytes(fmt.Q4_0, Hd), fmt.row_bytes(fmt.Q4_0, I)
     expert_bytes = 2 * I * q4r_h + Hd * q4r_i
     attn_bytes = ((nh + 2 * nkv) * hd * Hd + Hd * nh * hd) * 2
-    per_token_bytes = L * (K_TOP * expert_bytes + attn_bytes + E * Hd * 4) + V * Hd * 2
-    line = {"metric": "decode_tok_s_full_model", "value": 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
+    # distinct experts a step reads: expected over B tokens' independent top-8 picks
+    distinct = E * (1 - (1 - K_TOP / E) ** B)
+    per_step_bytes = L * (distinct * expert_bytes + attn_bytes + E * Hd * 4) + V * Hd * 2
+    line = {"metric": "decode_tok_s_full_model", "value": B * 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 experts, bf16 dense, f32 activations",
             "data": "synthetic",
-            "config": {"workload": "qwen3_30b_a3b_decode_b1", "layers": L, "hidden": Hd, "heads": nh,
+            "config": {"workload": f"qwen3_30b_a3b_decode_b{B}", "layers": L, "hidden": Hd, "heads": nh,
                        "kv_heads": nkv, "head_dim": hd, "vocab": V, "experts": E, "top_k": K_TOP,
-                       "moe_intermediate": I, "batch": 1, "positions_before_timing": args.prompt},
-            "timing": "CUDA events around each step; steps after the first replay one captured CUDA graph "
-                      "(token and position through device memory)",
-            "gpu_launches_per_token": 2 + L * 9,
-            "algorithmic_bytes_per_token": per_token_bytes,
-            "achieved_gbs": per_token_bytes / (ms / 1e3) / 1e9}
+                       "moe_intermediate": I, "batch": B, "positions_before_timing": args.prompt},
+            "timing": ("CUDA events around each step; steps after the first replay one captured CUDA graph "
+                       "(token and position through device memory)") if B == 1 else
+                      "CUDA events around each hale_decoder_step of B rows (one per sequence)",
+            "gpu_launches_per_step": 2 + L * 9,
+            "algorithmic_bytes_per_step": per_step_bytes,
+            "achieved_gbs": per_step_bytes / (ms / 1e3) / 1e9,
+            "prefill": {"tok_s": pre_tokens / (pre_ms / 1e3) if pre_ms > 0 else None, "prompt": args.prompt,
+                        "rows_per_step": chunk, "timed_tokens": pre_tokens,
+                        "timing": "CUDA events around batched hale_decoder_step calls (first one untimed at B > 1)"}}
     emit(line)
     dec.close()
     ctx.close()

@@ -117,6 +117,9 @@ SIGNATURES = {
     "hale_decoder_create": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, C.POINTER(P)]),
     "hale_decoder_destroy": (None, [P]),
     "hale_decoder_forward": (I32, [P, P, U32, U32, P, P, P]),
+    "hale_decoder_create_batched": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, U32, U32,
+                                         C.POINTER(P)]),
+    "hale_decoder_step": (I32, [P, P, P, P, P, U32, P, I32, P, P]),
     "hale_lm_head": (I32, [P, P, P, U32, P, P]),
     "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
     "hale_expf_host": (None, [P, P, U64]),
@@ -387,7 +390,7 @@ class Decoder:
     MoE layers in order (pool layer j = j-th MoE layer), or None.
     """
 
-    def __init__(self, ctx, dims, layers, embed, lm_head, final_norm, pool, max_len):
+    def __init__(self, ctx, dims, layers, embed, lm_head, final_norm, pool, max_len, n_seqs=1, max_batch=1):
         import numpy as np
         self.ctx, self.dims, self._keep = ctx, dict(dims), []
 
@@ -418,14 +421,30 @@ class Decoder:
                            d.get("n_experts", 0), d.get("top_k", 0), int(d.get("normalize_topk", 0)), d["eps"],
                            d["rope_theta"], mat(embed), mat(lm_head), vec(final_norm))
         h = P()
-        ctx.call("hale_decoder_create", ctx.h, C.byref(desc), arr, pool.h if pool is not None else None,
-                 max_len, C.byref(h))
+        ctx.call("hale_decoder_create_batched", ctx.h, C.byref(desc), arr, pool.h if pool is not None else None,
+                 max_len, n_seqs, max_batch, C.byref(h))
+        self.n_seqs, self.max_batch, self.max_len = n_seqs, max_batch, max_len
         self.h = h
         self.pool = pool
 
     def forward(self, token, position, logits=None, hidden=None, stream=None):
         """One decode step; logits / hidden: device tensors or None."""
         self.ctx.call("hale_decoder_forward", self.ctx.h, self.h, int(token), int(position), ptr(logits),
+                      ptr(hidden), _stream(stream))
+
+    def step(self, tokens, positions, seqs=None, logits=None, last_logits_only=False, hidden=None, stream=None):
+        """hale_decoder_step: one step over rows (tokens[r], positions[r],
+        seqs[r]); a prompt's consecutive positions in one call is batched
+        prefill, one row per sequence is batched decode. logits: device
+        [n, vocab] ([1, vocab] with last_logits_only) or None."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        sq = None if seqs is None else np.ascontiguousarray(seqs, dtype=np.uint32)
+        if p.shape != t.shape or (sq is not None and sq.shape != t.shape):
+            raise ValueError("tokens, positions and seqs must have the same length")
+        self.ctx.call("hale_decoder_step", self.ctx.h, self.h, t.ctypes.data, p.ctypes.data,
+                      None if sq is None else sq.ctypes.data, int(t.size), ptr(logits), int(bool(last_logits_only)),
                       ptr(hidden), _stream(stream))
 
     def close(self):

@@ -616,6 +616,35 @@ static void fgemv_dispatch(const hale_matrix* m, const float* x, uint32_t M, flo
 static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float* x, uint32_t M, float* out,
                                 cudaStream_t st) {
     ProfScope ps_(ctx, "fgemv", st);
+    if (m->lanes && M > 1) {
+        // several activation rows: each weight step read once per chunk of NB rows
+        const unsigned gx = (m->rows_pad / 4 + 7) / 8;
+        const int NB = m->cols <= 3072 ? 8 : (m->cols <= 6144 ? 4 : 2);
+        const dim3 grid(gx, (M + NB - 1) / NB);
+        const size_t smem = (size_t)NB * m->cols * 4;
+        hale_status r = HALE_OK;
+        auto go = [&](auto kern) {
+            cudaError_t e = allow_smem(kern, smem);
+            if (e != cudaSuccess) {
+                r = fail(ctx, HALE_E_CUDA, "fgemv_lanes_batch: %s", cudaGetErrorString(e));
+                return;
+            }
+            kern<<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, x, (int)M, out);
+        };
+        switch (m->dtype) {
+        case HALE_F32:
+            NB == 8 ? go(fgemv_lanes_batch_kernel<0, 8>) : NB == 4 ? go(fgemv_lanes_batch_kernel<0, 4>) : go(fgemv_lanes_batch_kernel<0, 2>);
+            break;
+        case HALE_F16:
+            NB == 8 ? go(fgemv_lanes_batch_kernel<1, 8>) : NB == 4 ? go(fgemv_lanes_batch_kernel<1, 4>) : go(fgemv_lanes_batch_kernel<1, 2>);
+            break;
+        default:
+            NB == 8 ? go(fgemv_lanes_batch_kernel<2, 8>) : NB == 4 ? go(fgemv_lanes_batch_kernel<2, 4>) : go(fgemv_lanes_batch_kernel<2, 2>);
+            break;
+        }
+        if (r) return r;
+        return check_launch(ctx, "fgemv_lanes_batch");
+    }
     if (m->lanes) {
         const unsigned grid = (m->rows_pad / 4 + 7) / 8;
         const size_t smem = (size_t)m->cols * 4;
@@ -1615,6 +1644,8 @@ struct hale_decoder {
     hale_ctx* ctx = nullptr;
     hale_pool* pool = nullptr;
     uint32_t H = 0, L = 0, nh = 0, nkv = 0, hd = 0, V = 0, E = 0, k = 0, max_len = 0;
+    uint32_t n_seqs = 1, max_batch = 1;
+    size_t seq_stride = 0;  // floats per sequence in one layer's K (or V) cache
     int normalize = 0;
     float eps = 0.0f, scale = 0.0f;
     std::vector<Layer> layers;
@@ -1626,9 +1657,10 @@ struct hale_decoder {
     float *x = nullptr, *normed = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr;
     float *g = nullptr, *u = nullptr, *h = nullptr, *scores = nullptr;
     std::vector<void*> allocs;
-    // step replay: token/position through device memory from a pinned slot
-    uint32_t* d_tp = nullptr;
-    uint32_t* h_tp = nullptr;
+    // step rows (token, position, sequence) through device memory from a
+    // pinned slot, so a captured step replays for any token
+    uint32_t* d_rows = nullptr;
+    uint32_t* h_rows = nullptr;
     cudaEvent_t ev_copied = nullptr;
     bool copied_recorded = false;
     cudaStream_t cap = nullptr;
@@ -1645,7 +1677,7 @@ extern "C" void hale_decoder_destroy(hale_decoder* d) {
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->cap) cudaStreamDestroy(d->cap);
     if (d->ev_copied) cudaEventDestroy(d->ev_copied);
-    if (d->h_tp) cudaFreeHost(d->h_tp);
+    if (d->h_rows) cudaFreeHost(d->h_rows);
     for (auto& ly : d->layers)
         for (hale_matrix* m : {ly.qkv, ly.o, ly.gate, ly.up, ly.down})
             if (m) hale_matrix_destroy(m);
@@ -1681,10 +1713,14 @@ static hale_status dec_matrix(hale_ctx* ctx, const hale_host_matrix& m, uint32_t
     return hale_matrix_create(ctx, (hale_dtype)m.dtype, rows, cols, m.data, (uint64_t)rows * rb, 0, out);
 }
 
-extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_desc* ds, const hale_decoder_layer* lys,
-                                           hale_pool* pool, uint32_t max_len, hale_decoder** out) {
+extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_decoder_desc* ds,
+                                                   const hale_decoder_layer* lys, hale_pool* pool, uint32_t max_len,
+                                                   uint32_t n_seqs, uint32_t max_batch, hale_decoder** out) {
     if (!ctx || !ds || !lys || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_create: NULL argument");
     *out = nullptr;
+    if (n_seqs == 0 || max_batch == 0 || max_batch > 4096)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: need 1 or more sequences and 1..4096 rows per step (got %u, %u)",
+                    n_seqs, max_batch);
     const uint32_t H = ds->hidden, nh = ds->n_heads, nkv = ds->n_kv_heads, hd = ds->head_dim;
     if (!H || !ds->n_layers || !nh || !nkv || !hd || !ds->vocab || !max_len || nh % nkv || hd % 4 || hd > 1024)
         return fail(ctx, HALE_E_INVALID_ARGUMENT,
@@ -1708,6 +1744,8 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
     d->normalize = ds->normalize_topk;
     d->eps = ds->eps;
     d->max_len = max_len;
+    d->n_seqs = n_seqs;
+    d->max_batch = max_batch;
     d->scale = 1.0f / sqrtf((float)hd);  // attention.rs: 1 / sqrt(head_dim)
     hale_status r = HALE_OK;
     auto bail = [&](hale_status st) {
@@ -1783,19 +1821,25 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
         }
     if ((r = dec_upload(ctx, d, cs.data(), cs.size() * 4, reinterpret_cast<void**>(&d->rope_cos)))) return bail(r);
     if ((r = dec_upload(ctx, d, sn.data(), sn.size() * 4, reinterpret_cast<void**>(&d->rope_sin)))) return bail(r);
-    const size_t cache = (size_t)d->L * max_len * kvd * 4;
+    // KV cache: [layer][sequence][position][kv heads * head_dim] f32
+    d->seq_stride = (size_t)max_len * kvd;
+    const size_t cache = (size_t)d->L * n_seqs * d->seq_stride * 4;
     if ((r = dec_alloc(ctx, d, cache, reinterpret_cast<void**>(&d->kcache)))) return bail(r);
     if ((r = dec_alloc(ctx, d, cache, reinterpret_cast<void**>(&d->vcache)))) return bail(r);
-    struct { float** p; size_t n; } bufs[] = {{&d->x, H}, {&d->normed, H}, {&d->delta, H}, {&d->qkv, qkv_rows},
-                                               {&d->attn, (size_t)nh * hd}, {&d->g, max_inter}, {&d->u, max_inter},
-                                               {&d->h, max_inter}, {&d->scores, (size_t)nh * max_len}};
+    // attention keeps q and up to 8192 scores in shared memory (below 48 KB);
+    // longer contexts keep scores in a [rows][heads][max_len] scratch
+    d->smem_scores = std::min<uint32_t>(max_len, 8192u);
+    const size_t B = max_batch;
+    const size_t score_floats = max_len > d->smem_scores ? B * nh * max_len : 4;
+    struct { float** p; size_t n; } bufs[] = {{&d->x, B * H}, {&d->normed, B * H}, {&d->delta, B * H},
+                                               {&d->qkv, B * qkv_rows}, {&d->attn, B * nh * hd},
+                                               {&d->g, B * max_inter}, {&d->u, B * max_inter},
+                                               {&d->h, B * max_inter}, {&d->scores, score_floats}};
     for (auto& b : bufs)
         if ((r = dec_alloc(ctx, d, b.n * 4, reinterpret_cast<void**>(b.p)))) return bail(r);
-    if ((r = dec_alloc(ctx, d, 8, reinterpret_cast<void**>(&d->d_tp)))) return bail(r);
-    // attention keeps q and up to 8192 scores in shared memory (below 48 KB)
-    d->smem_scores = std::min<uint32_t>(max_len, 8192u);
+    if ((r = dec_alloc(ctx, d, B * 12, reinterpret_cast<void**>(&d->d_rows)))) return bail(r);
     if (H > 12000) return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder: hidden %u above 12000", H));
-    if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_tp), 8, cudaHostAllocDefault) != cudaSuccess ||
+    if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_rows), B * 12, cudaHostAllocDefault) != cudaSuccess ||
         cudaEventCreateWithFlags(&d->ev_copied, cudaEventDisableTiming) != cudaSuccess ||
         cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) != cudaSuccess)
         return bail(fail(ctx, HALE_E_CUDA, "decoder: cannot create its step resources"));
@@ -1803,38 +1847,41 @@ extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_des
     return HALE_OK;
 }
 
-// One step on stream st: the token/position copy from the pinned slot, then
-// every kernel of the step.
-static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, float* logits, float* hidden, cudaStream_t st) {
+// One step of n rows on stream st: the row descriptors' copy from the pinned
+// slot, then every kernel of the step. logits: [n, V], or [1, V] for the last
+// row only when last_logits.
+static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, float* logits, bool last_logits,
+                                   float* hidden, cudaStream_t st) {
     void* stream = st;
-    CUDA_TRY(ctx, cudaMemcpyAsync(d->d_tp, d->h_tp, 8, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(ctx, cudaMemcpyAsync(d->d_rows, d->h_rows, (size_t)n * 12, cudaMemcpyHostToDevice, st));
     hale_status r;
     const int H = (int)d->H, hb = (H + 255) / 256;
-    const size_t kvd = (size_t)d->nkv * d->hd;
+    const size_t lstride = (size_t)d->n_seqs * d->seq_stride;
+    const dim3 eg(hb, n);
     switch (d->embed_dtype) {
-    case HALE_F32: embed_kernel<0><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
-    case HALE_F16: embed_kernel<1><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
-    default: embed_kernel<2><<<hb, 256, 0, st>>>(d->embed, H, d->d_tp, d->x); break;
+    case HALE_F32: embed_kernel<0><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
+    case HALE_F16: embed_kernel<1><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
+    default: embed_kernel<2><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
     }
     if ((r = check_launch(ctx, "embed"))) return r;
     for (uint32_t l = 0; l < d->L; l++) {
         const auto& ly = d->layers[l];
-        float* kc = d->kcache + (size_t)l * d->max_len * kvd;
-        float* vc = d->vcache + (size_t)l * d->max_len * kvd;
+        float* kc = d->kcache + (size_t)l * lstride;
+        float* vc = d->vcache + (size_t)l * lstride;
         // the previous layer's FFN residual folds into this norm
-        rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
-        if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, 1, d->qkv, nullptr, stream))) return r;
-        qk_rope_kernel<<<d->nh + 2 * d->nkv, 32, (size_t)d->hd * 4, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm,
-                                                          ly.k_norm, d->eps, d->rope_cos, d->rope_sin, d->d_tp, kc,
-                                                          vc);
+        if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
+        qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
+            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos, d->rope_sin,
+            d->d_rows, kc, vc, d->seq_stride);
         if ((r = check_launch(ctx, "qk_rope"))) return r;
-        attn_decode_kernel<<<d->nh, 256, ((size_t)d->hd + d->smem_scores) * 4, st>>>(
-            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_tp, (int)d->max_len, d->scale, d->scores,
-            d->attn, (int)d->smem_scores);
+        attn_decode_kernel<<<dim3(d->nh, n), 256, ((size_t)d->hd + d->smem_scores) * 4, st>>>(
+            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_rows, (int)d->max_len, d->scale, d->scores,
+            d->attn, (int)d->smem_scores, d->seq_stride);
         if ((r = check_launch(ctx, "attn_decode"))) return r;
-        if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, 1, d->delta, nullptr, stream))) return r;
-        rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+        if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
+        rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
             hale_moe_layer m{};
@@ -1844,20 +1891,29 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, float* logits
             m.n_experts = d->E;
             m.top_k = d->k;
             m.normalize_topk = d->normalize;
-            if ((r = hale_moe_forward(ctx, d->pool, &m, d->normed, 1, d->delta, nullptr, nullptr, stream))) return r;
+            if ((r = hale_moe_forward(ctx, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream))) return r;
         } else {
-            if ((r = hale_matrix_matvec(ctx, ly.gate, d->normed, 1, d->g, nullptr, stream))) return r;
-            if ((r = hale_matrix_matvec(ctx, ly.up, d->normed, 1, d->u, nullptr, stream))) return r;
-            silu_mul_kernel<<<(ly.inter + 255) / 256, 256, 0, st>>>(d->g, d->u, (int)ly.inter, d->h);
+            if ((r = hale_matrix_matvec(ctx, ly.gate, d->normed, n, d->g, nullptr, stream))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.up, d->normed, n, d->u, nullptr, stream))) return r;
+            const int cnt = (int)(n * ly.inter);
+            silu_mul_kernel<<<(cnt + 255) / 256, 256, 0, st>>>(d->g, d->u, cnt, d->h);
             if ((r = check_launch(ctx, "silu_mul"))) return r;
-            if ((r = hale_matrix_matvec(ctx, ly.down, d->h, 1, d->delta, nullptr, stream))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.down, d->h, n, d->delta, nullptr, stream))) return r;
         }
     }
-    rmsnorm_kernel<<<1, 256, (size_t)H * 4, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+    rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
-    if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)H * 4, cudaMemcpyDeviceToDevice, st));
-    if (logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed, 1, logits, nullptr, stream);
+    if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, st));
+    if (logits) {
+        if (last_logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed + (size_t)(n - 1) * H, 1, logits, nullptr, stream);
+        return hale_matrix_matvec(ctx, d->lm_head, d->normed, n, logits, nullptr, stream);
+    }
     return HALE_OK;
+}
+
+extern "C" hale_status hale_decoder_create(hale_ctx* ctx, const hale_decoder_desc* ds, const hale_decoder_layer* lys,
+                                           hale_pool* pool, uint32_t max_len, hale_decoder** out) {
+    return hale_decoder_create_batched(ctx, ds, lys, pool, max_len, 1, 1, out);
 }
 
 extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint32_t token, uint32_t position,
@@ -1871,8 +1927,9 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     cudaStream_t st = S(stream);
     // the previous step must have read the slot before it is rewritten
     if (d->copied_recorded) CUDA_TRY(ctx, cudaEventSynchronize(d->ev_copied));
-    d->h_tp[0] = token;
-    d->h_tp[1] = position;
+    d->h_rows[0] = token;
+    d->h_rows[1] = position;
+    d->h_rows[2] = 0;
     const bool capturing = stream_capturing(stream);
     d->copied_recorded = !capturing;
     if (d->exec && d->g_logits == logits && d->g_hidden == hidden && !capturing) {
@@ -1880,7 +1937,7 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
         CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
         return HALE_OK;
     }
-    hale_status r = decoder_enqueue(ctx, d, logits, hidden, st);
+    hale_status r = decoder_enqueue(ctx, d, 1, logits, false, hidden, st);
     if (!r && !capturing) CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
     if (r || capturing || d->no_graph) return r;
     // capture the step for the following calls with these outputs
@@ -1894,7 +1951,7 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
         d->no_graph = true;
         return HALE_OK;
     }
-    r = decoder_enqueue(ctx, d, logits, hidden, d->cap);
+    r = decoder_enqueue(ctx, d, 1, logits, false, hidden, d->cap);
     const cudaError_t ec = cudaStreamEndCapture(d->cap, &graph);
     if (r || ec != cudaSuccess || !graph || cudaGraphInstantiate(&d->exec, graph, 0) != cudaSuccess) {
         cudaGetLastError();
@@ -1906,6 +1963,50 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     d->g_logits = logits;
     d->g_hidden = hidden;
     return HALE_OK;
+}
+
+extern "C" hale_status hale_decoder_step(hale_ctx* ctx, hale_decoder* d, const uint32_t* tokens,
+                                         const uint32_t* positions, const uint32_t* seqs, uint32_t n, float* logits,
+                                         int32_t last_logits_only, float* hidden, void* stream) {
+    if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_step: bad handle");
+    if (n == 0) return HALE_OK;
+    if (!tokens || !positions) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_step: NULL tokens or positions");
+    if (n > d->max_batch)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "step of %u rows exceeds the decoder's %u", n, d->max_batch);
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t sq = seqs ? seqs[i] : 0;
+        if (tokens[i] >= d->V) return fail(ctx, HALE_E_INVALID_ARGUMENT, "token %u out of vocabulary (%u)", tokens[i], d->V);
+        if (sq >= d->n_seqs) return fail(ctx, HALE_E_INVALID_ARGUMENT, "sequence %u out of range (%u)", sq, d->n_seqs);
+        if (positions[i] >= d->max_len)
+            return fail(ctx, HALE_E_CONTEXT_OVERFLOW, "position %u exceeds the KV cache (%u positions)", positions[i],
+                        d->max_len);
+    }
+    {
+        // a (sequence, position) slot is written by at most one row of a step
+        std::vector<uint64_t> keys(n);
+        for (uint32_t i = 0; i < n; i++) keys[i] = ((uint64_t)(seqs ? seqs[i] : 0) << 32) | positions[i];
+        std::sort(keys.begin(), keys.end());
+        for (uint32_t i = 1; i < n; i++)
+            if (keys[i] == keys[i - 1])
+                return fail(ctx, HALE_E_INVALID_ARGUMENT, "two rows write sequence %u position %u",
+                            (unsigned)(keys[i] >> 32), (unsigned)(keys[i] & 0xffffffffu));
+    }
+    if (stream_capturing(stream))
+        return fail(ctx, HALE_E_UNSUPPORTED, "hale_decoder_step is not captured; hale_decoder_forward replays a graph");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    if (d->copied_recorded) CUDA_TRY(ctx, cudaEventSynchronize(d->ev_copied));
+    for (uint32_t i = 0; i < n; i++) {
+        d->h_rows[3 * i] = tokens[i];
+        d->h_rows[3 * i + 1] = positions[i];
+        d->h_rows[3 * i + 2] = seqs ? seqs[i] : 0;
+    }
+    hale_status r = decoder_enqueue(ctx, d, n, logits, last_logits_only != 0, hidden, st);
+    if (!r) {
+        CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
+        d->copied_recorded = true;
+    }
+    return r;
 }
 
 extern "C" hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, const float* hidden, uint32_t batch,

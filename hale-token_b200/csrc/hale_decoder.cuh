@@ -16,31 +16,38 @@
 
 namespace hale {
 
-// tp[0] = token, tp[1] = position of the step, in device memory so that a
-// captured step replays for any token.
+// A step processes n rows; row r is described in device memory by
+// rows[3r .. 3r+2] = token, position, sequence (so a captured step replays
+// for any token). Row r's activations sit at row r of every [n, width]
+// buffer; sequence s's KV cache of a layer starts at s * seq_stride floats.
 
-// x[c] = embed[token][c] decoded to f32 (row-major source rows; DT 0 f32,
-// 1 f16, 2 bf16).
+// x[r][c] = embed[token_r][c] decoded to f32 (row-major source rows; DT 0
+// f32, 1 f16, 2 bf16). Grid: (ceil(H / blockDim), n).
 template <int DT>
-__global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32_t* __restrict__ tp,
+__global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32_t* __restrict__ rows,
                              float* __restrict__ x) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
     if (c >= H) return;
-    const size_t i = (size_t)tp[0] * H + c;
-    if (DT == 0) x[c] = reinterpret_cast<const float*>(embed)[i];
-    else if (DT == 1) x[c] = half_bits_to_float(reinterpret_cast<const uint16_t*>(embed)[i]);
-    else x[c] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(embed)[i] << 16);
+    const size_t i = (size_t)rows[3 * r] * H + c;
+    float* xr = x + (size_t)r * H;
+    if (DT == 0) xr[c] = reinterpret_cast<const float*>(embed)[i];
+    else if (DT == 1) xr[c] = half_bits_to_float(reinterpret_cast<const uint16_t*>(embed)[i]);
+    else xr[c] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(embed)[i] << 16);
 }
 
 // The residual add x += delta (transformer.rs residual; delta nullable), then
 // RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
-// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA; x is
-// staged in shared memory by all threads so the one sequential chain runs
-// at the add's latency, not a global load's. Dynamic shared memory: n floats.
+// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA per
+// row (blockIdx.x); x is staged in shared memory by all threads so the one
+// sequential chain runs at the add's latency, not a global load's. Dynamic
+// shared memory: n floats.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                float eps, int n, float* __restrict__ out) {
     extern __shared__ float s_v[];
     __shared__ float s_scale;
+    x += (size_t)blockIdx.x * n;
+    out += (size_t)blockIdx.x * n;
+    if (delta) delta += (size_t)blockIdx.x * n;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const float v = delta ? fadd(x[i], delta[i]) : x[i];
         if (delta) x[i] = v;
@@ -61,16 +68,21 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
 // Per head (one warp each; q heads, then k heads, then v heads): the in-place
 // RMSNorm of q/k heads, x = x * (scale * w) (norm.rs:30-37, attention.rs:49-56),
 // when the model has it; RoPE (rope.rs:15-43) a' = a c - b s, b' = b c + a s on
-// the pairs (i, i + hd/2); k and v rows appended to the cache at `pos`.
-// qkv: [nh*hd | nkv*hd | nkv*hd] as the fused projection wrote it.
+// the pairs (i, i + hd/2); k and v rows appended to the row's sequence cache
+// at its position. qkv: per row [nh*hd | nkv*hd | nkv*hd] as the fused
+// projection wrote it. Grid: (nh + 2 nkv, n).
 __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd, const float* __restrict__ q_norm,
                                const float* __restrict__ k_norm, float eps, const float* __restrict__ rope_cos,
-                               const float* __restrict__ rope_sin, const uint32_t* __restrict__ tp,
-                               float* __restrict__ kcache, float* __restrict__ vcache) {
-    const int head = blockIdx.x, lane = threadIdx.x, half = hd / 2;
-    const uint32_t pos = tp[1];
+                               const float* __restrict__ rope_sin, const uint32_t* __restrict__ rows,
+                               float* __restrict__ kcache, float* __restrict__ vcache, size_t seq_stride) {
+    const int head = blockIdx.x, lane = threadIdx.x, half = hd / 2, r = blockIdx.y;
+    const uint32_t pos = rows[3 * r + 1];
+    const size_t seq = rows[3 * r + 2];
     const int kvd = nkv * hd;
     if (head >= nh + 2 * nkv) return;
+    qkv += (size_t)r * (nh + 2 * nkv) * hd;
+    kcache += seq * seq_stride;
+    vcache += seq * seq_stride;
     if (head >= nh + nkv) {  // v head: straight into the cache
         const int vh = head - nh - nkv;
         const float* v = qkv + (size_t)(nh + nkv) * hd + (size_t)vh * hd;
@@ -110,24 +122,31 @@ __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd,
     }
 }
 
-// Attention::forward for the token at pos (attention.rs:59-85), one CTA per
-// q head h (kv head h / (nh / nkv)): scores[t] = (sum_i q_i k_ti from -0) *
-// scale; softmax over t = 0..pos (activation.rs:11-21); ctx_i = sum_t
-// scores[t] v_ti from 0, t ascending. q sits in shared memory and each key
-// row is read 16 bytes at a time ahead of its chain; scores live in shared
-// memory when pos + 1 <= smem_scores (dynamic shared memory: hd +
-// smem_scores floats), else in the [nh][max_len] scratch.
+// Attention::forward for the row's token at pos (attention.rs:59-85), one CTA
+// per (q head h, row) (kv head h / (nh / nkv)): scores[t] = (sum_i q_i k_ti
+// from -0) * scale; softmax over t = 0..pos (activation.rs:11-21); ctx_i =
+// sum_t scores[t] v_ti from 0, t ascending, over the row's sequence cache. q
+// sits in shared memory and each key row is read 16 bytes at a time ahead of
+// its chain; scores live in shared memory when pos + 1 <= smem_scores
+// (dynamic shared memory: hd + smem_scores floats), else in the
+// [n][nh][max_len] scratch. Grid: (nh, n).
 __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
                                                           const float* __restrict__ kcache,
                                                           const float* __restrict__ vcache,
-                                                          const uint32_t* __restrict__ tp, int max_len,
+                                                          const uint32_t* __restrict__ rows, int max_len,
                                                           float scale, float* __restrict__ scores,
-                                                          float* __restrict__ ctx, int smem_scores) {
+                                                          float* __restrict__ ctx, int smem_scores,
+                                                          size_t seq_stride) {
     extern __shared__ __align__(16) float s_att[];  // [hd] q, then [smem_scores] scores
     __shared__ float s_red[32];
     __shared__ float s_bc[2];
-    const int h = blockIdx.x, tid = threadIdx.x;
-    const int seq = (int)tp[1] + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
+    const int h = blockIdx.x, tid = threadIdx.x, r = blockIdx.y;
+    const int seq = (int)rows[3 * r + 1] + 1, kvd = nkv * hd, off = (h / (nh / nkv)) * hd;
+    qkv += (size_t)r * (nh + 2 * nkv) * hd;
+    ctx += (size_t)r * nh * hd;
+    scores += (size_t)r * nh * max_len;
+    kcache += (size_t)rows[3 * r + 2] * seq_stride;
+    vcache += (size_t)rows[3 * r + 2] * seq_stride;
     float* s_q = s_att;
     for (int i = tid; i < hd; i += blockDim.x) s_q[i] = qkv[(size_t)h * hd + i];
     float* sc = seq <= smem_scores ? s_att + hd : scores + (size_t)h * max_len;

@@ -1148,6 +1148,48 @@ __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restr
     if (l == 0 && row < rows) out[row] = fadd(r, -0.0f);
 }
 
+// The same matvec for n activation rows, NB per CTA (blockIdx.y = chunk):
+// each weight step is loaded once and applied to the chunk's rows, staged in
+// shared memory ([NB][cols], rows past n zero-filled and never stored). Per
+// activation row the operations and their order are fgemv_lanes_kernel's, so
+// every row's result has the same bits as a one-row launch.
+template <int DT, int NB>
+__global__ void __launch_bounds__(256) fgemv_lanes_batch_kernel(const uint8_t* __restrict__ W, int rows, int cols,
+                                                                const float* __restrict__ x, int n,
+                                                                float* __restrict__ out) {
+    extern __shared__ float s_xb[];  // [NB][cols]
+    constexpr int ES = DT == 0 ? 4 : 2;
+    const int b0 = blockIdx.y * NB;
+    const int nb = min(NB, n - b0);
+    for (int i = threadIdx.x; i < NB * cols; i += blockDim.x)
+        s_xb[i] = i < nb * cols ? x[(size_t)b0 * cols + i] : 0.0f;
+    __syncthreads();
+    const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (q * 4 >= rows) return;
+    const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
+    const uint8_t* base = W + (((size_t)q * S8 * 4 + rr) * 64 + l * 8) * ES;
+    float acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) acc[b] = 0.0f;
+#pragma unroll 2
+    for (int s = 0; s < S8; s++) {
+        float w[8];
+        load8<DT>(base + (size_t)s * 4 * 64 * ES, w);
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int b = 0; b < NB; b++) acc[b] = fadd(acc[b], fmul(w[j], s_xb[b * cols + (8 * s + j) * 8 + l]));
+    }
+    const int row = q * 4 + rr;
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const float s1 = fadd(acc[b], __shfl_down_sync(0xffffffffu, acc[b], 4, 8));
+        const float p = fadd(s1, __shfl_down_sync(0xffffffffu, s1, 1, 8));
+        const float r = fadd(p, __shfl_down_sync(0xffffffffu, p, 2, 8));
+        if (l == 0 && row < rows && b < nb) out[(size_t)(b0 + b) * rows + row] = fadd(r, -0.0f);
+    }
+}
+
 // Row-major float rows -> the lane-major layout (rows padded to 4 with 0).
 template <int ES>
 __global__ void repack_lanes_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,

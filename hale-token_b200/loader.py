@@ -468,14 +468,15 @@ def cache_policy(config, record_bytes, budget_bytes, routing_counts=None):
 
 
 def load_decoder(ctx, directory, expert_dtype=None, max_len=None, policy=None, expert_hbm_bytes=None,
-                 routing_counts=None):
+                 routing_counts=None, n_seqs=1, max_batch=1):
     """Builds (decoder, pool, config) from a model directory: a Hugging Face
     checkpoint (config.json + safetensors) or a converted one (config.json,
     dense.safetensors, experts.hpk). Dense weights as stored; experts into an
     HBM-resident pool, or a tiered one when `policy` (a CachePolicy) or
     `expert_hbm_bytes` (planned like the reference's RAM budget, hottest
     experts of `routing_counts` pinned first) is given. max_len: KV-cache
-    positions (default the config's max_position_embeddings)."""
+    positions (default the config's max_position_embeddings); n_seqs /
+    max_batch: KV caches and rows per Decoder.step."""
     w = ModelWeights(directory, expert_dtype)
     cfg = w.config
     if policy is None and expert_hbm_bytes is not None:
@@ -488,5 +489,5 @@ def load_decoder(ctx, directory, expert_dtype=None, max_len=None, policy=None, e
             for e in range(cfg.num_experts):
                 pool.upload(j, e, w.expert_record(j, e))
     dec = hale.Decoder(ctx, w.dims, w.layers, w.embed, w.lm_head, w.final_norm, pool,
-                       max_len or cfg.max_position_embeddings)
+                       max_len or cfg.max_position_embeddings, n_seqs, max_batch)
     return dec, pool, cfg

@@ -370,6 +370,27 @@ HALE_API void hale_decoder_destroy(hale_decoder* dec);
 HALE_API hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* dec, uint32_t token, uint32_t position,
                                           float* logits, float* hidden, void* stream);
 
+/* A decoder with n_seqs independent KV caches whose steps take up to
+ * max_batch rows (hale_decoder_create is n_seqs = max_batch = 1). */
+HALE_API hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_decoder_desc* desc,
+                                                 const hale_decoder_layer* layers, hale_pool* experts,
+                                                 uint32_t max_len, uint32_t n_seqs, uint32_t max_batch,
+                                                 hale_decoder** out);
+/* One step over n rows (host arrays): row r is tokens[r] at positions[r] of
+ * sequence seqs[r] (seqs NULL = all sequence 0). Every row's K/V is appended
+ * before any row attends, and row r attends to positions 0..positions[r] of
+ * its sequence, so a prompt's consecutive positions in one step (batched
+ * prefill) or one row per sequence (batched decode) give each row exactly
+ * the logits of token-by-token Transformer::forward (transformer.rs:168-239):
+ * the MoE layers run all rows through the grouped expert kernels, every
+ * other op applies the one-row arithmetic to each row. Two rows may not
+ * write the same (sequence, position). logits: [n, vocab], or [1, vocab] for
+ * the last row when last_logits_only; hidden: [n, hidden]; both device,
+ * nullable. Not capturable into a CUDA graph. */
+HALE_API hale_status hale_decoder_step(hale_ctx* ctx, hale_decoder* dec, const uint32_t* tokens,
+                                       const uint32_t* positions, const uint32_t* seqs, uint32_t n,
+                                       float* logits, int32_t last_logits_only, float* hidden, void* stream);
+
 /* ---- sampling tail -------------------------------------------------------- */
 
 /* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .

@@ -38,7 +38,7 @@ def ctx():
     c.close()
 
 
-def build_decoder(ctx, om, expert_dtype, max_len):
+def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1):
     """The fixture's tensors (same names and normalisation as the oracle
     loader) as hale_decoder descriptors, experts encoded like the oracle's."""
     c = om.cfg
@@ -77,7 +77,7 @@ def build_decoder(ctx, om, expert_dtype, max_len):
     dims = dict(hidden=c["hidden"], n_layers=c["layers"], n_heads=c["heads"], n_kv_heads=c["kv_heads"],
                 head_dim=c["head_dim"], vocab=c["vocab"], n_experts=c["experts"] or 0, top_k=c["top_k"],
                 normalize_topk=c["normalize"], eps=c["eps"], rope_theta=c["theta"])
-    return hale.Decoder(ctx, dims, layers, embed, head, om.f32("model.norm.weight"), pool, max_len)
+    return hale.Decoder(ctx, dims, layers, embed, head, om.f32("model.norm.weight"), pool, max_len, n_seqs, max_batch)
 
 
 @pytest.mark.parametrize("name", ["tiny-qwen3-moe", "tiny-mixtral"])
@@ -158,4 +158,125 @@ def test_checkpoint_loader_builds_a_bit_exact_decoder(ctx, name):
     ctx.check()
     got = np.stack(got)
     assert (got.view(np.uint32) == want.view(np.uint32)).all()
+    dec.close()
+
+
+def _oracle_logits(name, tokens, expert_dtype=fmt.Q8_0):
+    return OM.OracleModel(os.path.join(GOLDEN, name), expert_dtype=expert_dtype).teacher_forced_logits(tokens)
+
+
+def _bits_equal(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    return a.shape == b.shape and bool((a.view(np.uint32) == b.view(np.uint32)).all())
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3-moe", "tiny-mixtral"])
+@pytest.mark.parametrize("chunk", [1, 5, 0])
+def test_batched_prefill_matches_token_by_token(ctx, name, chunk):
+    """A prompt in one step (chunk 0) or in chunks of consecutive positions:
+    every row's logits equal Transformer::forward token by token (the
+    oracle), then single-token decode continues on the same cache."""
+    with open(os.path.join(GOLDEN, name, "expected.json")) as f:
+        tokens = json.load(f)["tokens"]
+    om = OM.OracleModel(os.path.join(GOLDEN, name), expert_dtype=fmt.Q8_0)
+    want = om.teacher_forced_logits(tokens)
+    n_pre = len(tokens) - 3
+    dec = build_decoder(ctx, om, fmt.Q8_0, len(tokens), max_batch=n_pre)
+    V = om.cfg["vocab"]
+    logits = torch.empty((n_pre, V), dtype=torch.float32, device="cuda")
+    step = chunk or n_pre
+    for s0 in range(0, n_pre, step):
+        s1 = min(n_pre, s0 + step)
+        dec.step(tokens[s0:s1], list(range(s0, s1)), logits=logits[s0:s1])
+    got = logits.cpu().numpy()
+    one = torch.empty(V, dtype=torch.float32, device="cuda")
+    tail = []
+    for i in range(n_pre, len(tokens)):
+        dec.forward(tokens[i], i, one)
+        tail.append(one.cpu().numpy().copy())
+    ctx.check()
+    assert _bits_equal(got, want[:n_pre])
+    assert _bits_equal(np.stack(tail), want[n_pre:])
+    dec.close()
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3-moe", "tiny-mixtral"])
+def test_batched_decode_over_sequences(ctx, name):
+    """Three sequences with their own caches, one row each per step (plus a
+    step that mixes a prefill chunk of one with decode rows of the others):
+    each sequence's logits equal the oracle's for that sequence alone."""
+    with open(os.path.join(GOLDEN, name, "expected.json")) as f:
+        base = json.load(f)["tokens"]
+    om = OM.OracleModel(os.path.join(GOLDEN, name), expert_dtype=fmt.Q4_0)
+    V = om.cfg["vocab"]
+    seqs = [base, base[3:] + base[:3], [(t * 7 + 5) % V for t in base]]
+    n = len(base)
+    want = [om.teacher_forced_logits(s) for s in seqs]
+    dec = build_decoder(ctx, om, fmt.Q4_0, n, n_seqs=3, max_batch=8)
+    got = [np.zeros((n, V), np.float32) for _ in seqs]
+    # step 0: sequence 2 prefills positions 0..3 while 0 and 1 decode position 0
+    rows = [(2, 0), (2, 1), (0, 0), (2, 2), (1, 0), (2, 3)]
+    logits = torch.empty((8, V), dtype=torch.float32, device="cuda")
+    dec.step([seqs[s][p] for s, p in rows], [p for _, p in rows], [s for s, _ in rows], logits=logits[:len(rows)])
+    out = logits.cpu().numpy()
+    for r, (s, p) in enumerate(rows):
+        got[s][p] = out[r]
+    pos = [1, 1, 4]
+    while min(pos) < n:
+        rows = [(s, pos[s]) for s in range(3) if pos[s] < n]
+        dec.step([seqs[s][p] for s, p in rows], [p for _, p in rows], [s for s, _ in rows], logits=logits[:len(rows)])
+        out = logits.cpu().numpy()
+        for r, (s, p) in enumerate(rows):
+            got[s][p] = out[r]
+            pos[s] += 1
+    ctx.check()
+    for s in range(3):
+        assert _bits_equal(got[s], want[s]), f"sequence {s}"
+    dec.close()
+
+
+def test_step_last_logits_hidden_and_errors(ctx):
+    name = "tiny-qwen3-moe"
+    with open(os.path.join(GOLDEN, name, "expected.json")) as f:
+        tokens = json.load(f)["tokens"][:6]
+    om = OM.OracleModel(os.path.join(GOLDEN, name), expert_dtype=fmt.Q8_0)
+    want = om.teacher_forced_logits(tokens)
+    dec = build_decoder(ctx, om, fmt.Q8_0, 8, n_seqs=2, max_batch=6)
+    V, H = om.cfg["vocab"], om.cfg["hidden"]
+    last = torch.empty((1, V), dtype=torch.float32, device="cuda")
+    hidden = torch.empty((6, H), dtype=torch.float32, device="cuda")
+    dec.step(tokens, list(range(6)), logits=last, last_logits_only=True, hidden=hidden)
+    assert _bits_equal(last.cpu().numpy()[0], want[5])
+    assert torch.isfinite(hidden).all()
+    for bad, status in [(dict(tokens=[1, 2], positions=[3, 3]), hale.E_INVALID_ARGUMENT),
+                        (dict(tokens=[1], positions=[0], seqs=[2]), hale.E_INVALID_ARGUMENT),
+                        (dict(tokens=[1] * 7, positions=list(range(7))), hale.E_INVALID_ARGUMENT),
+                        (dict(tokens=[V], positions=[0]), hale.E_INVALID_ARGUMENT),
+                        (dict(tokens=[1], positions=[8]), hale.E_CONTEXT_OVERFLOW)]:
+        with pytest.raises(hale.HaleError) as ei:
+            dec.step(**bad)
+        assert ei.value.status == status
+    dec.step([1, 2], [3, 3], seqs=[0, 1])   # same position in two sequences is fine
+    ctx.check()
+    dec.close()
+
+
+def test_batched_prefill_through_a_tiered_pool(ctx, tmp_path):
+    """Batched rows resolve the tiers one token at a time: same logits."""
+    loader = importlib.import_module("hale-token_b200.loader")
+    pk = importlib.import_module("hale-token_b200.pack")
+    name = "tiny-mixtral"
+    with open(os.path.join(GOLDEN, name, "expected.json")) as f:
+        tokens = json.load(f)["tokens"]
+    dst = str(tmp_path / "c")
+    pk.convert_checkpoint(os.path.join(GOLDEN, name), dst, fmt.Q8_0)
+    want = _oracle_logits(name, tokens)
+    rb = loader.ModelWeights(dst).record_bytes
+    dec, pool, cfg = loader.load_decoder(ctx, dst, max_len=len(tokens), policy=hale.CachePolicy([], 2 * rb),
+                                         max_batch=len(tokens))
+    logits = torch.empty((len(tokens), cfg.vocab_size), dtype=torch.float32, device="cuda")
+    dec.step(tokens, list(range(len(tokens))), logits=logits)
+    ctx.check()
+    assert _bits_equal(logits.cpu().numpy(), want)
+    assert pool.stats().misses > 0
     dec.close()
