@@ -1668,6 +1668,7 @@ struct hale_decoder {
     float *g_logits = nullptr, *g_hidden = nullptr;
     bool no_graph = false;
     uint32_t smem_scores = 0;  // attention scores kept in shared memory up to this many positions
+    size_t attn_smem = 0;      // attention's dynamic shared memory
 };
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
@@ -1829,6 +1830,10 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     // attention keeps q and up to 8192 scores in shared memory (below 48 KB);
     // longer contexts keep scores in a [rows][heads][max_len] scratch
     d->smem_scores = std::min<uint32_t>(max_len, 8192u);
+    d->attn_smem = ((size_t)hd + ((d->smem_scores + 3) & ~3u) + (size_t)kAttnStages * attn_v_rows((int)hd) * hd) * 4;
+    if (allow_smem(attn_decode_kernel<1>, d->attn_smem) != cudaSuccess ||
+        allow_smem(attn_decode_kernel<4>, d->attn_smem) != cudaSuccess)
+        return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->attn_smem));
     const size_t B = max_batch;
     const size_t score_floats = max_len > d->smem_scores ? B * nh * max_len : 4;
     struct { float** p; size_t n; } bufs[] = {{&d->x, B * H}, {&d->normed, B * H}, {&d->delta, B * H},
@@ -1876,9 +1881,9 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos, d->rope_sin,
             d->d_rows, kc, vc, d->seq_stride);
         if ((r = check_launch(ctx, "qk_rope"))) return r;
-        attn_decode_kernel<<<dim3(d->nh, n), 256, ((size_t)d->hd + d->smem_scores) * 4, st>>>(
+        (d->hd <= 256 ? attn_decode_kernel<1> : attn_decode_kernel<4>)<<<dim3(d->nh, n), 256, d->attn_smem, st>>>(
             d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_rows, (int)d->max_len, d->scale, d->scores,
-            d->attn, (int)d->smem_scores, d->seq_stride);
+            d->attn, (int)d->smem_scores, d->seq_stride, attn_v_rows((int)d->hd));
         if ((r = check_launch(ctx, "attn_decode"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
         rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);

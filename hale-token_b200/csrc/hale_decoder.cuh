@@ -122,21 +122,56 @@ __global__ void qk_rope_kernel(float* __restrict__ qkv, int nh, int nkv, int hd,
     }
 }
 
+// 16-byte asynchronous global -> shared copies (cp.async, sm_80+).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Attention's V staging: kAttnStages stages of attn_v_rows(hd) positions
+// (16 KB each).
+constexpr int kAttnStages = 3;
+__host__ __device__ inline int attn_v_rows(int hd) { return 4096 / hd < 4 ? 4 : 4096 / hd; }
+
+// Copies V rows [tile * vt, +vt) of one kv head (vsrc = its column 0) into
+// stage tile % kAttnStages and commits the group (an empty group past the
+// last tile keeps the wait count uniform).
+__device__ __forceinline__ void attn_stage_v(float* s_v, const float* __restrict__ vsrc, int tile, int n_tiles,
+                                             int vt, int seq, int hd, int kvd, int tid) {
+    if (tile < n_tiles) {
+        float* dst = s_v + (size_t)(tile % kAttnStages) * vt * hd;
+        const int t0 = tile * vt, here = min(vt, seq - t0), q4 = hd >> 2;
+        for (int j = tid; j < here * q4; j += 256) {
+            const int tt = j / q4, c4 = j - tt * q4;
+            cp_async16(dst + tt * hd + 4 * c4, vsrc + (size_t)(t0 + tt) * kvd + 4 * c4);
+        }
+    }
+    cp_async_commit();
+}
+
 // Attention::forward for the row's token at pos (attention.rs:59-85), one CTA
 // per (q head h, row) (kv head h / (nh / nkv)): scores[t] = (sum_i q_i k_ti
 // from -0) * scale; softmax over t = 0..pos (activation.rs:11-21); ctx_i =
 // sum_t scores[t] v_ti from 0, t ascending, over the row's sequence cache. q
 // sits in shared memory and each key row is read 16 bytes at a time ahead of
-// its chain; scores live in shared memory when pos + 1 <= smem_scores
-// (dynamic shared memory: hd + smem_scores floats), else in the
-// [n][nh][max_len] scratch. Grid: (nh, n).
+// its chain; scores live in shared memory when pos + 1 <= smem_scores, else
+// in the [n][nh][max_len] scratch; V rows are staged through shared memory
+// (vt = attn_v_rows(hd) per stage). Dynamic shared memory: hd +
+// round4(smem_scores) + kAttnStages * vt * hd floats. Grid: (nh, n); 256
+// threads, each running CMAX context columns.
+template <int CMAX>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
                                                           const float* __restrict__ kcache,
                                                           const float* __restrict__ vcache,
                                                           const uint32_t* __restrict__ rows, int max_len,
                                                           float scale, float* __restrict__ scores,
                                                           float* __restrict__ ctx, int smem_scores,
-                                                          size_t seq_stride) {
+                                                          size_t seq_stride, int vt) {
     extern __shared__ __align__(16) float s_att[];  // [hd] q, then [smem_scores] scores
     __shared__ float s_red[32];
     __shared__ float s_bc[2];
@@ -183,17 +218,46 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
+#pragma unroll 16
         for (int t = 0; t < seq; t++) sum = fadd(sum, sc[t]);
         s_bc[1] = sum;
     }
     __syncthreads();
     const float sum = s_bc[1];
     for (int t = tid; t < seq; t += blockDim.x) sc[t] = fdiv(sc[t], sum);
-    __syncthreads();
-    for (int i = tid; i < hd; i += blockDim.x) {
-        float c = 0.0f;
-        for (int t = 0; t < seq; t++) c = fadd(c, fmul(sc[t], vcache[(size_t)t * kvd + off + i]));
-        ctx[(size_t)h * hd + i] = c;
+    // context: V rows stream through shared memory, vt positions per stage in
+    // kAttnStages stages (16-byte cp.async by every thread), while the threads
+    // of columns i run their chains over the staged rows in t order
+    float* s_v = s_att + hd + ((smem_scores + 3) & ~3);
+    const int n_tiles = (seq + vt - 1) / vt;
+    const float* vsrc = vcache + off;
+#pragma unroll
+    for (int st = 0; st < kAttnStages - 1; st++) attn_stage_v(s_v, vsrc, st, n_tiles, vt, seq, hd, kvd, tid);
+    float c[CMAX];  // columns tid, tid + 256, ... (CMAX * 256 >= hd)
+#pragma unroll
+    for (int q = 0; q < CMAX; q++) c[q] = 0.0f;
+    for (int tile = 0; tile < n_tiles; tile++) {
+        attn_stage_v(s_v, vsrc, tile + kAttnStages - 1, n_tiles, vt, seq, hd, kvd, tid);
+        cp_async_wait<kAttnStages - 1>();
+        __syncthreads();
+        const float* vtile = s_v + (size_t)(tile % kAttnStages) * vt * hd;
+        const int t0 = tile * vt, here = min(vt, seq - t0);
+#pragma unroll
+        for (int q = 0; q < CMAX; q++) {
+            const int i = tid + q * 256;
+            if (i < hd) {
+                float acc = c[q];
+#pragma unroll 8
+                for (int tt = 0; tt < here; tt++) acc = fadd(acc, fmul(sc[t0 + tt], vtile[tt * hd + i]));
+                c[q] = acc;
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < CMAX; q++) {
+        const int i = tid + q * 256;
+        if (i < hd) ctx[(size_t)h * hd + i] = c[q];
     }
 }
 
