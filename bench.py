@@ -241,7 +241,7 @@ def run_decode(args):
                            router=router))
     dims = dict(hidden=Hd, n_layers=L, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, n_experts=E, top_k=K_TOP,
                 normalize_topk=1, eps=1e-6, rope_theta=1e6)
-    max_len = args.prompt + args.steps + args.warmup + 1
+    max_len = args.prompt + args.steps + args.warmup + 6   # + the profiled steps
     chunk = max(B, min(args.prompt, 512))
     dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len, n_seqs=B,
                        max_batch=chunk)
@@ -285,6 +285,20 @@ def run_decode(args):
     torch.cuda.synchronize()
     ctx.check()
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    # per-kernel device time of eager steps (hale_ctx_profile: CUDA events around each launch)
+    n_prof = min(5, max(1, args.steps))
+    ctx.profile(True)
+    for _ in range(n_prof):
+        dec.step(toks[:, pos], np.full(B, pos), seq_ids, logits=logits)
+        pos += 1
+    names = ("embed", "rmsnorm", "fgemv", "qk_rope", "attention", "router", "expert_gate_up", "expert_down",
+             "silu_mul")
+    kernels = {}
+    for nm in names:
+        cnt, tot = ctx.profile_read(nm)
+        if cnt:
+            kernels[nm] = {"launches_per_step": cnt / n_prof, "us_per_step": tot * 1e3 / n_prof}
+    ctx.profile(False)
     q4r_h, q4r_i = fmt.row_bytes(fmt.Q4_0, Hd), fmt.row_bytes(fmt.Q4_0, I)
     expert_bytes = 2 * I * q4r_h + Hd * q4r_i
     attn_bytes = ((nh + 2 * nkv) * hd * Hd + Hd * nh * hd) * 2
@@ -304,6 +318,8 @@ def run_decode(args):
             "gpu_launches_per_step": 2 + L * 9,
             "algorithmic_bytes_per_step": per_step_bytes,
             "achieved_gbs": per_step_bytes / (ms / 1e3) / 1e9,
+            "kernels": kernels,
+            "kernels_timing": "eager hale_decoder_step calls with per-launch CUDA events (adds event overhead)",
             "prefill": {"tok_s": pre_tokens / (pre_ms / 1e3) if pre_ms > 0 else None, "prompt": args.prompt,
                         "rows_per_step": chunk, "timed_tokens": pre_tokens,
                         "timing": "CUDA events around batched hale_decoder_step calls (first one untimed at B > 1)"}}

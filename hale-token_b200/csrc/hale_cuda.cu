@@ -1669,6 +1669,12 @@ struct hale_decoder {
     bool no_graph = false;
     uint32_t smem_scores = 0;  // attention scores kept in shared memory up to this many positions
     size_t attn_smem = 0;      // attention's dynamic shared memory
+    // GQA-grouped attention (head_dim <= 256): heads per CTA at one row and in
+    // batched steps, and each variant's shared-memory layout
+    bool gqa = false;
+    int gc_one = 1, gc_batch = 1;
+    int gqa_cap[9] = {0};
+    size_t gqa_smem[9] = {0};
 };
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
@@ -1831,11 +1837,41 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     // longer contexts keep scores in a [rows][heads][max_len] scratch
     d->smem_scores = std::min<uint32_t>(max_len, 8192u);
     d->attn_smem = ((size_t)hd + ((d->smem_scores + 3) & ~3u) + (size_t)kAttnStages * attn_v_rows((int)hd) * hd) * 4;
-    if (allow_smem(attn_decode_kernel<1>, d->attn_smem) != cudaSuccess ||
+    if (allow_smem(rmsnorm_kernel, (size_t)H * 8) != cudaSuccess ||
+        allow_smem(attn_decode_kernel<1>, d->attn_smem) != cudaSuccess ||
         allow_smem(attn_decode_kernel<4>, d->attn_smem) != cudaSuccess)
         return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->attn_smem));
     const size_t B = max_batch;
-    const size_t score_floats = max_len > d->smem_scores ? B * nh * max_len : 4;
+    // GQA-grouped attention: one CTA per head at one row (most CTAs for a
+    // single token), the whole group (up to 8 heads) in batched steps (each
+    // K/V element read once per group); HALE_ATTN_GC overrides both
+    d->gqa = hd <= 256 && hd % 4 == 0;
+    uint32_t min_cap = d->smem_scores;
+    if (d->gqa) {
+        const uint32_t G = nh / nkv;
+        int gmax = 1;
+        for (int g : {8, 4, 2})
+            if (G % g == 0) { gmax = g; break; }
+        d->gc_batch = gmax;
+        d->gc_one = 1;
+        if (const char* e = std::getenv("HALE_ATTN_GC")) {
+            const int g = std::atoi(e);
+            if ((g == 1 || g == 2 || g == 4 || g == 8) && G % g == 0) d->gc_one = d->gc_batch = g;
+        }
+        for (int gc : {d->gc_one, d->gc_batch}) {
+            const int cap = (int)std::min<uint32_t>((uint32_t)gqa_score_cap(gc), (max_len + 3) & ~3u);
+            d->gqa_cap[gc] = cap;
+            d->gqa_smem[gc] = ((size_t)gc * hd + (size_t)gc * cap + (size_t)kGqaStages * gqa_v_rows((int)hd) * hd) * 4;
+            cudaError_t e = gc == 1 ? allow_smem(attn_gqa_kernel<1>, d->gqa_smem[gc])
+                          : gc == 2 ? allow_smem(attn_gqa_kernel<2>, d->gqa_smem[gc])
+                          : gc == 4 ? allow_smem(attn_gqa_kernel<4>, d->gqa_smem[gc])
+                                    : allow_smem(attn_gqa_kernel<8>, d->gqa_smem[gc]);
+            if (e != cudaSuccess)
+                return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->gqa_smem[gc]));
+            min_cap = std::min<uint32_t>(min_cap, (uint32_t)cap);
+        }
+    }
+    const size_t score_floats = max_len > min_cap ? B * nh * max_len : 4;
     struct { float** p; size_t n; } bufs[] = {{&d->x, B * H}, {&d->normed, B * H}, {&d->delta, B * H},
                                                {&d->qkv, B * qkv_rows}, {&d->attn, B * nh * hd},
                                                {&d->g, B * max_inter}, {&d->u, B * max_inter},
@@ -1863,10 +1899,13 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
     const int H = (int)d->H, hb = (H + 255) / 256;
     const size_t lstride = (size_t)d->n_seqs * d->seq_stride;
     const dim3 eg(hb, n);
+    {
+    ProfScope ps_(ctx, "embed", st);
     switch (d->embed_dtype) {
     case HALE_F32: embed_kernel<0><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
     case HALE_F16: embed_kernel<1><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
     default: embed_kernel<2><<<eg, 256, 0, st>>>(d->embed, H, d->d_rows, d->x); break;
+    }
     }
     if ((r = check_launch(ctx, "embed"))) return r;
     for (uint32_t l = 0; l < d->L; l++) {
@@ -1874,19 +1913,47 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         float* kc = d->kcache + (size_t)l * lstride;
         float* vc = d->vcache + (size_t)l * lstride;
         // the previous layer's FFN residual folds into this norm
-        rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed);
+        {
+            ProfScope ps_(ctx, "rmsnorm", st);
+            rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H,
+                                                         d->normed);
+        }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
-        qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
-            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos, d->rope_sin,
-            d->d_rows, kc, vc, d->seq_stride);
+        {
+            ProfScope ps_(ctx, "qk_rope", st);
+            qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
+                d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos, d->rope_sin,
+                d->d_rows, kc, vc, d->seq_stride);
+        }
         if ((r = check_launch(ctx, "qk_rope"))) return r;
-        (d->hd <= 256 ? attn_decode_kernel<1> : attn_decode_kernel<4>)<<<dim3(d->nh, n), 256, d->attn_smem, st>>>(
-            d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_rows, (int)d->max_len, d->scale, d->scores,
-            d->attn, (int)d->smem_scores, d->seq_stride, attn_v_rows((int)d->hd));
+        {
+            ProfScope ps_(ctx, "attention", st);
+            if (d->gqa) {
+                const int gc = n * d->nkv >= 32 ? d->gc_batch : d->gc_one;
+                const dim3 grid(d->nh / gc, n);
+                const size_t sm = d->gqa_smem[gc];
+                const int cap = d->gqa_cap[gc], vt = gqa_v_rows((int)d->hd);
+#define HALE_GQA(GCV)                                                                                               \
+    attn_gqa_kernel<GCV><<<grid, 256, sm, st>>>(d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_rows,   \
+                                                (int)d->max_len, d->scale, d->scores, d->attn, cap, d->seq_stride, vt)
+                if (gc == 1) HALE_GQA(1);
+                else if (gc == 2) HALE_GQA(2);
+                else if (gc == 4) HALE_GQA(4);
+                else HALE_GQA(8);
+#undef HALE_GQA
+            } else {
+                attn_decode_kernel<4><<<dim3(d->nh, n), 256, d->attn_smem, st>>>(
+                    d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, kc, vc, d->d_rows, (int)d->max_len, d->scale,
+                    d->scores, d->attn, (int)d->smem_scores, d->seq_stride, attn_v_rows((int)d->hd));
+            }
+        }
         if ((r = check_launch(ctx, "attn_decode"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
-        rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+        {
+            ProfScope ps_(ctx, "rmsnorm", st);
+            rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+        }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
             hale_moe_layer m{};
@@ -1906,7 +1973,10 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             if ((r = hale_matrix_matvec(ctx, ly.down, d->h, n, d->delta, nullptr, stream))) return r;
         }
     }
-    rmsnorm_kernel<<<n, 256, (size_t)H * 4, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+    {
+        ProfScope ps_(ctx, "rmsnorm", st);
+        rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+    }
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, st));
     if (logits) {
@@ -1937,14 +2007,15 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     d->h_rows[2] = 0;
     const bool capturing = stream_capturing(stream);
     d->copied_recorded = !capturing;
-    if (d->exec && d->g_logits == logits && d->g_hidden == hidden && !capturing) {
+    // per-kernel profiling (hale_ctx_profile) times eager launches only
+    if (d->exec && d->g_logits == logits && d->g_hidden == hidden && !capturing && !ctx->profiling) {
         CUDA_TRY(ctx, cudaGraphLaunch(d->exec, st));
         CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
         return HALE_OK;
     }
     hale_status r = decoder_enqueue(ctx, d, 1, logits, false, hidden, st);
     if (!r && !capturing) CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
-    if (r || capturing || d->no_graph) return r;
+    if (r || capturing || d->no_graph || ctx->profiling) return r;
     // capture the step for the following calls with these outputs
     if (d->exec) {
         cudaGraphExecDestroy(d->exec);

@@ -37,13 +37,14 @@ __global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32
 
 // The residual add x += delta (transformer.rs residual; delta nullable), then
 // RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
-// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA per
-// row (blockIdx.x); x is staged in shared memory by all threads so the one
-// sequential chain runs at the add's latency, not a global load's. Dynamic
-// shared memory: n floats.
+// -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA per row
+// (blockIdx.x). All threads stage v and the squares v*v in shared memory, so
+// the one sequential chain is FADDs alone over 16-byte shared loads issued
+// ahead of it. Dynamic shared memory: 2 n floats.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                float eps, int n, float* __restrict__ out) {
-    extern __shared__ float s_v[];
+    extern __shared__ __align__(16) float s_v[];  // [n] v, then [n] v*v
+    float* s_sq = s_v + n;
     __shared__ float s_scale;
     x += (size_t)blockIdx.x * n;
     out += (size_t)blockIdx.x * n;
@@ -52,12 +53,22 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
         const float v = delta ? fadd(x[i], delta[i]) : x[i];
         if (delta) x[i] = v;
         s_v[i] = v;
+        s_sq[i] = fmul(v, v);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         float s = -0.0f;
-#pragma unroll 16
-        for (int i = 0; i < n; i++) s = fadd(s, fmul(s_v[i], s_v[i]));
+        int i = 0;
+        if ((n & 3) == 0) {
+            const float4* q4 = reinterpret_cast<const float4*>(s_sq);
+#pragma unroll 8
+            for (; i < n / 4; i++) {
+                const float4 q = q4[i];
+                s = fadd(fadd(fadd(fadd(s, q.x), q.y), q.z), q.w);
+            }
+            i = n;
+        }
+        for (; i < n; i++) s = fadd(s, s_sq[i]);
         s_scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)n), eps)));
     }
     __syncthreads();
@@ -258,6 +269,205 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
     for (int q = 0; q < CMAX; q++) {
         const int i = tid + q * 256;
         if (i < hd) ctx[(size_t)h * hd + i] = c[q];
+    }
+}
+
+// Attention for GC query heads that share one KV head (GQA group; GC divides
+// nh / nkv), one CTA of 256 threads per (head chunk, row): each K and V
+// element is read once for the chunk's heads, and every thread runs GC
+// independent chains. Per head the arithmetic is Attention::forward's
+// (attention.rs:59-85) in attn_decode_kernel's order: scores[t] = (sum_i
+// q_i k_ti from -0) * scale; softmax over t = 0..pos; ctx_i = sum_t p_t v_ti
+// from 0, t ascending.
+//   - V rows start streaming into shared memory (kGqaStages stages of vt
+//     rows, 16-byte cp.async) before the scores are computed;
+//   - scores: thread per position, 16-byte key loads issued ahead of the GC
+//     chains, q of the chunk's heads in shared memory;
+//   - context: thread per (column, head subset), scores read four positions
+//     at a time.
+// Scores live in shared memory ([GC][sc_cap]) when pos + 1 <= sc_cap, else in
+// the [n][nh][max_len] scratch. Dynamic shared memory: GC*hd + GC*sc_cap +
+// kGqaStages*vt*hd floats (sc_cap a multiple of 4). hd <= 256, hd % 4 == 0.
+constexpr int kGqaStages = 4;
+
+// V rows [tile * vt, +vt) of the KV head (vbase = its column 0) into stage
+// tile % kGqaStages, then a commit (empty past the last tile).
+__device__ __forceinline__ void gqa_stage_v(float* s_v, const float* __restrict__ vbase, int tile, int n_tiles,
+                                            int vt, int seq, int hd, int kvd, int tid) {
+    if (tile < n_tiles) {
+        float* dst = s_v + (size_t)(tile % kGqaStages) * vt * hd;
+        const int t0 = tile * vt, here = min(vt, seq - t0), q4n = hd >> 2;
+        for (int j = tid; j < here * q4n; j += 256) {
+            const int tt = j / q4n, c4 = j - tt * q4n;
+            cp_async16(dst + tt * hd + 4 * c4, vbase + (size_t)(t0 + tt) * kvd + 4 * c4);
+        }
+    }
+    cp_async_commit();
+}
+
+// Shared-memory score capacity (positions) of attn_gqa_kernel<GC>.
+__host__ __device__ inline int gqa_score_cap(int gc) { return gc == 1 ? 8192 : (gc <= 4 ? 4096 : 2048); }
+// V rows per stage: 32 KB stages, a multiple of 4 rows (the context loop
+// reads scores four positions at a time from 16-byte-aligned offsets).
+__host__ __device__ inline int gqa_v_rows(int hd) { return (8192 / hd) & ~3; }
+
+template <int GC>
+__global__ void __launch_bounds__(256) attn_gqa_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
+                                                       const float* __restrict__ kcache,
+                                                       const float* __restrict__ vcache,
+                                                       const uint32_t* __restrict__ rows, int max_len, float scale,
+                                                       float* __restrict__ scores, float* __restrict__ ctx,
+                                                       int sc_cap, size_t seq_stride, int vt) {
+    extern __shared__ __align__(16) float s_gqa[];
+    __shared__ float s_red[8][GC];
+    __shared__ float s_mx[GC], s_sum[GC];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.y;
+    const int h0 = blockIdx.x * GC, G = nh / nkv;
+    const int seq = (int)rows[3 * r + 1] + 1, kvd = nkv * hd, off = (h0 / G) * hd, q4n = hd >> 2;
+    const size_t sbase = (size_t)rows[3 * r + 2] * seq_stride;
+    const float* kbase = kcache + sbase + off;
+    const float* vbase = vcache + sbase + off;
+    float* s_q = s_gqa;                                   // [GC][hd]
+    float* s_sc = s_q + GC * hd;                           // [GC][sc_cap]
+    float* s_v = s_sc + (size_t)GC * sc_cap;              // [kGqaStages][vt][hd]
+    const bool in_smem = seq <= sc_cap;
+    const size_t sc_stride = in_smem ? (size_t)sc_cap : (size_t)max_len;
+    float* sc = in_smem ? s_sc : scores + ((size_t)r * nh + h0) * max_len;
+    const int n_tiles = (seq + vt - 1) / vt;
+    // V prefetch: the first stages are in flight during the score phase
+#pragma unroll
+    for (int st = 0; st < kGqaStages - 1; st++) gqa_stage_v(s_v, vbase, st, n_tiles, vt, seq, hd, kvd, tid);
+    const float* qrow = qkv + (size_t)r * (nh + 2 * nkv) * hd + (size_t)h0 * hd;
+    for (int i = tid; i < GC * hd; i += 256) s_q[i] = qrow[i];
+    __syncthreads();
+
+    // ---- scores ----
+    float mx[GC];
+#pragma unroll
+    for (int g = 0; g < GC; g++) mx[g] = -__int_as_float(0x7f800000);
+    const float4* sq4 = reinterpret_cast<const float4*>(s_q);
+    for (int t = tid; t < seq; t += 256) {
+        const float4* key = reinterpret_cast<const float4*>(kbase + (size_t)t * kvd);
+        float acc[GC];
+#pragma unroll
+        for (int g = 0; g < GC; g++) acc[g] = -0.0f;
+#pragma unroll 8
+        for (int i4 = 0; i4 < q4n; i4++) {
+            const float4 k4 = key[i4];
+#pragma unroll
+            for (int g = 0; g < GC; g++) {
+                const float4 q = sq4[g * q4n + i4];
+                float a = acc[g];
+                a = fadd(a, fmul(q.x, k4.x));
+                a = fadd(a, fmul(q.y, k4.y));
+                a = fadd(a, fmul(q.z, k4.z));
+                a = fadd(a, fmul(q.w, k4.w));
+                acc[g] = a;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GC; g++) {
+            const float sv = fmul(acc[g], scale);
+            sc[(size_t)g * sc_stride + t] = sv;
+            mx[g] = fmaxf(mx[g], sv);
+        }
+    }
+    // max per head (order-independent)
+#pragma unroll
+    for (int g = 0; g < GC; g++) {
+        float m = mx[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[warp][g] = m;
+    }
+    __syncthreads();
+    if (tid < GC) {
+        float m = -__int_as_float(0x7f800000);
+        for (int w = 0; w < 8; w++) m = fmaxf(m, s_red[w][tid]);
+        s_mx[tid] = m;
+    }
+    __syncthreads();
+    for (int j = tid; j < GC * seq; j += 256) {
+        const int g = j / seq, t = j - g * seq;
+        float* p = sc + (size_t)g * sc_stride + t;
+        *p = hale_expf(fsub(*p, s_mx[g]));
+    }
+    __syncthreads();
+    // the reference's left-to-right denominator, one thread per head
+    if (tid < GC) {
+        const float* row = sc + (size_t)tid * sc_stride;
+        float sum = 0.0f;
+        int t = 0;
+        if (in_smem) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 8
+            for (; t + 4 <= seq; t += 4) {
+                const float4 e = r4[t >> 2];
+                sum = fadd(fadd(fadd(fadd(sum, e.x), e.y), e.z), e.w);
+            }
+        }
+        for (; t < seq; t++) sum = fadd(sum, row[t]);
+        s_sum[tid] = sum;
+    }
+    __syncthreads();
+    for (int j = tid; j < GC * seq; j += 256) {
+        const int g = j / seq, t = j - g * seq;
+        float* p = sc + (size_t)g * sc_stride + t;
+        *p = fdiv(*p, s_sum[g]);
+    }
+
+    // ---- context ----
+    const int tpc = 256 / hd;            // thread groups over the columns
+    const int gi = tid / hd, col = tid - gi * hd;
+    constexpr int HPT = GC;              // upper bound of heads per thread
+    float c[HPT];
+#pragma unroll
+    for (int j = 0; j < HPT; j++) c[j] = 0.0f;
+    for (int tile = 0; tile < n_tiles; tile++) {
+        gqa_stage_v(s_v, vbase, tile + kGqaStages - 1, n_tiles, vt, seq, hd, kvd, tid);
+        cp_async_wait<kGqaStages - 1>();
+        __syncthreads();
+        const float* vt_ = s_v + (size_t)(tile % kGqaStages) * vt * hd + col;
+        const int t0 = tile * vt, here = min(vt, seq - t0);
+        if (gi < tpc) {
+            int tt = 0;
+            if (in_smem) {
+                for (; tt + 4 <= here; tt += 4) {
+                    const float v0 = vt_[tt * hd], v1 = vt_[(tt + 1) * hd], v2 = vt_[(tt + 2) * hd],
+                                v3 = vt_[(tt + 3) * hd];
+#pragma unroll
+                    for (int j = 0; j < HPT; j++) {
+                        const int g = gi + j * tpc;
+                        if (g < GC) {
+                            const float4 p4 = *reinterpret_cast<const float4*>(sc + (size_t)g * sc_stride + t0 + tt);
+                            float a = c[j];
+                            a = fadd(a, fmul(p4.x, v0));
+                            a = fadd(a, fmul(p4.y, v1));
+                            a = fadd(a, fmul(p4.z, v2));
+                            a = fadd(a, fmul(p4.w, v3));
+                            c[j] = a;
+                        }
+                    }
+                }
+            }
+            for (; tt < here; tt++) {
+                const float v = vt_[tt * hd];
+#pragma unroll
+                for (int j = 0; j < HPT; j++) {
+                    const int g = gi + j * tpc;
+                    if (g < GC) c[j] = fadd(c[j], fmul(sc[(size_t)g * sc_stride + t0 + tt], v));
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (gi < tpc) {
+        float* out = ctx + (size_t)r * nh * hd + (size_t)h0 * hd;
+#pragma unroll
+        for (int j = 0; j < HPT; j++) {
+            const int g = gi + j * tpc;
+            if (g < GC) out[(size_t)g * hd + col] = c[j];
+        }
     }
 }
 
