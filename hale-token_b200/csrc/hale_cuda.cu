@@ -1861,7 +1861,7 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
         for (int gc : {d->gc_one, d->gc_batch}) {
             const int cap = (int)std::min<uint32_t>((uint32_t)gqa_score_cap(gc), (max_len + 3) & ~3u);
             d->gqa_cap[gc] = cap;
-            d->gqa_smem[gc] = ((size_t)gc * hd + (size_t)gc * cap + (size_t)kGqaStages * gqa_v_rows((int)hd) * hd) * 4;
+            d->gqa_smem[gc] = gqa_smem_floats(gc, cap, (int)hd) * 4;
             cudaError_t e = gc == 1 ? allow_smem(attn_gqa_kernel<1>, d->gqa_smem[gc])
                           : gc == 2 ? allow_smem(attn_gqa_kernel<2>, d->gqa_smem[gc])
                           : gc == 4 ? allow_smem(attn_gqa_kernel<4>, d->gqa_smem[gc])

@@ -274,42 +274,89 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const float* __restric
 
 // Attention for GC query heads that share one KV head (GQA group; GC divides
 // nh / nkv), one CTA of 256 threads per (head chunk, row): each K and V
-// element is read once for the chunk's heads, and every thread runs GC
-// independent chains. Per head the arithmetic is Attention::forward's
-// (attention.rs:59-85) in attn_decode_kernel's order: scores[t] = (sum_i
-// q_i k_ti from -0) * scale; softmax over t = 0..pos; ctx_i = sum_t p_t v_ti
-// from 0, t ascending.
-//   - V rows start streaming into shared memory (kGqaStages stages of vt
-//     rows, 16-byte cp.async) before the scores are computed;
-//   - scores: thread per position, 16-byte key loads issued ahead of the GC
-//     chains, q of the chunk's heads in shared memory;
-//   - context: thread per (column, head subset), scores read four positions
-//     at a time.
+// element is read once for the chunk's heads. Per head the arithmetic is
+// Attention::forward's (attention.rs:59-85) in attn_decode_kernel's order:
+// scores[t] = (sum_i q_i k_ti from -0) * scale; softmax over t = 0..pos;
+// ctx_i = sum_t p_t v_ti from 0, t ascending.
+//   - K, then V, stream through kGqaStages shared-memory stages with 16-byte
+//     cp.async copies, consecutive threads on consecutive bytes of a row;
+//     K rows are padded to hd + 4 floats so the score threads' 16-byte reads
+//     of 8 different rows hit distinct banks;
+//   - scores: thread (position p of a 64-row tile, head group hg) runs the
+//     chains of heads hg, hg + 4, ...; q sits in shared memory;
+//   - the first V stages load while the softmax runs;
+//   - context: thread (column, head subset), four positions per step with
+//     the loads of the next steps issued ahead.
 // Scores live in shared memory ([GC][sc_cap]) when pos + 1 <= sc_cap, else in
-// the [n][nh][max_len] scratch. Dynamic shared memory: GC*hd + GC*sc_cap +
-// kGqaStages*vt*hd floats (sc_cap a multiple of 4). hd <= 256, hd % 4 == 0.
+// the [n][nh][max_len] scratch. hd <= 256, hd % 4 == 0. Dynamic shared
+// memory: gqa_smem_floats(gc, cap, hd) floats.
 constexpr int kGqaStages = 4;
-
-// V rows [tile * vt, +vt) of the KV head (vbase = its column 0) into stage
-// tile % kGqaStages, then a commit (empty past the last tile).
-__device__ __forceinline__ void gqa_stage_v(float* s_v, const float* __restrict__ vbase, int tile, int n_tiles,
-                                            int vt, int seq, int hd, int kvd, int tid) {
-    if (tile < n_tiles) {
-        float* dst = s_v + (size_t)(tile % kGqaStages) * vt * hd;
-        const int t0 = tile * vt, here = min(vt, seq - t0), q4n = hd >> 2;
-        for (int j = tid; j < here * q4n; j += 256) {
-            const int tt = j / q4n, c4 = j - tt * q4n;
-            cp_async16(dst + tt * hd + 4 * c4, vbase + (size_t)(t0 + tt) * kvd + 4 * c4);
-        }
-    }
-    cp_async_commit();
-}
+constexpr int kGqaTK = 64;  // positions per K tile
 
 // Shared-memory score capacity (positions) of attn_gqa_kernel<GC>.
 __host__ __device__ inline int gqa_score_cap(int gc) { return gc == 1 ? 8192 : (gc <= 4 ? 4096 : 2048); }
 // V rows per stage: 32 KB stages, a multiple of 4 rows (the context loop
 // reads scores four positions at a time from 16-byte-aligned offsets).
 __host__ __device__ inline int gqa_v_rows(int hd) { return (8192 / hd) & ~3; }
+__host__ __device__ inline int gqa_stage_floats(int hd) {
+    const int k = kGqaTK * (hd + 4), v = gqa_v_rows(hd) * hd;
+    return k > v ? k : v;
+}
+__host__ __device__ inline size_t gqa_smem_floats(int gc, int cap, int hd) {
+    return (size_t)gc * hd + (size_t)gc * cap + (size_t)kGqaStages * gqa_stage_floats(hd);
+}
+
+// Rows [tile * rows, +rows) of one KV head (src = its column 0, rows kvd
+// floats apart) into stage tile % kGqaStages with destination row pitch
+// `pitch` floats, then a commit (an empty group past the last tile keeps the
+// wait count uniform). Thread tid copies 16-byte chunk (tid mod q4n) of every
+// (256 / q4n)-th row when q4n divides 256.
+__device__ __forceinline__ void gqa_stage(float* stages, int sfl, const float* __restrict__ src, int tile,
+                                          int n_tiles, int rows, int pitch, int seq, int hd, int kvd, int tid) {
+    if (tile < n_tiles) {
+        float* dst = stages + (size_t)(tile % kGqaStages) * sfl;
+        const int t0 = tile * rows, here = min(rows, seq - t0), q4n = hd >> 2;
+        if ((256 % q4n) == 0) {
+            const int c4 = tid % q4n, step = 256 / q4n;
+            for (int tt = tid / q4n; tt < here; tt += step)
+                cp_async16(dst + tt * pitch + 4 * c4, src + (size_t)(t0 + tt) * kvd + 4 * c4);
+        } else {
+            for (int j = tid; j < here * q4n; j += 256) {
+                const int tt = j / q4n, c4 = j - tt * q4n;
+                cp_async16(dst + tt * pitch + 4 * c4, src + (size_t)(t0 + tt) * kvd + 4 * c4);
+            }
+        }
+    }
+    cp_async_commit();
+}
+
+// One score chain step block: 8 key float4 and the matching q float4 of
+// each head loaded first, then the 32 chain steps of every head.
+template <int HN, int GC>
+__device__ __forceinline__ void gqa_score_block(const float4* __restrict__ key, const float4* __restrict__ sq4,
+                                                int q4n, int hg, int i0, float (&acc)[HN]) {
+    float4 kb[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) kb[u] = key[i0 + u];
+#pragma unroll
+    for (int j = 0; j < HN; j++) {
+        const int g = hg + 4 * j;
+        if (g < GC) {
+            float4 qb[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) qb[u] = sq4[g * q4n + i0 + u];
+            float a = acc[j];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                a = fadd(a, fmul(qb[u].x, kb[u].x));
+                a = fadd(a, fmul(qb[u].y, kb[u].y));
+                a = fadd(a, fmul(qb[u].z, kb[u].z));
+                a = fadd(a, fmul(qb[u].w, kb[u].w));
+            }
+            acc[j] = a;
+        }
+    }
+}
 
 template <int GC>
 __global__ void __launch_bounds__(256) attn_gqa_kernel(const float* __restrict__ qkv, int nh, int nkv, int hd,
@@ -321,64 +368,87 @@ __global__ void __launch_bounds__(256) attn_gqa_kernel(const float* __restrict__
     extern __shared__ __align__(16) float s_gqa[];
     __shared__ float s_red[8][GC];
     __shared__ float s_mx[GC], s_sum[GC];
+    __shared__ uint64_t s_tab[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.y;
     const int h0 = blockIdx.x * GC, G = nh / nkv;
     const int seq = (int)rows[3 * r + 1] + 1, kvd = nkv * hd, off = (h0 / G) * hd, q4n = hd >> 2;
     const size_t sbase = (size_t)rows[3 * r + 2] * seq_stride;
     const float* kbase = kcache + sbase + off;
     const float* vbase = vcache + sbase + off;
+    const int sfl = gqa_stage_floats(hd), kp = hd + 4;
     float* s_q = s_gqa;                                   // [GC][hd]
     float* s_sc = s_q + GC * hd;                           // [GC][sc_cap]
-    float* s_v = s_sc + (size_t)GC * sc_cap;              // [kGqaStages][vt][hd]
+    float* stages = s_sc + (size_t)GC * sc_cap;           // [kGqaStages][sfl]
     const bool in_smem = seq <= sc_cap;
-    const size_t sc_stride = in_smem ? (size_t)sc_cap : (size_t)max_len;
-    float* sc = in_smem ? s_sc : scores + ((size_t)r * nh + h0) * max_len;
-    const int n_tiles = (seq + vt - 1) / vt;
-    // V prefetch: the first stages are in flight during the score phase
+    float* g_sc = scores + ((size_t)r * nh + h0) * max_len;  // used when !in_smem
+    const int nk = (seq + kGqaTK - 1) / kGqaTK;
 #pragma unroll
-    for (int st = 0; st < kGqaStages - 1; st++) gqa_stage_v(s_v, vbase, st, n_tiles, vt, seq, hd, kvd, tid);
+    for (int st = 0; st < kGqaStages - 1; st++) gqa_stage(stages, sfl, kbase, st, nk, kGqaTK, kp, seq, hd, kvd, tid);
     const float* qrow = qkv + (size_t)r * (nh + 2 * nkv) * hd + (size_t)h0 * hd;
     for (int i = tid; i < GC * hd; i += 256) s_q[i] = qrow[i];
-    __syncthreads();
+    if (tid < 32) s_tab[tid] = kExp2TabDev[tid];
 
-    // ---- scores ----
-    float mx[GC];
+    // ---- scores: thread (p, hg) runs heads hg, hg + 4, ... of position p ----
+    const int p = tid & (kGqaTK - 1), hg = tid / kGqaTK;  // a warp has one hg
+    constexpr int HN = (GC + 3) / 4;
+    float mx[HN];
 #pragma unroll
-    for (int g = 0; g < GC; g++) mx[g] = -__int_as_float(0x7f800000);
+    for (int j = 0; j < HN; j++) mx[j] = -__int_as_float(0x7f800000);
+    if (tid < 8 * GC) s_red[tid / GC][tid % GC] = -__int_as_float(0x7f800000);
     const float4* sq4 = reinterpret_cast<const float4*>(s_q);
-    for (int t = tid; t < seq; t += 256) {
-        const float4* key = reinterpret_cast<const float4*>(kbase + (size_t)t * kvd);
-        float acc[GC];
+    for (int tile = 0; tile < nk; tile++) {
+        gqa_stage(stages, sfl, kbase, tile + kGqaStages - 1, nk, kGqaTK, kp, seq, hd, kvd, tid);
+        cp_async_wait<kGqaStages - 1>();
+        __syncthreads();
+        const int t = tile * kGqaTK + p;
+        if (t < seq && hg < GC) {
+            const float4* key = reinterpret_cast<const float4*>(stages + (size_t)(tile % kGqaStages) * sfl + p * kp);
+            float acc[HN];
 #pragma unroll
-        for (int g = 0; g < GC; g++) acc[g] = -0.0f;
-#pragma unroll 8
-        for (int i4 = 0; i4 < q4n; i4++) {
-            const float4 k4 = key[i4];
+            for (int j = 0; j < HN; j++) acc[j] = -0.0f;
+            int i0 = 0;
+            for (; i0 + 8 <= q4n; i0 += 8) gqa_score_block<HN, GC>(key, sq4, q4n, hg, i0, acc);
+            for (; i0 < q4n; i0++) {
+                const float4 k4 = key[i0];
 #pragma unroll
-            for (int g = 0; g < GC; g++) {
-                const float4 q = sq4[g * q4n + i4];
-                float a = acc[g];
-                a = fadd(a, fmul(q.x, k4.x));
-                a = fadd(a, fmul(q.y, k4.y));
-                a = fadd(a, fmul(q.z, k4.z));
-                a = fadd(a, fmul(q.w, k4.w));
-                acc[g] = a;
+                for (int j = 0; j < HN; j++) {
+                    const int g = hg + 4 * j;
+                    if (g < GC) {
+                        const float4 q = sq4[g * q4n + i0];
+                        float a = acc[j];
+                        a = fadd(a, fmul(q.x, k4.x));
+                        a = fadd(a, fmul(q.y, k4.y));
+                        a = fadd(a, fmul(q.z, k4.z));
+                        a = fadd(a, fmul(q.w, k4.w));
+                        acc[j] = a;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < HN; j++) {
+                const int g = hg + 4 * j;
+                if (g < GC) {
+                    const float sv = fmul(acc[j], scale);
+                    if (in_smem) s_sc[g * sc_cap + t] = sv;
+                    else g_sc[(size_t)g * max_len + t] = sv;
+                    mx[j] = fmaxf(mx[j], sv);
+                }
             }
         }
-#pragma unroll
-        for (int g = 0; g < GC; g++) {
-            const float sv = fmul(acc[g], scale);
-            sc[(size_t)g * sc_stride + t] = sv;
-            mx[g] = fmaxf(mx[g], sv);
-        }
+        __syncthreads();
     }
-    // max per head (order-independent)
+    // V streams in while the softmax runs
+    const int nv = (seq + vt - 1) / vt;
 #pragma unroll
-    for (int g = 0; g < GC; g++) {
-        float m = mx[g];
+    for (int st = 0; st < kGqaStages - 1; st++) gqa_stage(stages, sfl, vbase, st, nv, vt, hd, seq, hd, kvd, tid);
+    // max per head (order-independent): each warp reduces the heads of its hg
+#pragma unroll
+    for (int j = 0; j < HN; j++) {
+        float m = mx[j];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_red[warp][g] = m;
+        const int g = hg + 4 * j;
+        if (lane == 0 && g < GC) s_red[warp][g] = m;
     }
     __syncthreads();
     if (tid < GC) {
@@ -387,81 +457,111 @@ __global__ void __launch_bounds__(256) attn_gqa_kernel(const float* __restrict__
         s_mx[tid] = m;
     }
     __syncthreads();
-    for (int j = tid; j < GC * seq; j += 256) {
-        const int g = j / seq, t = j - g * seq;
-        float* p = sc + (size_t)g * sc_stride + t;
-        *p = hale_expf(fsub(*p, s_mx[g]));
+#pragma unroll
+    for (int g = 0; g < GC; g++) {
+        const float m = s_mx[g];
+        if (in_smem)
+            for (int t = tid; t < seq; t += 256) s_sc[g * sc_cap + t] = hale_expf_tab(fsub(s_sc[g * sc_cap + t], m), s_tab);
+        else
+            for (int t = tid; t < seq; t += 256)
+                g_sc[(size_t)g * max_len + t] = hale_expf_tab(fsub(g_sc[(size_t)g * max_len + t], m), s_tab);
     }
     __syncthreads();
     // the reference's left-to-right denominator, one thread per head
     if (tid < GC) {
-        const float* row = sc + (size_t)tid * sc_stride;
         float sum = 0.0f;
-        int t = 0;
         if (in_smem) {
+            const float* row = s_sc + tid * sc_cap;
             const float4* r4 = reinterpret_cast<const float4*>(row);
-#pragma unroll 8
-            for (; t + 4 <= seq; t += 4) {
-                const float4 e = r4[t >> 2];
-                sum = fadd(fadd(fadd(fadd(sum, e.x), e.y), e.z), e.w);
+            int t = 0;
+            for (; t + 16 <= seq; t += 16) {
+                const float4 e0 = r4[t >> 2], e1 = r4[(t >> 2) + 1], e2 = r4[(t >> 2) + 2], e3 = r4[(t >> 2) + 3];
+                sum = fadd(fadd(fadd(fadd(sum, e0.x), e0.y), e0.z), e0.w);
+                sum = fadd(fadd(fadd(fadd(sum, e1.x), e1.y), e1.z), e1.w);
+                sum = fadd(fadd(fadd(fadd(sum, e2.x), e2.y), e2.z), e2.w);
+                sum = fadd(fadd(fadd(fadd(sum, e3.x), e3.y), e3.z), e3.w);
             }
+            for (; t < seq; t++) sum = fadd(sum, row[t]);
+        } else {
+            const float* row = g_sc + (size_t)tid * max_len;
+            for (int t = 0; t < seq; t++) sum = fadd(sum, row[t]);
         }
-        for (; t < seq; t++) sum = fadd(sum, row[t]);
         s_sum[tid] = sum;
     }
     __syncthreads();
-    for (int j = tid; j < GC * seq; j += 256) {
-        const int g = j / seq, t = j - g * seq;
-        float* p = sc + (size_t)g * sc_stride + t;
-        *p = fdiv(*p, s_sum[g]);
+#pragma unroll
+    for (int g = 0; g < GC; g++) {
+        const float sm = s_sum[g];
+        if (in_smem)
+            for (int t = tid; t < seq; t += 256) s_sc[g * sc_cap + t] = fdiv(s_sc[g * sc_cap + t], sm);
+        else
+            for (int t = tid; t < seq; t += 256) g_sc[(size_t)g * max_len + t] = fdiv(g_sc[(size_t)g * max_len + t], sm);
     }
 
-    // ---- context ----
-    const int tpc = 256 / hd;            // thread groups over the columns
+    // ---- context: thread (col, gi) runs heads gi, gi + tpc, ... ----
+    const int tpc = 256 / hd;
     const int gi = tid / hd, col = tid - gi * hd;
-    constexpr int HPT = GC;              // upper bound of heads per thread
+    const bool busy = gi < tpc && gi < GC;
+    constexpr int HPT = GC;  // upper bound of heads per thread
     float c[HPT];
 #pragma unroll
     for (int j = 0; j < HPT; j++) c[j] = 0.0f;
-    for (int tile = 0; tile < n_tiles; tile++) {
-        gqa_stage_v(s_v, vbase, tile + kGqaStages - 1, n_tiles, vt, seq, hd, kvd, tid);
+    for (int tile = 0; tile < nv; tile++) {
+        gqa_stage(stages, sfl, vbase, tile + kGqaStages - 1, nv, vt, hd, seq, hd, kvd, tid);
         cp_async_wait<kGqaStages - 1>();
         __syncthreads();
-        const float* vt_ = s_v + (size_t)(tile % kGqaStages) * vt * hd + col;
+        const float* vt_ = stages + (size_t)(tile % kGqaStages) * sfl + col;
         const int t0 = tile * vt, here = min(vt, seq - t0);
-        if (gi < tpc) {
+        if (busy) {
             int tt = 0;
             if (in_smem) {
-                for (; tt + 4 <= here; tt += 4) {
-                    const float v0 = vt_[tt * hd], v1 = vt_[(tt + 1) * hd], v2 = vt_[(tt + 2) * hd],
-                                v3 = vt_[(tt + 3) * hd];
+                // blocks of 16 positions: the 16 v values and each head's 16
+                // scores are loaded before the block's chain steps
+                for (; tt + 16 <= here; tt += 16) {
+                    float vb[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++) vb[u] = vt_[(tt + u) * hd];
 #pragma unroll
                     for (int j = 0; j < HPT; j++) {
                         const int g = gi + j * tpc;
                         if (g < GC) {
-                            const float4 p4 = *reinterpret_cast<const float4*>(sc + (size_t)g * sc_stride + t0 + tt);
+                            const float4* p4 = reinterpret_cast<const float4*>(s_sc + g * sc_cap + t0 + tt);
+                            const float4 a0 = p4[0], a1 = p4[1], a2 = p4[2], a3 = p4[3];
                             float a = c[j];
-                            a = fadd(a, fmul(p4.x, v0));
-                            a = fadd(a, fmul(p4.y, v1));
-                            a = fadd(a, fmul(p4.z, v2));
-                            a = fadd(a, fmul(p4.w, v3));
+                            a = fadd(a, fmul(a0.x, vb[0]));  a = fadd(a, fmul(a0.y, vb[1]));
+                            a = fadd(a, fmul(a0.z, vb[2]));  a = fadd(a, fmul(a0.w, vb[3]));
+                            a = fadd(a, fmul(a1.x, vb[4]));  a = fadd(a, fmul(a1.y, vb[5]));
+                            a = fadd(a, fmul(a1.z, vb[6]));  a = fadd(a, fmul(a1.w, vb[7]));
+                            a = fadd(a, fmul(a2.x, vb[8]));  a = fadd(a, fmul(a2.y, vb[9]));
+                            a = fadd(a, fmul(a2.z, vb[10])); a = fadd(a, fmul(a2.w, vb[11]));
+                            a = fadd(a, fmul(a3.x, vb[12])); a = fadd(a, fmul(a3.y, vb[13]));
+                            a = fadd(a, fmul(a3.z, vb[14])); a = fadd(a, fmul(a3.w, vb[15]));
                             c[j] = a;
                         }
                     }
                 }
-            }
-            for (; tt < here; tt++) {
-                const float v = vt_[tt * hd];
+                for (; tt < here; tt++) {
+                    const float v = vt_[tt * hd];
 #pragma unroll
-                for (int j = 0; j < HPT; j++) {
-                    const int g = gi + j * tpc;
-                    if (g < GC) c[j] = fadd(c[j], fmul(sc[(size_t)g * sc_stride + t0 + tt], v));
+                    for (int j = 0; j < HPT; j++) {
+                        const int g = gi + j * tpc;
+                        if (g < GC) c[j] = fadd(c[j], fmul(s_sc[g * sc_cap + t0 + tt], v));
+                    }
+                }
+            } else {
+                for (; tt < here; tt++) {
+                    const float v = vt_[tt * hd];
+#pragma unroll
+                    for (int j = 0; j < HPT; j++) {
+                        const int g = gi + j * tpc;
+                        if (g < GC) c[j] = fadd(c[j], fmul(g_sc[(size_t)g * max_len + t0 + tt], v));
+                    }
                 }
             }
         }
         __syncthreads();
     }
-    if (gi < tpc) {
+    if (busy) {
         float* out = ctx + (size_t)r * nh * hd + (size_t)h0 * hd;
 #pragma unroll
         for (int j = 0; j < HPT; j++) {
