@@ -291,8 +291,8 @@ def run_decode(args):
     for _ in range(n_prof):
         dec.step(toks[:, pos], np.full(B, pos), seq_ids, logits=logits)
         pos += 1
-    names = ("embed", "rmsnorm", "fgemv", "qk_rope", "attention", "router", "expert_gate_up", "expert_down",
-             "silu_mul")
+    names = ("embed", "rmsnorm", "fgemv", "lm_head", "qk_rope", "attention", "router", "expert_gate_up",
+             "expert_down", "silu_mul")
     kernels = {}
     for nm in names:
         cnt, tot = ctx.profile_read(nm)

@@ -646,15 +646,18 @@ static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float
         return check_launch(ctx, "fgemv_lanes_batch");
     }
     if (m->lanes) {
-        const unsigned grid = (m->rows_pad / 4 + 7) / 8;
+        // 8 warps (32 rows) per CTA when that still gives every SM two CTAs;
+        // otherwise 4 warps, so a decode-size matrix spreads over more SMs
+        const unsigned wpc = m->rows_pad / 32 >= 2u * (unsigned)ctx->sm_count ? 8u : 4u;
+        const unsigned grid = (m->rows_pad / 4 + wpc - 1) / wpc, threads = 32 * wpc;
         const size_t smem = (size_t)m->cols * 4;
         for (uint32_t t = 0; t < M; t++) {
             const float* xt = x + (size_t)t * m->cols;
             float* ot = out + (size_t)t * m->rows;
             switch (m->dtype) {
-            case HALE_F32: fgemv_lanes_kernel<0><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
-            case HALE_F16: fgemv_lanes_kernel<1><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
-            default: fgemv_lanes_kernel<2><<<grid, 256, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            case HALE_F32: fgemv_lanes_kernel<0><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            case HALE_F16: fgemv_lanes_kernel<1><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
+            default: fgemv_lanes_kernel<2><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
             }
         }
         return check_launch(ctx, "fgemv_lanes");
@@ -1837,7 +1840,7 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     // longer contexts keep scores in a [rows][heads][max_len] scratch
     d->smem_scores = std::min<uint32_t>(max_len, 8192u);
     d->attn_smem = ((size_t)hd + ((d->smem_scores + 3) & ~3u) + (size_t)kAttnStages * attn_v_rows((int)hd) * hd) * 4;
-    if (allow_smem(rmsnorm_kernel, (size_t)H * 8) != cudaSuccess ||
+    if (allow_smem(rmsnorm_kernel, (size_t)H * 12) != cudaSuccess ||
         allow_smem(attn_decode_kernel<1>, d->attn_smem) != cudaSuccess ||
         allow_smem(attn_decode_kernel<4>, d->attn_smem) != cudaSuccess)
         return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->attn_smem));
@@ -1853,12 +1856,13 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
         for (int g : {8, 4, 2})
             if (G % g == 0) { gmax = g; break; }
         d->gc_batch = gmax;
-        d->gc_one = 1;
+        d->gc_one = 0;  // 0: chosen per step from the row count
         if (const char* e = std::getenv("HALE_ATTN_GC")) {
             const int g = std::atoi(e);
             if ((g == 1 || g == 2 || g == 4 || g == 8) && G % g == 0) d->gc_one = d->gc_batch = g;
         }
-        for (int gc : {d->gc_one, d->gc_batch}) {
+        for (int gc : {1, 2, 4, 8}) {
+            if (G % gc != 0 || gc > gmax) continue;
             const int cap = (int)std::min<uint32_t>((uint32_t)gqa_score_cap(gc), (max_len + 3) & ~3u);
             d->gqa_cap[gc] = cap;
             d->gqa_smem[gc] = gqa_smem_floats(gc, cap, (int)hd) * 4;
@@ -1915,7 +1919,7 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         // the previous layer's FFN residual folds into this norm
         {
             ProfScope ps_(ctx, "rmsnorm", st);
-            rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H,
+            rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H,
                                                          d->normed);
         }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
@@ -1930,7 +1934,14 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         {
             ProfScope ps_(ctx, "attention", st);
             if (d->gqa) {
-                const int gc = n * d->nkv >= 32 ? d->gc_batch : d->gc_one;
+                // the most heads per CTA (each K/V element read once per group)
+                // that still gives about two thirds of the SMs a CTA
+                int gc = d->gc_one;
+                if (gc == 0) {
+                    gc = 1;
+                    for (int g = d->gc_batch; g > 1; g /= 2)
+                        if ((d->nh / d->nkv) % g == 0 && (size_t)n * d->nh / g >= 96) { gc = g; break; }
+                }
                 const dim3 grid(d->nh / gc, n);
                 const size_t sm = d->gqa_smem[gc];
                 const int cap = d->gqa_cap[gc], vt = gqa_v_rows((int)d->hd);
@@ -1952,7 +1963,7 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
         {
             ProfScope ps_(ctx, "rmsnorm", st);
-            rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+            rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
         }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
@@ -1975,11 +1986,12 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
     }
     {
         ProfScope ps_(ctx, "rmsnorm", st);
-        rmsnorm_kernel<<<n, 256, (size_t)H * 8, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
     }
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, st));
     if (logits) {
+        ProfScope ps_(ctx, "lm_head", st);
         if (last_logits) return hale_matrix_matvec(ctx, d->lm_head, d->normed + (size_t)(n - 1) * H, 1, logits, nullptr, stream);
         return hale_matrix_matvec(ctx, d->lm_head, d->normed, n, logits, nullptr, stream);
     }

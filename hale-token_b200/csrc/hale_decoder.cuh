@@ -38,22 +38,27 @@ __global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32
 // The residual add x += delta (transformer.rs residual; delta nullable), then
 // RmsNorm::forward (src/ops/norm.rs:7-28): s = sum of v*v left to right from
 // -0; scale = 1 / sqrt(s / n + eps); out = (x * scale) * w. One CTA per row
-// (blockIdx.x). All threads stage v and the squares v*v in shared memory, so
-// the one sequential chain is FADDs alone over 16-byte shared loads issued
-// ahead of it. Dynamic shared memory: 2 n floats.
+// (blockIdx.x). All threads stage v, the squares v*v and w in shared memory
+// with every global load issued up front, so the one sequential chain is
+// FADDs alone over 16-byte shared loads issued ahead of it and the output
+// pass reads no global memory. Dynamic shared memory: 3 n floats.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
                                float eps, int n, float* __restrict__ out) {
-    extern __shared__ __align__(16) float s_v[];  // [n] v, then [n] v*v
+    extern __shared__ __align__(16) float s_v[];  // [n] v, [n] v*v, [n] w
     float* s_sq = s_v + n;
+    float* s_w = s_sq + n;
     __shared__ float s_scale;
     x += (size_t)blockIdx.x * n;
     out += (size_t)blockIdx.x * n;
     if (delta) delta += (size_t)blockIdx.x * n;
+#pragma unroll 4
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = delta ? fadd(x[i], delta[i]) : x[i];
+        const float xv = x[i], dv = delta ? delta[i] : 0.0f, wv = w[i];
+        const float v = delta ? fadd(xv, dv) : xv;
         if (delta) x[i] = v;
         s_v[i] = v;
         s_sq[i] = fmul(v, v);
+        s_w[i] = wv;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -73,7 +78,7 @@ __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ 
     }
     __syncthreads();
     const float scale = s_scale;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fmul(fmul(s_v[i], scale), w[i]);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fmul(fmul(s_v[i], scale), s_w[i]);
 }
 
 // Per head (one warp each; q heads, then k heads, then v heads): the in-place

@@ -1058,6 +1058,40 @@ __device__ __forceinline__ void load8(const uint8_t* p, float (&w)[8]) {
     }
 }
 
+// Raw 16-byte words of one lane's 8 weights (DT 1/2: one uint4 of 8 halves;
+// DT 0: two uint4 of 4 floats), loaded ahead and decoded when used.
+template <int DT>
+struct Raw8 {
+    uint4 a, b;
+};
+template <int DT>
+__device__ __forceinline__ void raw8_load(const uint8_t* p, Raw8<DT>& r) {
+    r.a = __ldg(reinterpret_cast<const uint4*>(p));
+    if (DT == 0) r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+}
+template <int DT>
+__device__ __forceinline__ void raw8_decode(const Raw8<DT>& r, float (&w)[8]) {
+    if (DT == 0) {
+        w[0] = __uint_as_float(r.a.x); w[1] = __uint_as_float(r.a.y);
+        w[2] = __uint_as_float(r.a.z); w[3] = __uint_as_float(r.a.w);
+        w[4] = __uint_as_float(r.b.x); w[5] = __uint_as_float(r.b.y);
+        w[6] = __uint_as_float(r.b.z); w[7] = __uint_as_float(r.b.w);
+    } else {
+        const uint32_t u[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint16_t lo = (uint16_t)(u[q] & 0xffffu), hi = (uint16_t)(u[q] >> 16);
+            if (DT == 2) {
+                w[2 * q] = __uint_as_float((uint32_t)lo << 16);
+                w[2 * q + 1] = __uint_as_float((uint32_t)hi << 16);
+            } else {
+                w[2 * q] = half_bits_to_float(lo);
+                w[2 * q + 1] = half_bits_to_float(hi);
+            }
+        }
+    }
+}
+
 template <int DT, int TG>
 __global__ void __launch_bounds__(128) fgemv_kernel(const uint8_t* __restrict__ W, int rows,
                                                     int cols, int steps,
@@ -1125,19 +1159,50 @@ __global__ void __launch_bounds__(128) fgemv_kernel(const uint8_t* __restrict__ 
 template <int DT>
 __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restrict__ W, int rows, int cols,
                                                           const float* __restrict__ x, float* __restrict__ out) {
-    extern __shared__ float s_x[];  // [cols]
+    extern __shared__ __align__(16) float s_x[];  // [cols]
     constexpr int ES = DT == 0 ? 4 : 2;
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[i] = x[i];
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        float4* s4 = reinterpret_cast<float4*>(s_x);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) s4[i] = x4[i];
+    } else {
+        for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[i] = x[i];
+    }
     __syncthreads();
     const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (q * 4 >= rows) return;
     const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
     const uint8_t* base = W + (((size_t)q * S8 * 4 + rr) * 64 + l * 8) * ES;
+    const size_t sstep = (size_t)4 * 64 * ES;
     float acc = 0.0f;
-#pragma unroll 8
-    for (int s = 0; s < S8; s++) {
+    // blocks of 8 steps: the next block's weights are in flight while this
+    // block's chain runs (the chain alone is ~6 cycles a step)
+    constexpr int BS = 8;
+    int s = 0;
+    if (S8 >= BS) {
+        Raw8<DT> cur[BS];
+#pragma unroll
+        for (int u = 0; u < BS; u++) raw8_load<DT>(base + (size_t)u * sstep, cur[u]);
+        for (; s + BS <= S8; s += BS) {
+            Raw8<DT> nxt[BS];
+            const int ns = s + BS + BS <= S8 ? s + BS : s;  // the last block reloads itself (unused)
+#pragma unroll
+            for (int u = 0; u < BS; u++) raw8_load<DT>(base + (size_t)(ns + u) * sstep, nxt[u]);
+#pragma unroll
+            for (int u = 0; u < BS; u++) {
+                float w[8];
+                raw8_decode<DT>(cur[u], w);
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc = fadd(acc, fmul(w[j], s_x[(8 * (s + u) + j) * 8 + l]));
+            }
+#pragma unroll
+            for (int u = 0; u < BS; u++) cur[u] = nxt[u];
+        }
+    }
+    for (; s < S8; s++) {
         float w[8];
-        load8<DT>(base + (size_t)s * 4 * 64 * ES, w);
+        load8<DT>(base + (size_t)s * sstep, w);
 #pragma unroll
         for (int j = 0; j < 8; j++) acc = fadd(acc, fmul(w[j], s_x[(8 * s + j) * 8 + l]));
     }
