@@ -749,11 +749,23 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         const int tok = blockIdx.x * kRouterTT + tt;
         if (tok >= a.M) break;
         const float* lg = a.logits + (size_t)tok * a.E;
-        float mx = -__int_as_float(0x7f800000);
-        for (int i = lane; i < a.E; i += 32) mx = fmaxf(mx, __ldcg(lg + i));
+        // the token's logits (E <= 256) read once into registers
+        float lv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = lane + 32 * j;
+            lv[j] = i < a.E ? __ldcg(lg + i) : -__int_as_float(0x7f800000);
+        }
+        float mx = lv[0];
+#pragma unroll
+        for (int j = 1; j < 8; j++) mx = fmaxf(mx, lv[j]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        for (int i = lane; i < a.E; i += 32) s_e[warp][i] = hale_expf_tab(fsub(__ldcg(lg + i), mx), s_tab);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = lane + 32 * j;
+            if (i < a.E) s_e[warp][i] = hale_expf_tab(fsub(lv[j], mx), s_tab);
+        }
         __syncwarp();
         // the reference's left-to-right sum, on one lane, loads batched 4 wide
         float sum = 0.0f;
@@ -809,18 +821,26 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         }
         __syncwarp();
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        a.tile_cnt[blockIdx.x] = 0u;
-        s_flag = (atomicAdd(a.grid_cnt, 1u) == gridDim.x - 1) ? 1u : 0u;
+    if (gridDim.x == 1) {
+        // one token tile: this CTA is also the last of the grid, and its own
+        // writes are visible to all its threads after the barrier
+        __syncthreads();
+        if (tid == 0) a.tile_cnt[blockIdx.x] = 0u;
+        if (!a.elist_off) return;
+    } else {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            a.tile_cnt[blockIdx.x] = 0u;
+            s_flag = (atomicAdd(a.grid_cnt, 1u) == gridDim.x - 1) ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!s_flag || !a.elist_off) {
+            if (s_flag && tid == 0) *a.grid_cnt = 0u;
+            return;
+        }
+        __threadfence();
     }
-    __syncthreads();
-    if (!s_flag || !a.elist_off) {
-        if (s_flag && tid == 0) *a.grid_cnt = 0u;
-        return;
-    }
-    __threadfence();
 
     // ---- last CTA of the grid: group routes by expert ----------------------
     const int R = a.M * a.k;
@@ -1146,6 +1166,16 @@ __global__ void __launch_bounds__(128) fgemv_kernel(const uint8_t* __restrict__ 
     }
 }
 
+// Activation staging for the lane-major kernels: element c = (8 s + j) 8 + l
+// (step s, accumulator lane l, j-th value of the lane's step) goes to
+// shared-memory float (s << 6) | ((j >> 2) << 5) | (l << 2) | (j & 3), so
+// lane l reads its step's 8 values as two 16-byte words, and the 8 lanes of a
+// quarter-warp read 128 contiguous bytes.
+__device__ __forceinline__ int lanes_x_slot(int c) {
+    const int s = c >> 6, j = (c >> 3) & 7, l = c & 7;
+    return (s << 6) | ((j >> 2) << 5) | (l << 2) | (j & 3);
+}
+
 // Float matvec for one activation row in the lane-major layout (cols a
 // multiple of 64): in each group of 4 rows, for each group of 8 steps (a step
 // = 8 columns), row rr's lane l holds its 8 consecutive step values
@@ -1163,13 +1193,19 @@ __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restr
     constexpr int ES = DT == 0 ? 4 : 2;
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const float4* x4 = reinterpret_cast<const float4*>(x);
-        float4* s4 = reinterpret_cast<float4*>(s_x);
 #pragma unroll 4
-        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) s4[i] = x4[i];
+        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+            const float4 v = x4[i];
+            s_x[lanes_x_slot(4 * i)] = v.x;
+            s_x[lanes_x_slot(4 * i + 1)] = v.y;
+            s_x[lanes_x_slot(4 * i + 2)] = v.z;
+            s_x[lanes_x_slot(4 * i + 3)] = v.w;
+        }
     } else {
-        for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[i] = x[i];
+        for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[lanes_x_slot(i)] = x[i];
     }
     __syncthreads();
+    const float4* s_x4 = reinterpret_cast<const float4*>(s_x);
     const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (q * 4 >= rows) return;
     const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
@@ -1193,8 +1229,11 @@ __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restr
             for (int u = 0; u < BS; u++) {
                 float w[8];
                 raw8_decode<DT>(cur[u], w);
-#pragma unroll
-                for (int j = 0; j < 8; j++) acc = fadd(acc, fmul(w[j], s_x[(8 * (s + u) + j) * 8 + l]));
+                const float4 xa = s_x4[((s + u) << 4) + l], xb = s_x4[((s + u) << 4) + 8 + l];
+                acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
+                acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
+                acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
+                acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
             }
 #pragma unroll
             for (int u = 0; u < BS; u++) cur[u] = nxt[u];
@@ -1203,8 +1242,11 @@ __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restr
     for (; s < S8; s++) {
         float w[8];
         load8<DT>(base + (size_t)s * sstep, w);
-#pragma unroll
-        for (int j = 0; j < 8; j++) acc = fadd(acc, fmul(w[j], s_x[(8 * s + j) * 8 + l]));
+        const float4 xa = s_x4[(s << 4) + l], xb = s_x4[(s << 4) + 8 + l];
+        acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
+        acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
+        acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
+        acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
     }
     const float s1 = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
     const float p = fadd(s1, __shfl_down_sync(0xffffffffu, s1, 1, 8));
@@ -1222,17 +1264,36 @@ template <int DT, int NB>
 __global__ void __launch_bounds__(256) fgemv_lanes_batch_kernel(const uint8_t* __restrict__ W, int rows, int cols,
                                                                 const float* __restrict__ x, int n,
                                                                 float* __restrict__ out) {
-    extern __shared__ float s_xb[];  // [NB][cols]
+    extern __shared__ __align__(16) float s_xb[];  // [NB][cols], each row in lanes_x_slot order
     constexpr int ES = DT == 0 ? 4 : 2;
     const int b0 = blockIdx.y * NB;
     const int nb = min(NB, n - b0);
-    for (int i = threadIdx.x; i < NB * cols; i += blockDim.x)
-        s_xb[i] = i < nb * cols ? x[(size_t)b0 * cols + i] : 0.0f;
+    const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // cols % 64 == 0: every row aligned
+#pragma unroll 1
+    for (int b = 0; b < NB; b++) {
+        const float* xr = x + (size_t)(b0 + b) * cols;
+        float* dst = s_xb + b * cols;
+        if (x16) {
+            const float4* x4 = reinterpret_cast<const float4*>(xr);
+#pragma unroll 4
+            for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+                const float4 v = b < nb ? x4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                dst[lanes_x_slot(4 * i)] = v.x;
+                dst[lanes_x_slot(4 * i + 1)] = v.y;
+                dst[lanes_x_slot(4 * i + 2)] = v.z;
+                dst[lanes_x_slot(4 * i + 3)] = v.w;
+            }
+        } else {
+            for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[lanes_x_slot(c)] = b < nb ? xr[c] : 0.0f;
+        }
+    }
     __syncthreads();
     const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (q * 4 >= rows) return;
     const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
     const uint8_t* base = W + (((size_t)q * S8 * 4 + rr) * 64 + l * 8) * ES;
+    const float4* s_x4 = reinterpret_cast<const float4*>(s_xb);
+    const int c4 = cols >> 2;  // float4 per staged row
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) acc[b] = 0.0f;
@@ -1241,9 +1302,15 @@ __global__ void __launch_bounds__(256) fgemv_lanes_batch_kernel(const uint8_t* _
         float w[8];
         load8<DT>(base + (size_t)s * 4 * 64 * ES, w);
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-#pragma unroll
-            for (int b = 0; b < NB; b++) acc[b] = fadd(acc[b], fmul(w[j], s_xb[b * cols + (8 * s + j) * 8 + l]));
+        for (int b = 0; b < NB; b++) {
+            const float4 xa = s_x4[b * c4 + (s << 4) + l], xb = s_x4[b * c4 + (s << 4) + 8 + l];
+            float a = acc[b];
+            a = fadd(a, fmul(w[0], xa.x)); a = fadd(a, fmul(w[1], xa.y));
+            a = fadd(a, fmul(w[2], xa.z)); a = fadd(a, fmul(w[3], xa.w));
+            a = fadd(a, fmul(w[4], xb.x)); a = fadd(a, fmul(w[5], xb.y));
+            a = fadd(a, fmul(w[6], xb.z)); a = fadd(a, fmul(w[7], xb.w));
+            acc[b] = a;
+        }
     }
     const int row = q * 4 + rr;
 #pragma unroll
