@@ -619,6 +619,7 @@ static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float
     if (m->lanes && M > 1) {
         // several activation rows: each weight step read once per chunk of NB rows
         const unsigned gx = (m->rows_pad / 4 + 7) / 8;
+        // rows per chunk: 96 KB of staged activations at most (two or more CTAs per SM)
         const int NB = m->cols <= 3072 ? 8 : (m->cols <= 6144 ? 4 : 2);
         const dim3 grid(gx, (M + NB - 1) / NB);
         const size_t smem = (size_t)NB * m->cols * 4;
