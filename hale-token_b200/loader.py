@@ -416,6 +416,78 @@ class ModelWeights:
         return fmt.pack_record(*enc)
 
 
+class RoutingStats:
+    """RoutingStats (src/expert/stats.rs:15-130): selection counts per (model
+    layer, expert), flat at layer * num_experts + expert, saved as the
+    reference's JSON ({"num_layers", "num_experts", "counts"}) so a run's
+    routing warms the next start's pinned tier."""
+
+    def __init__(self, num_layers, num_experts, counts=None):
+        self.num_layers, self.num_experts = int(num_layers), int(num_experts)
+        n = self.num_layers * self.num_experts
+        self.counts = np.zeros(n, np.uint64) if counts is None else np.asarray(counts, np.uint64).reshape(-1).copy()
+        if self.counts.size != n:
+            raise LoadError("counter length does not match its shape")
+
+    @staticmethod
+    def from_pool(pool, config):
+        """The counts a pool recorded (pool layer j = j-th MoE layer) placed
+        at their model layers."""
+        st = RoutingStats(config.num_layers, config.num_experts)
+        c = np.asarray(pool.routing_counts(), np.uint64)
+        for j, l in enumerate(l for l in range(config.num_layers) if config.is_moe_layer(l)):
+            st.counts[l * st.num_experts:(l + 1) * st.num_experts] = c[j]
+        return st
+
+    def pool_counts(self, config):
+        """[MoE layers, experts] counts in pool-layer order (for cache_policy)."""
+        rows = [self.counts[l * self.num_experts:(l + 1) * self.num_experts]
+                for l in range(config.num_layers) if config.is_moe_layer(l)]
+        return np.stack(rows) if rows else np.zeros((0, self.num_experts), np.uint64)
+
+    def record(self, layer, expert):
+        self.counts[layer * self.num_experts + expert] += 1
+
+    def count(self, layer, expert):
+        return int(self.counts[layer * self.num_experts + expert])
+
+    def total(self):
+        return int(self.counts.sum())
+
+    def merge(self, other):
+        """Adds counters of the same shape (others are ignored, as stats.rs:64-70)."""
+        if (other.num_layers, other.num_experts) == (self.num_layers, self.num_experts):
+            self.counts += other.counts
+
+    def hottest(self, n):
+        return hottest(self.counts.reshape(self.num_layers, self.num_experts), n)
+
+    def coverage(self, n):
+        """Fraction of all selections that went to the n hottest experts."""
+        t = self.total()
+        return 0.0 if t == 0 else sum(self.count(l, e) for l, e in self.hottest(n)) / t
+
+    def save(self, path):
+        with open(path, "w") as f:
+            json.dump({"num_layers": self.num_layers, "num_experts": self.num_experts,
+                       "counts": [int(c) for c in self.counts]}, f, separators=(",", ":"))
+
+    @staticmethod
+    def load(path):
+        try:
+            with open(path) as f:
+                d = json.load(f)
+            return RoutingStats(d["num_layers"], d["num_experts"], d["counts"])
+        except (OSError, json.JSONDecodeError, KeyError, TypeError, ValueError) as e:
+            if isinstance(e, LoadError):
+                raise
+            raise LoadError(f"{path}: {e}") from None
+
+    def __eq__(self, other):
+        return isinstance(other, RoutingStats) and (self.num_layers, self.num_experts) == \
+            (other.num_layers, other.num_experts) and np.array_equal(self.counts, other.counts)
+
+
 def split_budget(experts_in_ram, total_experts, per_token_experts):
     """planner::split_budget (src/expert/planner.rs:253-267) -> (pinned, lru)
     expert counts: below twice one token's working set an LRU only thrashes
@@ -474,11 +546,14 @@ def load_decoder(ctx, directory, expert_dtype=None, max_len=None, policy=None, e
     dense.safetensors, experts.hpk). Dense weights as stored; experts into an
     HBM-resident pool, or a tiered one when `policy` (a CachePolicy) or
     `expert_hbm_bytes` (planned like the reference's RAM budget, hottest
-    experts of `routing_counts` pinned first) is given. max_len: KV-cache
+    experts of `routing_counts` -- a RoutingStats, or [MoE layers, experts]
+    counts -- pinned first) is given. max_len: KV-cache
     positions (default the config's max_position_embeddings); n_seqs /
     max_batch: KV caches and rows per Decoder.step."""
     w = ModelWeights(directory, expert_dtype)
     cfg = w.config
+    if isinstance(routing_counts, RoutingStats):
+        routing_counts = routing_counts.pool_counts(cfg)
     if policy is None and expert_hbm_bytes is not None:
         policy = cache_policy(cfg, w.record_bytes, expert_hbm_bytes, routing_counts)
     pool = None

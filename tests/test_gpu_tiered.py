@@ -157,7 +157,7 @@ def test_tiered_forward_is_bit_identical_to_resident(ctx, dtype, policy):
     assert (pool.routing_counts() == routed).all()
 
 
-def test_routing_stats_warm_start_pins_the_hottest_experts(ctx):
+def test_routing_stats_warm_start_pins_the_hottest_experts(ctx, tmp_path):
     E, H, I, k = 16, 128, 64, 2
     layers = [fmt.SyntheticLayer(110 + j, E, H, I, fmt.Q8_0) for j in range(2)]
     rb = layers[0].expert_bytes()
@@ -165,10 +165,13 @@ def test_routing_stats_warm_start_pins_the_hottest_experts(ctx):
     upload_all(first, layers)
     for j in range(2):
         _forward(ctx, first, layers[j], j, layers[j].tokens(8, seed=j), k, False)
-    counts = first.routing_counts()
     cfg = loader.ModelConfig.from_hf({"architectures": ["MixtralForCausalLM"], "hidden_size": H,
                                       "intermediate_size": I, "num_hidden_layers": 2, "num_attention_heads": 4,
                                       "vocab_size": 10, "num_local_experts": E, "num_experts_per_tok": k})
+    # saved after the first run and loaded at the next start (stats.rs save / load)
+    loader.RoutingStats.from_pool(first, cfg).save(tmp_path / "routing.json")
+    counts = loader.RoutingStats.load(tmp_path / "routing.json").pool_counts(cfg)
+    assert (counts == first.routing_counts()).all()
     policy = loader.cache_policy(cfg, rb, 4 * rb, counts)   # 4 < 2 x (2 layers x top-2): all pinned
     assert len(policy.pinned) == 4 and policy.lru_bytes == 0
     assert policy.pinned == loader.hottest(counts, 4)

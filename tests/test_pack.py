@@ -189,3 +189,41 @@ def test_cache_policy_from_a_budget():
     big = L.ModelConfig.from_hf(dict(TINY, num_hidden_layers=8, num_local_experts=8))  # 64 experts, 16 per token
     p = L.cache_policy(big, rb, 40 * rb)
     assert len(p.pinned) == 20 and p.lru_bytes == 20 * rb
+
+
+def test_routing_stats_save_load_and_merge(tmp_path):
+    s = L.RoutingStats(1, 3)
+    s.record(0, 2)
+    path = tmp_path / "stats.json"
+    s.save(path)
+    loaded = L.RoutingStats.load(path)
+    assert loaded == s
+    loaded.merge(s)
+    assert loaded.count(0, 2) == 2
+    loaded.merge(L.RoutingStats(2, 3))          # other shapes are ignored
+    assert loaded.total() == 2
+    d = json.loads(path.read_text())
+    assert d == {"num_layers": 1, "num_experts": 3, "counts": [0, 0, 1]}
+    path.write_text('{"num_layers": 2, "num_experts": 3, "counts": [1]}')
+    with pytest.raises(L.LoadError, match="does not match"):
+        L.RoutingStats.load(path)
+
+
+def test_routing_stats_hottest_coverage_and_pool_layers():
+    s = L.RoutingStats(2, 4)
+    for _ in range(5):
+        s.record(1, 2)
+    for _ in range(3):
+        s.record(0, 1)
+    s.record(0, 3)
+    assert s.hottest(10) == [(1, 2), (0, 1), (0, 3)]
+    assert abs(s.coverage(2) - 8 / 9) < 1e-12
+    c = L.ModelConfig.from_hf({"architectures": ["Qwen3MoeForCausalLM"], "hidden_size": 64,
+                               "num_hidden_layers": 3, "num_attention_heads": 4, "vocab_size": 10,
+                               "num_experts": 4, "num_experts_per_tok": 2, "mlp_only_layers": [1]})
+    st = L.RoutingStats(3, 4)
+    st.record(2, 3)                              # model layer 2 = MoE ordinal 1
+    pc = st.pool_counts(c)
+    assert pc.shape == (2, 4) and pc[1, 3] == 1 and pc.sum() == 1
+    p = L.cache_policy(c, 100, 300, pc)         # 3 of 8 experts, below 2 x 4 per token: all pinned
+    assert p.pinned == [(1, 3), (0, 0), (1, 0)] and p.lru_bytes == 0
