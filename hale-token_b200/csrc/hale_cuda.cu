@@ -52,6 +52,22 @@ struct hale_ctx {
     // scratch for unit-level calls
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // bumped whenever ws or scratch is reallocated: CUDA graphs captured
+    // before hold the old addresses and must not be replayed
+    uint64_t ws_gen = 1;
+    // hale_moe_forward_host replays: one captured graph per (pool, layer,
+    // M, host buffers), valid while ws_gen matches
+    struct HostGraph {
+        const hale_pool* pool;
+        hale_moe_layer layer;
+        uint32_t M;
+        const void *x, *out, *idx, *w;
+        uint64_t gen;
+        cudaGraphExec_t exec;
+    };
+    std::vector<HostGraph> host_graphs;
+    cudaStream_t cap_st = nullptr;
+    uint32_t* h_err = nullptr;  // page-locked copy of d_err
     uint64_t launches = 0;
     // per-kernel event timing (hale_ctx_profile)
     bool profiling = false;
@@ -342,9 +358,24 @@ extern "C" hale_status hale_ctx_create(int device, hale_ctx** out) {
     return HALE_OK;
 }
 
+static void drop_host_graphs(hale_ctx* ctx, const hale_pool* pool) {
+    for (size_t i = 0; i < ctx->host_graphs.size();) {
+        if (!pool || ctx->host_graphs[i].pool == pool) {
+            cudaGraphExecDestroy(ctx->host_graphs[i].exec);
+            ctx->host_graphs.erase(ctx->host_graphs.begin() + (long)i);
+        } else {
+            i++;
+        }
+    }
+}
+
 extern "C" void hale_ctx_destroy(hale_ctx* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    drop_host_graphs(ctx, nullptr);
+    if (ctx->cap_st) cudaStreamDestroy(ctx->cap_st);
+    cudaFreeHost(ctx->h_err);
     cudaFree(ctx->d_err);
     cudaFree(ctx->ws);
     cudaFree(ctx->scratch);
@@ -440,6 +471,7 @@ static hale_status ensure_moe_ws(hale_ctx* ctx, int M, int E, int k, int H, int 
     CUDA_TRY(ctx, cudaDeviceSynchronize());
     cudaFree(ctx->ws);
     ctx->ws = nullptr;
+    ctx->ws_gen++;
     CUDA_TRY(ctx, cudaMalloc(&ctx->ws, L.total));
     CUDA_TRY(ctx, cudaMemset(ctx->ws, 0, L.total));
     ctx->ws_bytes = L.total;
@@ -456,6 +488,7 @@ static hale_status ensure_scratch(hale_ctx* ctx, size_t bytes, void* stream) {
     CUDA_TRY(ctx, cudaDeviceSynchronize());
     cudaFree(ctx->scratch);
     ctx->scratch = nullptr;
+    ctx->ws_gen++;
     size_t b = align_up(std::max(bytes, (size_t)1 << 20), 1 << 20);
     CUDA_TRY(ctx, cudaMalloc(&ctx->scratch, b));
     ctx->scratch_bytes = b;
@@ -781,6 +814,7 @@ extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_
 extern "C" void hale_pool_destroy(hale_pool* p) {
     if (!p) return;
     cudaSetDevice(p->ctx->device);
+    drop_host_graphs(p->ctx, p);
     if (p->copy_st) cudaStreamSynchronize(p->copy_st);
     cudaFree(p->data);
     cudaFree(p->staging);
@@ -1429,6 +1463,40 @@ static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, u
     return small ? expert_go<1, 1>(ctx, a, max_active, st) : expert_go<1, 2>(ctx, a, max_active, st);
 }
 
+// The host-buffer call's work on stream st: x in, the layer, results out.
+static hale_status moe_forward_host_enqueue(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly,
+                                            const float* x_host, uint32_t M, float* out_host, int32_t* idx_host,
+                                            float* w_host, cudaStream_t st) {
+    const size_t xb = (size_t)M * p->H * 4, kb = (size_t)M * ly->top_k * 4;
+    uint8_t* s = static_cast<uint8_t*>(ctx->scratch);
+    float* dx = reinterpret_cast<float*>(s);
+    float* dout = reinterpret_cast<float*>(s + align_up(xb, 256));
+    int32_t* didx = reinterpret_cast<int32_t*>(s + 2 * align_up(xb, 256));
+    float* dw = reinterpret_cast<float*>(s + 2 * align_up(xb, 256) + align_up(kb, 256));
+    CUDA_TRY(ctx, cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
+    hale_status r = hale_moe_forward(ctx, p, ly, dx, M, dout, idx_host ? didx : nullptr, w_host ? dw : nullptr, st);
+    if (r) return r;
+    CUDA_TRY(ctx, cudaMemcpyAsync(out_host, dout, xb, cudaMemcpyDeviceToHost, st));
+    if (idx_host) CUDA_TRY(ctx, cudaMemcpyAsync(idx_host, didx, kb, cudaMemcpyDeviceToHost, st));
+    if (w_host) CUDA_TRY(ctx, cudaMemcpyAsync(w_host, dw, kb, cudaMemcpyDeviceToHost, st));
+    return HALE_OK;
+}
+
+static bool host_pinned(const void* p) {
+    if (!p) return true;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+static bool same_layer(const hale_moe_layer& a, const hale_moe_layer& b) {
+    return a.layer == b.layer && a.router == b.router && a.router_dtype == b.router_dtype &&
+           a.n_experts == b.n_experts && a.top_k == b.top_k && a.normalize_topk == b.normalize_topk;
+}
+
 extern "C" hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly,
                                              const float* x_host, uint32_t M, float* out_host,
                                              int32_t* idx_host, float* w_host, void* stream) {
@@ -1441,19 +1509,64 @@ extern "C" hale_status hale_moe_forward_host(hale_ctx* ctx, hale_pool* p, const 
     size_t xb = (size_t)M * p->H * 4, kb = (size_t)M * ly->top_k * 4;
     size_t need = 2 * align_up(xb, 256) + 2 * align_up(kb, 256);
     if ((r = ensure_scratch(ctx, need, stream))) return r;
-    uint8_t* s = static_cast<uint8_t*>(ctx->scratch);
-    float* dx = reinterpret_cast<float*>(s);
-    float* dout = reinterpret_cast<float*>(s + align_up(xb, 256));
-    int32_t* didx = reinterpret_cast<int32_t*>(s + 2 * align_up(xb, 256));
-    float* dw = reinterpret_cast<float*>(s + 2 * align_up(xb, 256) + align_up(kb, 256));
     cudaStream_t st = S(stream);
-    CUDA_TRY(ctx, cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
-    if ((r = hale_moe_forward(ctx, p, ly, dx, M, dout, idx_host ? didx : nullptr, w_host ? dw : nullptr, stream)))
-        return r;
-    CUDA_TRY(ctx, cudaMemcpyAsync(out_host, dout, xb, cudaMemcpyDeviceToHost, st));
-    if (idx_host) CUDA_TRY(ctx, cudaMemcpyAsync(idx_host, didx, kb, cudaMemcpyDeviceToHost, st));
-    if (w_host) CUDA_TRY(ctx, cudaMemcpyAsync(w_host, dw, kb, cudaMemcpyDeviceToHost, st));
-    return hale_ctx_check(ctx, stream);
+    // Repeated calls with the same pool, layer, size and page-locked buffers
+    // replay one CUDA graph of the whole call (copies, three kernels, the
+    // error word): one launch instead of eight. Tiered pools resolve routes
+    // on the host mid-call and always run step by step.
+    const bool graphable = !p->tiered && !ctx->profiling && !stream_capturing(stream);
+    if (graphable) {
+        for (const auto& g : ctx->host_graphs)
+            if (g.pool == p && same_layer(g.layer, *ly) && g.M == M && g.x == x_host && g.out == out_host &&
+                g.idx == idx_host && g.w == w_host && g.gen == ctx->ws_gen) {
+                CUDA_TRY(ctx, cudaGraphLaunch(g.exec, st));
+                CUDA_TRY(ctx, cudaStreamSynchronize(st));
+                if (*ctx->h_err == 0) return HALE_OK;
+                return hale_ctx_check(ctx, stream);
+            }
+    }
+    if ((r = moe_forward_host_enqueue(ctx, p, ly, x_host, M, out_host, idx_host, w_host, st))) return r;
+    r = hale_ctx_check(ctx, stream);
+    if (r || !graphable) return r;
+    // this call sized the workspaces: capture it for the next ones
+    if (!host_pinned(x_host) || !host_pinned(out_host) || !host_pinned(idx_host) || !host_pinned(w_host))
+        return HALE_OK;
+    if (!ctx->cap_st && cudaStreamCreateWithFlags(&ctx->cap_st, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        ctx->cap_st = nullptr;
+        return HALE_OK;
+    }
+    if (!ctx->h_err && cudaHostAlloc(reinterpret_cast<void**>(&ctx->h_err), 4, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        ctx->h_err = nullptr;
+        return HALE_OK;
+    }
+    const uint64_t gen = ctx->ws_gen;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (cudaStreamBeginCapture(ctx->cap_st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return HALE_OK;
+    }
+    hale_status cr = moe_forward_host_enqueue(ctx, p, ly, x_host, M, out_host, idx_host, w_host, ctx->cap_st);
+    const bool copied = cudaMemcpyAsync(ctx->h_err, ctx->d_err, 4, cudaMemcpyDeviceToHost, ctx->cap_st) == cudaSuccess;
+    const cudaError_t ec = cudaStreamEndCapture(ctx->cap_st, &graph);
+    if (cr || !copied || ec != cudaSuccess || !graph || gen != ctx->ws_gen ||
+        cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+        cudaGetLastError();
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        g_thread_status = HALE_OK;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    if (exec) {
+        if (ctx->host_graphs.size() >= 8) {
+            cudaGraphExecDestroy(ctx->host_graphs.front().exec);
+            ctx->host_graphs.erase(ctx->host_graphs.begin());
+        }
+        ctx->host_graphs.push_back({p, *ly, M, x_host, out_host, idx_host, w_host, gen, exec});
+    }
+    return HALE_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -1674,6 +1787,7 @@ struct hale_decoder {
     cudaStream_t cap = nullptr;
     cudaGraphExec_t exec = nullptr;
     float *g_logits = nullptr, *g_hidden = nullptr;
+    uint64_t g_gen = 0;  // ctx->ws_gen the graph was captured against
     bool no_graph = false;
     uint32_t smem_scores = 0;  // attention scores kept in shared memory up to this many positions
     size_t attn_smem = 0;      // attention's dynamic shared memory
@@ -2025,7 +2139,8 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     const bool capturing = stream_capturing(stream);
     d->copied_recorded = !capturing;
     // per-kernel profiling (hale_ctx_profile) times eager launches only
-    if (d->exec && d->g_logits == logits && d->g_hidden == hidden && !capturing && !ctx->profiling) {
+    if (d->exec && d->g_logits == logits && d->g_hidden == hidden && d->g_gen == ctx->ws_gen && !capturing &&
+        !ctx->profiling) {
         CUDA_TRY(ctx, cudaGraphLaunch(d->exec, st));
         CUDA_TRY(ctx, cudaEventRecord(d->ev_copied, st));
         return HALE_OK;
@@ -2055,6 +2170,7 @@ extern "C" hale_status hale_decoder_forward(hale_ctx* ctx, hale_decoder* d, uint
     if (graph) cudaGraphDestroy(graph);
     d->g_logits = logits;
     d->g_hidden = hidden;
+    d->g_gen = ctx->ws_gen;
     return HALE_OK;
 }
 

@@ -327,6 +327,30 @@ def test_moe_forward_host_buffers_and_second_layer(ctx):
     assert ei.value.status == hale.E_INVALID_ARGUMENT
 
 
+def test_moe_forward_host_replays_with_new_inputs(ctx):
+    """Repeated host-buffer calls on the same page-locked buffers replay one
+    captured graph: every call must still read the buffers' current contents
+    and match the oracle, also after the workspace grew in between."""
+    ld = fmt.SyntheticLayer(33, 16, 256, 128, fmt.Q8_0)
+    pool, experts = build_pool(ctx, ld)
+    renc = fmt.encode(fmt.F32, ld.router)
+    layer = hale.moe_layer(0, dev(renc), fmt.F32, 16, 4, True)
+    xh = torch.empty((6, 256), dtype=torch.float32).pin_memory()
+    oh = torch.empty((6, 256), dtype=torch.float32).pin_memory()
+    ih = torch.empty((6, 4), dtype=torch.int32).pin_memory()
+    for step in range(5):
+        if step == 3:   # a bigger call grows the workspace: cached graphs must be dropped
+            big = torch.from_numpy(ld.tokens(1500, seed=77)).cuda()
+            hale.moe_forward(ctx, pool, layer, big, torch.empty_like(big))
+            ctx.check()
+        x = ld.tokens(6, seed=step)
+        xh.copy_(torch.from_numpy(x))
+        hale.moe_forward_host(ctx, pool, layer, xh, oh, ih)
+        want, widx, _ = O.moe_forward(fmt.F32, renc, experts, 4, True, x)
+        assert np.array_equal(ih.numpy(), widx.astype(np.int32)), f"step {step}"
+        assert_bit_equal(oh.numpy(), want, f"host forward step {step}")
+
+
 def test_pool_fetch_keeps_request_order_and_counts(ctx):
     """ExpertProvider::fetch (cache.rs:246-272 analogue)."""
     ld = fmt.SyntheticLayer(41, 4, 64, 32, fmt.Q8_0)
