@@ -8,7 +8,9 @@ files verbatim -- config.json, model.safetensors, expected.json -- and records
 their SHA-256 in MANIFEST.json, so the tests can run where the reference is
 not mounted (the GPU box).
 
-Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
+Usage: python tests/golden/make_golden.py REFERENCE_ROOT
+(REFERENCE_ROOT: the reference crate's checkout; also read from the
+HALE_REFERENCE_ROOT environment variable)
 """
 import hashlib
 import json
@@ -37,4 +39,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HALE_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT")
+    main(root)
