@@ -23,6 +23,7 @@
 #include "hale_stream.cuh"
 #include "hale_ep.cuh"
 #include "hale_decoder.cuh"
+#include "hale_tier.h"
 
 using namespace hale;
 
@@ -90,71 +91,6 @@ struct hale_matrix {
     bool lanes = false;  // float, lane-major layout (fgemv_lanes_kernel); rows_pad = rows rounded to 4
 };
 
-// LruCache (src/expert/lru.rs:40-160) over expert keys 0 .. n-1 (layer * E +
-// expert): a doubly linked recency list in index arrays, every entry of the
-// same weight (one expert record).
-struct KeyLru {
-    std::vector<int64_t> prev, next;
-    std::vector<uint8_t> in;
-    int64_t head = -1, tail = -1;
-    uint64_t used = 0, cap = 0, weight = 0;
-    size_t count = 0;
-
-    void init(size_t n, uint64_t cap_bytes, uint64_t w) {
-        prev.assign(n, -1);
-        next.assign(n, -1);
-        in.assign(n, 0);
-        head = tail = -1;
-        used = 0;
-        cap = cap_bytes;
-        weight = w;
-        count = 0;
-    }
-    void unlink(int64_t k) {
-        if (prev[k] >= 0) next[prev[k]] = next[k]; else head = next[k];
-        if (next[k] >= 0) prev[next[k]] = prev[k]; else tail = prev[k];
-        prev[k] = next[k] = -1;
-    }
-    void push_front(int64_t k) {
-        prev[k] = -1;
-        next[k] = head;
-        if (head >= 0) prev[head] = k;
-        head = k;
-        if (tail < 0) tail = k;
-    }
-    void remove(int64_t k) {
-        unlink(k);
-        in[k] = 0;
-        used -= weight;
-        count--;
-    }
-    // get(): a hit becomes the most recently used entry
-    bool get(int64_t k) {
-        if (!in[k]) return false;
-        unlink(k);
-        push_front(k);
-        return true;
-    }
-    // insert(): evicts from the tail until the entry fits; an entry heavier
-    // than the whole budget is not stored and comes back as evicted
-    void insert(int64_t k, std::vector<int64_t>& evicted) {
-        if (in[k]) remove(k);
-        if (weight > cap) {
-            evicted.push_back(k);
-            return;
-        }
-        while (used + weight > cap) {
-            const int64_t t = tail;
-            remove(t);
-            evicted.push_back(t);
-        }
-        push_front(k);
-        in[k] = 1;
-        used += weight;
-        count++;
-    }
-};
-
 struct hale_pool {
     hale_ctx* ctx;
     hale_dtype dtype;
@@ -172,14 +108,7 @@ struct hale_pool {
     bool tiered = false;
     uint8_t* host_tier = nullptr;          // [L * E] tiled experts, page-locked host memory
     uint8_t* scratch = nullptr;            // one tiled expert (upload of an unpinned key)
-    uint32_t n_slots = 0;
-    std::vector<int32_t> slot_of;          // [L * E] HBM slot or -1
-    std::vector<int64_t> slot_key;         // [n_slots] key or -1
-    std::vector<int32_t> free_slots;
-    std::vector<uint8_t> pinned_key;       // [L * E]
-    KeyLru lru;
-    std::vector<int64_t> held;             // unpinned keys of the request in flight
-    std::vector<uint8_t> held_mark;        // [L * E]
+    hale_tier::Book book;                  // slots, LRU and counters (hale_tier.h)
     int32_t* d_slot = nullptr;             // [L * E] slot table read by the expert kernels
     int32_t* h_slot = nullptr;             // page-locked staging of one layer's row [E]
     int32_t* h_routes = nullptr;           // page-locked read-back of a forward's routes
@@ -862,18 +791,20 @@ extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, 
     p->tiered = true;
     p->expert_stride = 2 * tiled_bytes(dtype, inter, hidden) + tiled_bytes(dtype, hidden, inter);
     p->record_bytes = 2 * (size_t)inter * hale_row_bytes(dtype, hidden) + (size_t)hidden * hale_row_bytes(dtype, inter);
-    p->pinned_key.assign(nk, 0);
-    uint64_t n_pinned = 0;
-    for (uint64_t i = 0; i < policy->n_pinned; i++) {
-        const size_t key = (size_t)policy->pinned[i].layer * n_experts + policy->pinned[i].expert;
-        if (!p->pinned_key[key]) n_pinned++;
-        p->pinned_key[key] = 1;
-    }
+    std::vector<int64_t> pinned(policy->n_pinned);
+    for (uint64_t i = 0; i < policy->n_pinned; i++)
+        pinned[i] = (int64_t)policy->pinned[i].layer * n_experts + policy->pinned[i].expert;
     // slots: the pinned tier, the LRU at full budget, and one forward's
     // distinct experts (at most one layer's E) held while the LRU evicts them
-    const uint64_t lru_cap = policy->lru_bytes / p->record_bytes;
-    p->n_slots = (uint32_t)std::min<uint64_t>(nk, n_pinned + lru_cap + n_experts);
-    const size_t dev_bytes = p->expert_stride * p->n_slots;
+    std::vector<uint8_t> seen(nk, 0);
+    uint64_t n_pinned = 0;
+    for (int64_t k : pinned)
+        if (!seen[k]) {
+            seen[k] = 1;
+            n_pinned++;
+        }
+    const uint32_t n_slots = hale_tier::Book::slots_needed(nk, n_pinned, policy->lru_bytes, p->record_bytes, n_experts);
+    const size_t dev_bytes = p->expert_stride * n_slots;
     bool ok = cudaMalloc(&p->data, dev_bytes) == cudaSuccess &&
               cudaMalloc(&p->staging, p->record_bytes) == cudaSuccess &&
               cudaMalloc(&p->scratch, p->expert_stride) == cudaSuccess &&
@@ -895,19 +826,7 @@ extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, 
     p->resident.assign(nk, 0);
     p->layer_resident.assign(n_layers, 0);
     p->host_routing.assign(nk, 0);
-    p->slot_of.assign(nk, -1);
-    p->slot_key.assign(p->n_slots, -1);
-    p->held_mark.assign(nk, 0);
-    p->lru.init(nk, policy->lru_bytes, p->record_bytes);
-    // pinned keys take the first slots for good
-    uint32_t next = 0;
-    for (size_t key = 0; key < nk; key++)
-        if (p->pinned_key[key]) {
-            p->slot_of[key] = (int32_t)next;
-            p->slot_key[next] = (int64_t)key;
-            next++;
-        }
-    for (int32_t sl = (int32_t)p->n_slots - 1; sl >= (int32_t)next; sl--) p->free_slots.push_back(sl);
+    p->book.init(nk, pinned, policy->lru_bytes, p->record_bytes, n_slots);  // pinned keys take the first slots
     // CacheStats at construction (cache.rs:96-103)
     p->stats.pinned_experts = n_pinned;
     p->stats.pinned_bytes = n_pinned * p->record_bytes;
@@ -917,18 +836,10 @@ extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, 
 }
 
 extern "C" uint64_t hale_pool_hbm_slots(const hale_pool* p) {
-    return p ? (p->tiered ? p->n_slots : (uint64_t)p->L * p->E) : 0;
+    return p ? (p->tiered ? p->book.n_slots : (uint64_t)p->L * p->E) : 0;
 }
 
 // ---- tier bookkeeping (host) ------------------------------------------------
-
-static void tier_free_slot(hale_pool* p, int64_t key) {
-    const int32_t sl = p->slot_of[key];
-    if (sl < 0) return;
-    p->slot_of[key] = -1;
-    p->slot_key[sl] = -1;
-    p->free_slots.push_back(sl);
-}
 
 // Folds the device-timed duration of the last batch of tier loads into
 // load_seconds once it has completed.
@@ -941,67 +852,24 @@ static void tier_collect_timing(hale_pool* p) {
     p->timing_pending = false;
 }
 
-// The previous request's kernels have completed (the caller synchronised):
-// slots of its experts that no tier keeps become free.
+// The previous request's kernels have completed (waited for here): its held
+// slots are released (hale_tier::Book::release).
 static void tier_release(hale_pool* p) {
     if (p->done_recorded) {
         cudaEventSynchronize(p->ev_done);  // the previous forward may have run on another stream
         p->done_recorded = false;
     }
-    for (int64_t key : p->held) {
-        p->held_mark[key] = 0;
-        if (!p->pinned_key[key] && !p->lru.in[key]) tier_free_slot(p, key);
-    }
-    p->held.clear();
+    p->book.release();
     tier_collect_timing(p);
 }
 
-// ExpertCache::fetch (cache.rs:124-194) for one request: routing recorded,
-// pass 1 serves pinned and LRU hits (a hit refreshes recency), pass 2 loads
-// the misses in request order and inserts them into the LRU. Every expert of
-// the request keeps its slot until the next release, even if a later insert
-// evicts it from the LRU. A miss whose bytes are still in a held slot needs
-// no copy (it counts as a miss all the same). Copies to issue go to `loads`.
+// One ExpertCache::fetch request through the book; copies to issue go to
+// `loads`.
 static hale_status tier_request(hale_pool* p, const int64_t* keys, size_t n,
                                 std::vector<std::pair<int32_t, int64_t>>& loads) {
-    for (size_t i = 0; i < n; i++) p->host_routing[keys[i]]++;
-    uint64_t pinned_hits = 0, lru_hits = 0;
-    std::vector<int64_t> missing;
-    for (size_t i = 0; i < n; i++) {
-        const int64_t key = keys[i];
-        if (p->pinned_key[key]) {
-            pinned_hits++;
-            continue;
-        }
-        if (!p->held_mark[key]) {
-            p->held_mark[key] = 1;
-            p->held.push_back(key);
-        }
-        if (p->lru.get(key)) lru_hits++;
-        else missing.push_back(key);
-    }
-    std::vector<int64_t> evicted;
-    for (int64_t key : missing) {
-        if (p->slot_of[key] < 0) {
-            if (p->free_slots.empty())
-                return fail(p->ctx, HALE_E_OUT_OF_MEMORY, "tiered pool ran out of HBM slots (%u)", p->n_slots);
-            const int32_t sl = p->free_slots.back();
-            p->free_slots.pop_back();
-            p->slot_of[key] = sl;
-            p->slot_key[sl] = key;
-            loads.emplace_back(sl, key);
-        }
-        evicted.clear();
-        p->lru.insert(key, evicted);
-        for (int64_t ev : evicted)
-            if (!p->held_mark[ev]) tier_free_slot(p, ev);
-    }
-    p->stats.pinned_hits += pinned_hits;
-    p->stats.lru_hits += lru_hits;
-    p->stats.misses += missing.size();
-    p->stats.bytes_loaded += (uint64_t)missing.size() * p->record_bytes;
-    p->stats.lru_experts = p->lru.count;
-    p->stats.lru_bytes = p->lru.used;
+    if (!p->book.request(keys, n, loads))
+        return fail(p->ctx, HALE_E_OUT_OF_MEMORY, "tiered pool ran out of HBM slots (%u): one request names more "
+                    "distinct experts than a layer has", p->book.n_slots);
     return HALE_OK;
 }
 
@@ -1047,7 +915,8 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
     // tiered: a pinned key is tiled straight into its slot, any other through
     // the scratch expert; both then land in the host tier
     uint8_t* dst = !p->tiered ? p->data + i * p->expert_stride
-                              : (p->pinned_key[i] ? p->data + (size_t)p->slot_of[i] * p->expert_stride : p->scratch);
+                              : (p->book.pinned_key[i] ? p->data + (size_t)p->book.slot_of[i] * p->expert_stride
+                                                       : p->scratch);
     size_t proj = (size_t)p->I * hale_row_bytes(p->dtype, p->H);
     size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
     hale_status r;
@@ -1057,8 +926,8 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
     if (p->tiered) {
         CUDA_TRY(ctx, cudaMemcpyAsync(p->host_tier + i * p->expert_stride, dst, p->expert_stride,
                                       cudaMemcpyDeviceToHost, st));
-        if (!p->pinned_key[i] && p->slot_of[i] >= 0)
-            CUDA_TRY(ctx, cudaMemcpyAsync(p->data + (size_t)p->slot_of[i] * p->expert_stride, dst, p->expert_stride,
+        if (!p->book.pinned_key[i] && p->book.slot_of[i] >= 0)
+            CUDA_TRY(ctx, cudaMemcpyAsync(p->data + (size_t)p->book.slot_of[i] * p->expert_stride, dst, p->expert_stride,
                                           cudaMemcpyDeviceToDevice, st));
     }
     CUDA_TRY(ctx, cudaStreamSynchronize(st));
@@ -1107,7 +976,7 @@ extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys
         CUDA_TRY(ctx, cudaStreamSynchronize(p->copy_st));
         const size_t gu_tiled = tiled_bytes(p->dtype, p->I, p->H);
         for (uint64_t i = 0; i < n; i++) {
-            const uint8_t* base = p->data + (size_t)p->slot_of[ks[i]] * p->expert_stride;
+            const uint8_t* base = p->data + (size_t)p->book.slot_of[ks[i]] * p->expert_stride;
             out[i].gate = base;
             out[i].up = base + gu_tiled;
             out[i].down = base + 2 * gu_tiled;
@@ -1148,7 +1017,8 @@ extern "C" hale_status hale_pool_routing_counts(hale_pool* p, uint64_t* counts, 
     std::vector<uint64_t> dev(total);
     CUDA_TRY(p->ctx, cudaDeviceSynchronize());
     CUDA_TRY(p->ctx, cudaMemcpy(dev.data(), p->d_routing, total * 8, cudaMemcpyDeviceToHost));
-    for (size_t i = 0; i < total; i++) counts[i] = dev[i] + p->host_routing[i];
+    for (size_t i = 0; i < total; i++)
+        counts[i] = dev[i] + p->host_routing[i] + (p->tiered ? p->book.routing[i] : 0);
     return HALE_OK;
 }
 
@@ -1163,6 +1033,12 @@ extern "C" hale_status hale_pool_stats(hale_pool* p, hale_cache_stats* out) {
         // routes were counted on the host as they were resolved
         tier_collect_timing(p);
         *out = p->stats;
+        out->pinned_hits = p->book.c.pinned_hits;
+        out->lru_hits = p->book.c.lru_hits;
+        out->misses = p->book.c.misses;
+        out->bytes_loaded = p->book.c.bytes_loaded;
+        out->lru_experts = p->book.lru.count;
+        out->lru_bytes = p->book.lru.used;
         return HALE_OK;
     }
     *out = p->stats;
@@ -1368,7 +1244,7 @@ static hale_status tier_forward(hale_pool* p, uint32_t layer, const int* d_route
     }
     hale_status r = tier_issue(p, loads, st);
     if (r) return r;
-    for (uint32_t e = 0; e < p->E; e++) p->h_slot[e] = p->slot_of[(size_t)layer * p->E + e];
+    for (uint32_t e = 0; e < p->E; e++) p->h_slot[e] = p->book.slot_of[(size_t)layer * p->E + e];
     CUDA_TRY(ctx, cudaMemcpyAsync(p->d_slot + (size_t)layer * p->E, p->h_slot, (size_t)p->E * 4,
                                   cudaMemcpyHostToDevice, st));
     return HALE_OK;
