@@ -1835,8 +1835,8 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     // longer contexts keep scores in a [rows][heads][max_len] scratch
     d->smem_scores = std::min<uint32_t>(max_len, 8192u);
     d->attn_smem = ((size_t)hd + ((d->smem_scores + 3) & ~3u) + (size_t)kAttnStages * attn_v_rows((int)hd) * hd) * 4;
+    // attn_decode_kernel serves head_dim > 256 only (attn_gqa_kernel the rest)
     if (allow_smem(rmsnorm_kernel, (size_t)H * 12) != cudaSuccess ||
-        allow_smem(attn_decode_kernel<1>, d->attn_smem) != cudaSuccess ||
         allow_smem(attn_decode_kernel<4>, d->attn_smem) != cudaSuccess)
         return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->attn_smem));
     const size_t B = max_batch;
