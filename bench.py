@@ -90,6 +90,8 @@ def oracle_tok_s(ld, encoded, m, budget_s=8.0):
     like rayon) on a bounded sample of the same tokens -> tokens/s."""
     from oracle import oracle as O
     fmt = __import__("importlib").import_module("hale-token_b200.formats")
+    # every core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    O.set_num_threads(len(os.sched_getaffinity(0)), native=True)
     experts = [O.ExpertWeights(fmt.Q4_0, H, I, *encoded[e]) for e in range(E)]
     renc = fmt.encode(fmt.F32, ld.router)
     x = ld.tokens(m)
@@ -330,6 +332,7 @@ def run_decode(args):
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return
     fmt = __import__("importlib").import_module("hale-token_b200.formats")
@@ -348,7 +351,7 @@ def run_reference(args):
         "metric": "decode_tok_s_moe_layer", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights x i8 activations, f32 accumulate",
-        "data": "synthetic", "config": config(m, 1), "impl": "reference",
+        "data": "synthetic", "config": config(m, world), "impl": "reference",
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
                          "sample": f"each step: >=2 s of the layer over up to 8 of the {m} tokens, repeated; "
                                    f"oracle/hale_oracle.c -O2 -march=native, OpenMP {cores} threads on {cpu_model()}"},

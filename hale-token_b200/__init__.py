@@ -90,6 +90,7 @@ SIGNATURES = {
     "hale_ctx_check": (I32, [P, P]),
     "hale_ctx_launch_count": (U64, [P]),
     "hale_ctx_profile": (I32, [P, C.c_int]),
+    "hale_ctx_set_expert_kernel": (I32, [P, C.c_int]),
     "hale_ctx_profile_read": (I32, [P, C.c_char_p, C.POINTER(U64), C.POINTER(C.c_double)]),
     "hale_row_bytes": (I64, [C.c_int, U64]),
     "hale_matrix_create": (I32, [P, C.c_int, U32, U32, P, U64, C.c_int, C.POINTER(P)]),
@@ -181,26 +182,18 @@ class Context:
     expert_kernel picks the expert-kernel family for this context: "auto"
     (by batch shape), "tc" (tcgen05 kernels), "ps" (persistent streaming
     warp-MMA kernels) or "dp4a" (per-CTA kernels); the first two wherever the
-    shapes allow.
-    The library reads it from HALE_EXPERT_KERNEL when the context is created;
-    None leaves that variable as it is.
+    shapes allow (hale_ctx_set_expert_kernel).
     """
+
+    FAMILIES = {"auto": 0, "tc": 1, "dp4a": 2, "ps": 3}
 
     def __init__(self, device=0, expert_kernel=None):
         h = P()
-        old = os.environ.get("HALE_EXPERT_KERNEL")
+        if expert_kernel is not None and expert_kernel not in self.FAMILIES:
+            raise ValueError(f"expert_kernel must be one of {sorted(self.FAMILIES)}, not {expert_kernel!r}")
+        _check(lib().hale_ctx_create(device, C.byref(h)))
         if expert_kernel is not None:
-            if expert_kernel not in ("auto", "tc", "ps", "dp4a"):
-                raise ValueError(f"expert_kernel must be auto, tc, ps or dp4a, not {expert_kernel!r}")
-            os.environ["HALE_EXPERT_KERNEL"] = expert_kernel
-        try:
-            _check(lib().hale_ctx_create(device, C.byref(h)))
-        finally:
-            if expert_kernel is not None:
-                if old is None:
-                    os.environ.pop("HALE_EXPERT_KERNEL", None)
-                else:
-                    os.environ["HALE_EXPERT_KERNEL"] = old
+            _check(lib().hale_ctx_set_expert_kernel(h, self.FAMILIES[expert_kernel]), h)
         self.h = h
         self.device = device
 

@@ -38,10 +38,10 @@ thread_local hale_status g_thread_status = HALE_OK;
 struct hale_ctx {
     int device = 0;
     int sm_count = 0;
-    // expert kernel family (environment HALE_EXPERT_KERNEL): 0 "auto" = by
-    // batch shape, 1 "tc" = tcgen05 kernels, 2 "dp4a" = per-CTA kernels
-    // (dp4a / warp MMA), 3 "ps" = persistent streaming warp-MMA kernels;
-    // each where the shapes allow, else the per-CTA kernels
+    // expert kernel family (hale_ctx_set_expert_kernel): HALE_EXPERT_AUTO =
+    // by batch shape, _TC = tcgen05 kernels, _DP4A = per-CTA kernels (dp4a /
+    // warp MMA), _PS = persistent streaming warp-MMA kernels; each where the
+    // shapes allow, else the per-CTA kernels
     int expert_kernel = 0;
     std::string msg;
     hale_status status = HALE_OK;
@@ -273,11 +273,6 @@ extern "C" hale_status hale_ctx_create(int device, hale_ctx** out) {
     hale_ctx* c = new hale_ctx();
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
-    if (const char* ek = std::getenv("HALE_EXPERT_KERNEL")) {
-        if (!std::strcmp(ek, "tc")) c->expert_kernel = 1;
-        else if (!std::strcmp(ek, "dp4a")) c->expert_kernel = 2;
-        else if (!std::strcmp(ek, "ps")) c->expert_kernel = 3;
-    }
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&c->d_err, 4) != cudaSuccess ||
         cudaMemset(c->d_err, 0, 4) != cudaSuccess) {
         delete c;
@@ -311,6 +306,14 @@ extern "C" void hale_ctx_destroy(hale_ctx* ctx) {
     drain_marks(ctx);
     for (cudaEvent_t e : ctx->spare) cudaEventDestroy(e);
     delete ctx;
+}
+
+extern "C" hale_status hale_ctx_set_expert_kernel(hale_ctx* ctx, int family) {
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ctx_set_expert_kernel: ctx is NULL");
+    if (family < HALE_EXPERT_AUTO || family > HALE_EXPERT_PS)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ctx_set_expert_kernel: unknown family %d", family);
+    ctx->expert_kernel = family;
+    return HALE_OK;
 }
 
 extern "C" hale_status hale_ctx_profile(hale_ctx* ctx, int enable) {
@@ -1842,7 +1845,7 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     const size_t B = max_batch;
     // GQA-grouped attention: one CTA per head at one row (most CTAs for a
     // single token), the whole group (up to 8 heads) in batched steps (each
-    // K/V element read once per group); HALE_ATTN_GC overrides both
+    // K/V element read once per group)
     d->gqa = hd <= 256 && hd % 4 == 0;
     uint32_t min_cap = d->smem_scores;
     if (d->gqa) {
@@ -1852,10 +1855,6 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
             if (G % g == 0) { gmax = g; break; }
         d->gc_batch = gmax;
         d->gc_one = 0;  // 0: chosen per step from the row count
-        if (const char* e = std::getenv("HALE_ATTN_GC")) {
-            const int g = std::atoi(e);
-            if ((g == 1 || g == 2 || g == 4 || g == 8) && G % g == 0) d->gc_one = d->gc_batch = g;
-        }
         for (int gc : {1, 2, 4, 8}) {
             if (G % gc != 0 || gc > gmax) continue;
             const int cap = (int)std::min<uint32_t>((uint32_t)gqa_score_cap(gc), (max_len + 3) & ~3u);

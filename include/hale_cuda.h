@@ -87,6 +87,16 @@ HALE_API hale_status hale_last_error(const hale_ctx* ctx, char* buf, size_t len)
 HALE_API hale_status hale_ctx_check(hale_ctx* ctx, void* stream);
 /* Number of this library's kernels launched on ctx so far. */
 HALE_API uint64_t hale_ctx_launch_count(const hale_ctx* ctx);
+/* Expert-kernel family of a context's MoE forwards (default HALE_EXPERT_AUTO:
+ * chosen per call from the batch shape). The others force one family wherever
+ * the layer's shapes allow it: all give bit-identical results; they differ
+ * only in speed. Settings are per context; nothing is read from the process
+ * environment. */
+#define HALE_EXPERT_AUTO 0 /* by batch shape */
+#define HALE_EXPERT_TC 1   /* tcgen05 kind::i8 kernels (TMEM accumulators) */
+#define HALE_EXPERT_DP4A 2 /* per-CTA kernels: dp4a, warp MMA from 3 tokens */
+#define HALE_EXPERT_PS 3   /* persistent streaming warp-MMA kernels */
+HALE_API hale_status hale_ctx_set_expert_kernel(hale_ctx* ctx, int family);
 /* Per-kernel timing: while enabled, every launch on ctx is bracketed by a
  * pair of CUDA events on its stream. hale_ctx_profile_read synchronises,
  * and returns the launches and summed device milliseconds recorded for the
@@ -255,19 +265,21 @@ HALE_API hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* layer, 
 
 /* Routing that allocates nothing. No counterpart in the reference: it exists
  * for hosts that cannot call cudaMalloc on the routing path -- a serving loop
- * replaying captured CUDA graphs (allocation is not permitted inside stream
- * capture and would add a device-wide synchronisation), or an embedding that
- * hands all device memory to its own fixed arena up front. Same arguments and
- * results as hale_moe_route, without a context: it runs on the calling
- * thread's current device. Its scratch (router logits and a few counters) is
- * a fixed 1 MiB array inside this library, held on every GPU that loads the
- * library until the process exits, so m_tokens * n_experts must be at most
- * 261,888 and m_tokens at most 1016 (larger requests are rejected with
+ * that must not add the device-wide synchronisation an allocation can cause
+ * in the middle of a decode step, or an embedding that hands all device
+ * memory to its own fixed arena up front. Same arguments and results as
+ * hale_moe_route, without a context: it runs on the calling thread's current
+ * device. Its scratch (router logits and a few counters) is a fixed 1 MiB
+ * array inside this library, held on every GPU that loads the library until
+ * the process exits, so m_tokens * n_experts must be at most 261,888 and
+ * m_tokens at most 1016 (larger requests are rejected with
  * HALE_E_INVALID_ARGUMENT). The first call on a device looks up that array's
- * device address; make it before any stream capture. Calls share the array:
- * calls that overlap on the GPU race, so keep them on one stream. Errors are
- * reported through hale_last_error(NULL, ...); a device-side wait that times
- * out is not reported by this entry point. */
+ * device address and keeps it for the life of the device's primary context
+ * (a host that resets the device must not call this entry point again in
+ * the same process); make that first call before any stream capture. Calls
+ * share the array: calls that overlap on the GPU race, so keep them on one
+ * stream. Errors are reported through hale_last_error(NULL, ...); a
+ * device-side wait that times out is not reported by this entry point. */
 HALE_API hale_status hale_moe_route_noalloc(const void* router, hale_dtype router_dtype,
                                             uint32_t n_experts, uint32_t top_k,
                                             int32_t normalize_topk, uint32_t hidden,

@@ -747,3 +747,13 @@ int ho_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Threads of the parallel regions (the reference's rayon pool uses every
+ * core; a launcher such as torchrun may have set OMP_NUM_THREADS=1). */
+void ho_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

@@ -146,6 +146,7 @@ void ho_expf_batch(const float* x, float* y, size_t n);
 
 /* Threads OpenMP will use (1 when built without OpenMP). */
 int ho_num_threads(void);
+void ho_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -93,10 +93,20 @@ class OracleModel:
     src/convert.rs:56-127 via WeightMatrix::convert, matrix.rs:103-109).
     """
 
-    def __init__(self, directory, expert_dtype=None):
-        with open(os.path.join(directory, "config.json")) as f:
-            self.cfg = normalize_config(json.load(f))
-        self.t = read_safetensors(os.path.join(directory, "model.safetensors"))
+    def __init__(self, directory=None, expert_dtype=None, hf_config=None, tensors=None, expert_encoded=None):
+        """From a checkpoint directory (config.json + model.safetensors), or
+        from memory: `hf_config` (the config.json dict) and `tensors`
+        ({name: (safetensors dtype, shape, raw uint8)}). `expert_encoded`
+        (optional): (layer, expert, "gate"|"up"|"down") -> that routed
+        expert matrix already encoded in expert_dtype, for models whose
+        experts are not held as float tensors."""
+        if directory is not None:
+            with open(os.path.join(directory, "config.json")) as f:
+                hf_config = json.load(f)
+            tensors = read_safetensors(os.path.join(directory, "model.safetensors"))
+        self.cfg = normalize_config(hf_config)
+        self.t = tensors
+        self.expert_encoded = expert_encoded
         self._keep = []
         c = self.cfg
         expert_name, router_name, dense_name = _names(c["qwen"])
@@ -132,8 +142,13 @@ class OracleModel:
                 L.router = self.matrix(router_name(l))
                 exps = []
                 for e in range(c["experts"]):
-                    exps.append(O.Expert(*(self.matrix(expert_name(l, e, pj), expert_dtype)
-                                           for pj in ("gate", "up", "down"))))
+                    if expert_encoded is not None:
+                        exps.append(O.Expert(*(self.encoded_matrix(expert_dtype, expert_encoded(l, e, pj),
+                                                                   *self.expert_shape(pj))
+                                               for pj in ("gate", "up", "down"))))
+                    else:
+                        exps.append(O.Expert(*(self.matrix(expert_name(l, e, pj), expert_dtype)
+                                               for pj in ("gate", "up", "down"))))
                 arr = (O.Expert * len(exps))(*exps)
                 self._keep.append(arr)
                 L.experts = C.cast(arr, C.c_void_p)
@@ -175,6 +190,16 @@ class OracleModel:
             d = dtype
         self._keep.append(data)
         return O.Matrix(d, rows, cols, data.ctypes.data)
+
+    def expert_shape(self, proj):
+        h, i = self.cfg["hidden"], self.cfg["expert_inter"]
+        return (h, i) if proj == "down" else (i, h)
+
+    def encoded_matrix(self, dtype, data, rows, cols):
+        data = np.ascontiguousarray(data)
+        assert data.nbytes == rows * O.row_bytes(dtype, cols)
+        self._keep.append(data)
+        return O.Matrix(dtype, rows, cols, data.ctypes.data)
 
     def vector(self, name):
         """TensorSource::vector (loader/safetensors.rs:162-170): decoded to f32."""

@@ -89,6 +89,7 @@ def lib(native=False):
         "ho_model_forward": (C.c_int, [P, C.c_uint32, C.c_uint32, P, P, C.c_uint32, P, P, C.c_int]),
         "ho_expf_batch": (None, [P, P, sz]),
         "ho_num_threads": (C.c_int, []),
+        "ho_set_num_threads": (None, [C.c_int]),
     }
     for fn, (res, args) in sig.items():
         f = getattr(L, fn)
@@ -349,3 +350,9 @@ def expf_batch(x):
 
 def num_threads(native=False):
     return lib(native).ho_num_threads()
+
+
+def set_num_threads(n, native=False):
+    """OpenMP threads of the oracle's parallel loops (all host cores, like
+    the reference's rayon pool, unless told otherwise)."""
+    lib(native).ho_set_num_threads(int(n))

@@ -18,6 +18,8 @@ import pytest
 from oracle import model as OM
 from oracle import oracle as O
 
+import synth
+
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
@@ -69,7 +71,10 @@ def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1):
             L["router"] = hm(router_name(l))
             j = moe_layers.index(l)
             for e in range(c["experts"]):
-                enc = [O.encode(expert_dtype, om.f32(expert_name(l, e, pj))) for pj in ("gate", "up", "down")]
+                if om.expert_encoded is not None:
+                    enc = [om.expert_encoded(l, e, pj) for pj in ("gate", "up", "down")]
+                else:
+                    enc = [O.encode(expert_dtype, om.f32(expert_name(l, e, pj))) for pj in ("gate", "up", "down")]
                 pool.upload(j, e, fmt.pack_record(*enc))
         layers.append(L)
     embed = hm("model.embed_tokens.weight")
@@ -280,3 +285,72 @@ def test_batched_prefill_through_a_tiered_pool(ctx, tmp_path):
     assert _bits_equal(logits.cpu().numpy(), want)
     assert pool.stats().misses > 0
     dec.close()
+
+
+def _decode_and_compare(ctx, om, expert_dtype, prompt, n_new):
+    """Greedy decode on the GPU (argmax of its own logits, first index of
+    the max as activation.rs:24-32) and on the oracle (generate() with
+    greedy sampling, generator.rs:55-94): the generated ids must be equal,
+    and the logits of every position (prompt and generated) bit-identical
+    to the oracle's teacher-forced logits over the same ids."""
+    want_ids = om.greedy(prompt, n_new)
+    tokens = list(prompt) + list(want_ids)
+    want = om.teacher_forced_logits(tokens)
+    dec = build_decoder(ctx, om, expert_dtype, len(tokens) + 1)
+    logits = torch.empty(om.cfg["vocab"], dtype=torch.float32, device="cuda")
+    got, gen = [], []
+    for i, t in enumerate(prompt):
+        dec.forward(t, i, logits)
+        got.append(logits.cpu().numpy().copy())
+    pos = len(prompt)
+    for step in range(n_new):
+        tok = int(torch.argmax(logits).item())
+        gen.append(tok)
+        if step + 1 == n_new:
+            break
+        dec.forward(tok, pos, logits)
+        got.append(logits.cpu().numpy().copy())
+        pos += 1
+    # the last generated id's own logits (position len(tokens) - 1)
+    dec.forward(gen[-1], pos, logits)
+    got.append(logits.cpu().numpy().copy())
+    ctx.check()
+    dec.close()
+    assert gen == list(want_ids), "greedy ids differ"
+    got = np.stack(got)
+    diff = got.view(np.uint32) != want.view(np.uint32)
+    assert not diff.any(), f"{diff.sum()} of {diff.size} logits differ; first at {np.argwhere(diff)[0]}"
+
+
+def test_config0_tiny_qwen3_moe_exactly_as_specified(ctx):
+    """4 decoder layers, hidden 256, 8 query / 2 KV heads
+    of 32, RoPE theta 1e6, RMSNorm eps 1e-6, 16 experts top-4 of
+    intermediate 128 with normalised top-k weights, vocab 1024, q8_0
+    experts, f32 dense weights, N(0, 0.02) from a seed (norm weights 1.0).
+    A 32-token uniform random prompt, then 64 greedy tokens; logits compared
+    at all 96 positions."""
+    hf, t, enc = synth.qwen3_moe(0, 4, 256, 8, 2, 32, 16, 4, 128, 1024, fmt.Q8_0, "F32")
+    om = OM.OracleModel(expert_dtype=fmt.Q8_0, hf_config=hf, tensors=t, expert_encoded=enc)
+    prompt = np.random.default_rng(1).integers(0, 1024, 32).tolist()
+    _decode_and_compare(ctx, om, fmt.Q8_0, prompt, 64)
+
+
+def test_config2_shapes_qwen3_30b_a3b_reduced_layers(ctx):
+    """BASELINE config 2's shapes (Qwen3-30B-A3B: hidden 2048, 32 query / 4
+    KV heads of 128, 128 experts top-8 of intermediate 768 in q4_0, vocab
+    151936, bf16 dense weights) at 2 decoder layers: a 4-token prompt and 4
+    greedy tokens, every position's logits bit-identical to the oracle."""
+    hf, t, enc = synth.qwen3_moe(2, 2, 2048, 32, 4, 128, 128, 8, 768, 151936, fmt.Q4_0, "BF16")
+    om = OM.OracleModel(expert_dtype=fmt.Q4_0, hf_config=hf, tensors=t, expert_encoded=enc)
+    prompt = np.random.default_rng(3).integers(0, 151936, 4).tolist()
+    _decode_and_compare(ctx, om, fmt.Q4_0, prompt, 4)
+
+
+@pytest.mark.parametrize("head_dim", [384, 512])
+def test_wide_heads_take_the_decode_attention_kernel(ctx, head_dim):
+    """head_dim above 256 runs attn_decode_kernel (V rows staged three stages
+    deep): 20 positions, past several V stages, bit-identical logits."""
+    hf, t, enc = synth.qwen3_moe(4, 1, 256, 2, 1, head_dim, 4, 2, 64, 256, fmt.Q8_0, "F32")
+    om = OM.OracleModel(expert_dtype=fmt.Q8_0, hf_config=hf, tensors=t, expert_encoded=enc)
+    prompt = np.random.default_rng(5).integers(0, 256, 12).tolist()
+    _decode_and_compare(ctx, om, fmt.Q8_0, prompt, 8)

@@ -256,35 +256,35 @@ def test_moe_forward_tiny_config_is_bit_exact(ctx, dtype, m):
     assert_bit_equal(out, want, "layer output")
 
 
-@pytest.mark.parametrize("m", [1, 8, 64])
+@pytest.mark.parametrize("m", [1, 8, 64, 512])
 def test_moe_forward_qwen3_30b_shape_is_bit_exact(ctx, m):
-    """BASELINE config 1 shape: H=2048, 128 experts top-8, I=768, q4_0.
-    The oracle checks every token at M<=8 and a sample of 12 at M=64."""
+    """BASELINE config 1 shape: H=2048, 128 experts top-8, I=768, q4_0, at
+    every batch size the config names. Every token of the batch is checked
+    against the oracle (the -march=native OpenMP build keeps M=512 to about
+    a second of CPU time)."""
     ld = fmt.SyntheticLayer(7, 128, 2048, 768, fmt.Q4_0)
     pool, experts = build_pool(ctx, ld)
     x = ld.tokens(m)
     out, idx, w, renc = run_forward(ctx, pool, ld, x, 8, True)
-    toks = np.arange(m) if m <= 8 else np.random.default_rng(m).choice(m, 12, replace=False)
-    want, widx, ww = O.moe_forward(fmt.F32, renc, experts, 8, True, x[toks])
-    assert np.array_equal(idx[toks], widx.astype(np.int32))
-    assert_bit_equal(w[toks], ww, "weights")
-    assert_bit_equal(out[toks], want, "layer output")
-    # the whole batch is within the north-star tolerance and finite
-    assert np.isfinite(out).all()
+    want, widx, ww = O.moe_forward(fmt.F32, renc, experts, 8, True, x, native=True)
+    assert np.array_equal(idx, widx.astype(np.int32))
+    assert_bit_equal(w, ww, "weights")
+    assert_bit_equal(out, want, "layer output")
 
 
 def test_moe_forward_full_batch_properties(ctx):
-    """M=512 (the largest config-1 batch): deterministic run to run, routing
-    stats count every route, and sampled tokens match the oracle."""
+    """M=512 (the largest config-1 batch) on other seeds: deterministic run
+    to run, routing stats count every route, and every token matches the
+    oracle."""
     ld = fmt.SyntheticLayer(9, 128, 2048, 768, fmt.Q4_0)
     pool, experts = build_pool(ctx, ld)
     x = ld.tokens(512)
     a = run_forward(ctx, pool, ld, x, 8, True)
     b = run_forward(ctx, pool, ld, x, 8, True)
     assert_bit_equal(a[0], b[0], "determinism")
-    toks = np.random.default_rng(0).choice(512, 6, replace=False)
-    want, widx, ww = O.moe_forward(fmt.F32, a[3], experts, 8, True, x[toks])
-    assert_bit_equal(a[0][toks], want, "sampled tokens")
+    want, widx, ww = O.moe_forward(fmt.F32, a[3], experts, 8, True, x, native=True)
+    assert np.array_equal(a[1], widx.astype(np.int32))
+    assert_bit_equal(a[0], want, "every token")
     counts = pool.routing_counts()
     assert counts.sum() == 2 * 512 * 8
     per_expert = np.bincount(a[1].reshape(-1), minlength=128)
