@@ -185,7 +185,7 @@ class Context:
     shapes allow (hale_ctx_set_expert_kernel).
     """
 
-    FAMILIES = {"auto": 0, "tc": 1, "dp4a": 2, "ps": 3}
+    FAMILIES = {"auto": 0, "tc": 1, "dp4a": 2, "ps": 3, "ws": 4}
 
     def __init__(self, device=0, expert_kernel=None):
         h = P()

@@ -3,6 +3,8 @@
 // Host orchestration only: argument checks mirroring the reference's
 // assertions and HaleError cases, workspace management, and launches. The
 // arithmetic lives in hale_kernels.cuh.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -21,6 +23,7 @@
 #include "hale_kernels.cuh"
 #include "hale_tc.cuh"
 #include "hale_stream.cuh"
+#include "hale_ws.cuh"
 #include "hale_ep.cuh"
 #include "hale_decoder.cuh"
 #include "hale_tier.h"
@@ -118,6 +121,10 @@ struct hale_pool {
     cudaEvent_t ev_done = nullptr;         // after the last tiered forward's expert kernels
     bool done_recorded = false;
     bool timing_pending = false;
+    // TMA tensor maps over the tile layout of every expert slot (the
+    // warp-specialised streaming kernels): gate/up tiles and down tiles
+    bool ws_maps = false;
+    CUtensorMap map_gu, map_d;
 };
 
 static hale_status fail(hale_ctx* ctx, hale_status st, const char* fmt, ...) {
@@ -310,7 +317,7 @@ extern "C" void hale_ctx_destroy(hale_ctx* ctx) {
 
 extern "C" hale_status hale_ctx_set_expert_kernel(hale_ctx* ctx, int family) {
     if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_ctx_set_expert_kernel: ctx is NULL");
-    if (family < HALE_EXPERT_AUTO || family > HALE_EXPERT_PS)
+    if (family < HALE_EXPERT_AUTO || family > HALE_EXPERT_WS)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_ctx_set_expert_kernel: unknown family %d", family);
     ctx->expert_kernel = family;
     return HALE_OK;
@@ -350,7 +357,7 @@ extern "C" uint64_t hale_ctx_launch_count(const hale_ctx* ctx) { return ctx ? ct
 
 // Counter region of the MoE workspace (zero between calls).
 struct MoeLayout {
-    size_t tile_cnt, grid_cnt, comb_cnt, counters_end;
+    size_t tile_cnt, grid_cnt, comb_cnt, ws_cnt, counters_end;
     size_t logits, topk_idx, topk_w, xq, xaux, elist_off, elist, active, n_active;
     size_t hq, haux, ybuf, total;
 };
@@ -367,6 +374,7 @@ static MoeLayout moe_layout(int M, int E, int k, int H, int I) {
     L.tile_cnt = take((size_t)(M + kRouterTT - 1) / kRouterTT * 4);
     L.grid_cnt = take(4);
     L.comb_cnt = take((size_t)M * ((H + 127) / 128) * 4);
+    L.ws_cnt = take(4 * 4);
     L.counters_end = o;
     L.logits = take((size_t)M * E * 4);
     L.topk_idx = take((size_t)M * k * 4);
@@ -703,6 +711,72 @@ extern "C" hale_status hale_matrix_matvec_q8(hale_ctx* ctx, const hale_matrix* m
 }
 
 // ---------------------------------------------------------------------------
+// TMA tensor maps over the pool's tile layout
+// ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point
+// (no link-time dependency on the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static std::mutex mu;
+    static bool tried = false;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!tried) {
+        tried = true;
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// A 4-D map over `n_slots` experts' region starting `offset` bytes into each
+// expert: [slot][tile][block][record as u64], boxes of box_tiles tiles x SB
+// blocks (whole records, so every copy starts on a 16-byte boundary).
+static bool pool_tensor_map(CUtensorMap* m, uint8_t* data, size_t offset, int rec, int nb, int tiles, size_t n_slots,
+                            size_t stride, int box_tiles, int SB) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+    if (!enc || rec % 16 || rec / 8 > 256 || ((uintptr_t)(data + offset) & 15) || stride % 16) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)(rec / 8), (cuuint64_t)nb, (cuuint64_t)tiles, (cuuint64_t)n_slots};
+    cuuint64_t strides[3] = {(cuuint64_t)rec, (cuuint64_t)nb * rec, (cuuint64_t)stride};
+    cuuint32_t box[4] = {(cuuint32_t)(rec / 8), (cuuint32_t)SB, (cuuint32_t)box_tiles, 1u};
+    cuuint32_t es[4] = {1u, 1u, 1u, 1u};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, data + offset, dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// CTAs per SM of the streaming kernels for these shapes: three where both
+// kernels' shared-memory plans fit a third of the SM, else two; 0 = the
+// shapes do not suit them.
+static int ws_ctas_per_sm(hale_dtype dt, int H, int I) {
+    const int rec = 32 * block_bytes(dt);
+    for (int cps : {3, 2}) {
+        const int budget = ws_budget(cps);
+        if (ws_plan_ok(ws_plan(rec, 2, 2, kWsSB, H, budget), budget) &&
+            ws_plan_ok(ws_plan(rec, 1, 4, kWsSB, I, budget), budget))
+            return cps;
+    }
+    return 0;
+}
+
+// Builds the pool's maps (gate/up: H/32 blocks per tile, 2 * I/32 tiles;
+// down: I/32 blocks per tile, H/32 tiles) when its shapes suit the
+// streaming kernels; otherwise they are left unused.
+static void pool_build_maps(hale_pool* p, size_t n_slots) {
+    p->ws_maps = false;
+    const int H = (int)p->H, I = (int)p->I, rec = 32 * block_bytes(p->dtype);
+    if (I % 64 || H % 128 || !ws_ctas_per_sm(p->dtype, H, I)) return;
+    const int nbh = H / 32, nbi = I / 32, TI = I / 32, TH = H / 32;
+    const size_t gu = 2 * tiled_bytes(p->dtype, p->I, p->H);
+    p->ws_maps = pool_tensor_map(&p->map_gu, p->data, 0, rec, nbh, 2 * TI, n_slots, p->expert_stride, 2, kWsSB) &&
+                 pool_tensor_map(&p->map_d, p->data, gu, rec, nbi, TH, n_slots, p->expert_stride, 4, kWsSB);
+}
+
+// ---------------------------------------------------------------------------
 // expert pool
 // ---------------------------------------------------------------------------
 extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
@@ -739,6 +813,7 @@ extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_
     p->resident.assign((size_t)n_layers * n_experts, 0);
     p->layer_resident.assign(n_layers, 0);
     p->host_routing.assign((size_t)n_layers * n_experts, 0);
+    pool_build_maps(p, (size_t)n_layers * n_experts);
     *out = p;
     return HALE_OK;
 }
@@ -834,6 +909,7 @@ extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, 
     p->stats.pinned_experts = n_pinned;
     p->stats.pinned_bytes = n_pinned * p->record_bytes;
     p->stats.lru_capacity_bytes = policy->lru_bytes;
+    pool_build_maps(p, n_slots);
     *out = p;
     return HALE_OK;
 }
@@ -1130,8 +1206,10 @@ extern "C" hale_status hale_moe_route(hale_ctx* ctx, const hale_moe_layer* ly, u
 // and HALE_EXPERT_KERNEL=tc selects them.
 static constexpr uint32_t kTcMinTokens = 1u << 30;
 static bool use_tc(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
-    if (ctx->expert_kernel == 2 || ctx->expert_kernel == 3 || I % 64 != 0 || H % 128 != 0) return false;
-    if (ctx->expert_kernel == 0 && M < kTcMinTokens) return false;
+    if ((ctx->expert_kernel != HALE_EXPERT_TC && ctx->expert_kernel != HALE_EXPERT_AUTO) || I % 64 != 0 ||
+        H % 128 != 0)
+        return false;
+    if (ctx->expert_kernel == HALE_EXPERT_AUTO && M < kTcMinTokens) return false;
     return tc_plan_ok(dt == HALE_Q4_0 ? tc_plan(QFmt<0>::BB, TcStage<0>::SB) : tc_plan(QFmt<1>::BB, TcStage<1>::SB));
 }
 
@@ -1164,7 +1242,7 @@ static hale_status expert_go_tc(hale_ctx* ctx, const ExpertArgs& a, unsigned max
 static constexpr int kPsCtas = 2;
 static constexpr int kPsBudget = (kPsCtas == 1 ? 219 : 104) * 1024;
 static bool use_ps(const hale_ctx* ctx, hale_dtype dt, uint32_t M, int H, int I) {
-    if (ctx->expert_kernel != 3 || I % 64 != 0 || H % 128 != 0) return false;
+    if (ctx->expert_kernel != HALE_EXPERT_PS || I % 64 != 0 || H % 128 != 0) return false;
     const int bb = block_bytes(dt), sb = ps_stage_blocks(dt == HALE_Q4_0 ? 0 : 1, kPsCtas);
     return ps_plan_ok(ps_plan(bb, sb, H, kPsBudget), kPsBudget) && ps_plan_ok(ps_plan(bb, sb, I, kPsBudget), kPsBudget);
 }
@@ -1191,6 +1269,41 @@ static hale_status expert_go_ps(hale_ctx* ctx, const ExpertArgs& a, unsigned max
     return check_launch(ctx, "expert_down_ps");
 }
 
+// Warp-specialised streaming kernels (hale_ws.cuh): two persistent CTAs per
+// SM, weights by TMA tensor loads through the pool's maps. "auto" takes them
+// from kWsMinTokens tokens (the per-CTA kernels keep the smallest batches,
+// where more CTAs per expert win).
+static constexpr uint32_t kWsMinTokens = 3;
+static bool use_ws(const hale_ctx* ctx, const hale_pool* p, uint32_t M, int k, int E) {
+    (void)k;
+    (void)E;
+    if (!p->ws_maps || (ctx->expert_kernel != HALE_EXPERT_AUTO && ctx->expert_kernel != HALE_EXPERT_WS)) return false;
+    return ctx->expert_kernel == HALE_EXPERT_WS || M >= kWsMinTokens;
+}
+
+template <int QT, int CPS>
+static hale_status expert_go_ws(hale_ctx* ctx, const hale_pool* p, const ExpertArgs& a, unsigned max_active,
+                                unsigned* ctr, cudaStream_t st) {
+    const int TI = a.I / 32, TH = a.H / 32, rec = 32 * QFmt<QT>::BB, budget = ws_budget(CPS);
+    const WsPlan P1 = ws_plan(rec, 2, 2, kWsSB, a.H, budget), P2 = ws_plan(rec, 1, 4, kWsSB, a.I, budget);
+    CUDA_TRY(ctx, allow_smem(expert_gate_up_ws_kernel<QT, CPS>, (size_t)P1.total));
+    CUDA_TRY(ctx, allow_smem(expert_down_ws_kernel<QT, CPS>, (size_t)P2.total));
+    const unsigned slots = (unsigned)(ctx->sm_count * CPS);
+    const unsigned g1 = std::min(max_active * (unsigned)(TI / 2), slots);
+    const unsigned g2 = std::min(max_active * (unsigned)(TH / 4), slots);
+    {
+        ProfScope ps_(ctx, "expert_gate_up", st);
+        expert_gate_up_ws_kernel<QT, CPS><<<g1, kWsThreads, P1.total, st>>>(p->map_gu, a, P1, ctr);
+    }
+    hale_status r = check_launch(ctx, "expert_gate_up_ws");
+    if (r) return r;
+    {
+        ProfScope ps_(ctx, "expert_down", st);
+        expert_down_ws_kernel<QT, CPS><<<g2, kWsThreads, P2.total, st>>>(p->map_d, a, P2, ctr + 2);
+    }
+    return check_launch(ctx, "expert_down_ws");
+}
+
 template <int QT, int RT>
 static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_active, cudaStream_t st) {
     const int TI = a.I / 32, TH = a.H / 32;
@@ -1212,7 +1325,7 @@ static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_ac
     return check_launch(ctx, "expert_down");
 }
 
-static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, uint32_t M, int k, int E,
+static hale_status launch_experts(hale_ctx* ctx, const hale_pool* p, ExpertArgs& a, uint32_t M, int k, int E,
                                   cudaStream_t st);
 
 // A tiered pool's forward: read the routes back (the calling thread waits for
@@ -1286,6 +1399,7 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
         a.slot = p->d_slot + (size_t)ly->layer * p->E;
     } else {
         a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+        a.expert0 = (int)(ly->layer * p->E);
     }
     a.expert_stride = p->expert_stride;
     a.H = H;
@@ -1302,10 +1416,11 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     a.haux = reinterpret_cast<int2*>(ws + L.haux);
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
+    a.ws_cnt = reinterpret_cast<unsigned*>(ws + L.ws_cnt);
     a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
     a.out = out;
     a.err = ctx->d_err;
-    r = launch_experts(ctx, p->dtype, a, M, k, E, st);
+    r = launch_experts(ctx, p, a, M, k, E, st);
     if (!r && p->tiered) {
         CUDA_TRY(ctx, cudaEventRecord(p->ev_done, st));
         p->done_recorded = true;
@@ -1315,8 +1430,9 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
 
 // The expert kernels over the routes in a (expert lists built, activations
 // quantized): the family by context setting and batch shape.
-static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, uint32_t M, int k, int E,
+static hale_status launch_experts(hale_ctx* ctx, const hale_pool* p, ExpertArgs& a, uint32_t M, int k, int E,
                                   cudaStream_t st) {
+    const hale_dtype dt = p->dtype;
     const int H = a.H, I = a.I;
     // ring depth, capped at the stages one tile has
     // ring depth: deep rings only for a single token, where a CTA's whole
@@ -1326,6 +1442,14 @@ static hale_status launch_experts(hale_ctx* ctx, hale_dtype dt, ExpertArgs& a, u
     a.S1 = std::min(depth, (H / 32 + kStageBlocks - 1) / kStageBlocks);
     a.S2 = std::min(depth, (I / 32 + kStageBlocks - 1) / kStageBlocks);
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
+    if (use_ws(ctx, p, M, k, E)) {
+        const int cps = ws_ctas_per_sm(dt, H, I);
+        if (dt == HALE_Q4_0)
+            return cps == 3 ? expert_go_ws<0, 3>(ctx, p, a, max_active, a.ws_cnt, st)
+                            : expert_go_ws<0, 2>(ctx, p, a, max_active, a.ws_cnt, st);
+        return cps == 3 ? expert_go_ws<1, 3>(ctx, p, a, max_active, a.ws_cnt, st)
+                        : expert_go_ws<1, 2>(ctx, p, a, max_active, a.ws_cnt, st);
+    }
     if (use_tc(ctx, dt, M, H, I)) {
         // 16-token passes once experts average ~16 tokens; 8-token passes below
         const bool wide = (long long)M * k >= 16LL * E;
@@ -1542,6 +1666,7 @@ extern "C" hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* p, uint32_t lay
     // the expert kernels then writes y itself (0 + 1 * y == y)
     ExpertArgs a{};
     a.experts = p->data + (size_t)layer * p->E * p->expert_stride;
+    a.expert0 = (int)(layer * p->E);
     a.expert_stride = p->expert_stride;
     a.H = H;
     a.I = I;
@@ -1557,10 +1682,11 @@ extern "C" hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* p, uint32_t lay
     a.haux = reinterpret_cast<int2*>(ws + L.haux);
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
+    a.ws_cnt = reinterpret_cast<unsigned*>(ws + L.ws_cnt);
     a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
     a.out = y;
     a.err = ctx->d_err;
-    return launch_experts(ctx, p->dtype, a, n, 1, El, st);
+    return launch_experts(ctx, p, a, n, 1, El, st);
 }
 
 extern "C" hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, const float* y_back, uint32_t M,

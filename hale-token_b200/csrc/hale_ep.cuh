@@ -78,12 +78,21 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const EpMeta* __restrict
         atomicAdd(&s_cnt[le], 1);
     }
     __syncthreads();
+    // the active list with the most records first (ties: lower id), the
+    // order in which the persistent expert kernels claim work
+    for (int e = threadIdx.x; e < El; e += blockDim.x) {
+        const int c = s_cnt[e];
+        if (!c) continue;
+        int rank = 0;
+        for (int e2 = 0; e2 < El; e2++) rank += (s_cnt[e2] > c) || (s_cnt[e2] == c && e2 < e);
+        active[rank] = e;
+    }
     if (threadIdx.x == 0) {
         int off = 0, na = 0;
         for (int e = 0; e < El; e++) {
             elist_off[e] = off;
             cursor[e] = 0;
-            if (s_cnt[e]) active[na++] = e;
+            na += s_cnt[e] > 0;
             off += s_cnt[e];
         }
         elist_off[El] = off;

@@ -868,7 +868,15 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             a.elist_off[tid] = off;
             s_cur[tid] = off;
             if (c > 0) {
-                a.active[base_a + act - 1] = tid;
+                // experts with work, most routes first (ties: lower id): the
+                // persistent kernels claim work in this order, so the longest
+                // units start first and the tail is short
+                int rank = 0;
+                for (int e2 = 0; e2 < a.E; e2++) {
+                    const int c2 = s_cnt[e2];
+                    rank += (c2 > c) || (c2 == c && e2 < tid);
+                }
+                a.active[rank] = tid;
                 if (a.routing_counts) a.routing_counts[tid] += (unsigned long long)c;
             }
         }
@@ -906,9 +914,11 @@ struct ExpertArgs {
     int2* haux;               // [M*k slots, nbp(I)]
     float* ybuf;              // [M*k routes, H]  (route order)
     unsigned* comb_cnt;       // [M, ceil(H / 128)]
+    unsigned* ws_cnt;         // [4]: streaming kernels' unit / retire counters
     const float* topk_w;      // [M, k]
     float* out;               // [M, H]
     int S1, S2;               // ring depths of the gate/up and down kernels
+    int expert0;              // tensor-map slot of expert 0 of the layer (resident pools)
     uint32_t* err;
 };
 

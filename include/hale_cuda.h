@@ -96,6 +96,7 @@ HALE_API uint64_t hale_ctx_launch_count(const hale_ctx* ctx);
 #define HALE_EXPERT_TC 1   /* tcgen05 kind::i8 kernels (TMEM accumulators) */
 #define HALE_EXPERT_DP4A 2 /* per-CTA kernels: dp4a, warp MMA from 3 tokens */
 #define HALE_EXPERT_PS 3   /* persistent streaming warp-MMA kernels */
+#define HALE_EXPERT_WS 4   /* warp-specialised streaming: TMA tensor loads, warp MMA */
 HALE_API hale_status hale_ctx_set_expert_kernel(hale_ctx* ctx, int family);
 /* Per-kernel timing: while enabled, every launch on ctx is bracketed by a
  * pair of CUDA events on its stream. hale_ctx_profile_read synchronises,

@@ -1,6 +1,7 @@
 """GPU parity of the expert-kernel families.
 
-Contexts here force a family at every batch size the shapes allow: "tc" the
+Contexts here force a family at every batch size the shapes allow: "ws" the
+warp-specialised streaming kernels (TMA tensor loads, warp MMA), "tc" the
 tcgen05 kind::i8 kernels, "ps" the persistent streaming warp-MMA kernels,
 "dp4a" the per-CTA kernels. Each must equal the oracle (MoeLayer::forward,
 src/moe.rs:56-70, with dot_q4_0 / dot_q8_0 of src/tensor/quant.rs:115-144)
@@ -21,7 +22,7 @@ hale = importlib.import_module("hale-token_b200")
 fmt = importlib.import_module("hale-token_b200.formats")
 
 
-FAMILIES = ["tc", "ps"]
+FAMILIES = ["ws", "tc", "ps"]
 
 
 @pytest.fixture(scope="module")
@@ -128,3 +129,18 @@ def test_repeated_calls_are_deterministic(ctxs, family):
     a = forward(tc, pool, ld, x, 4)[0]
     b = forward(tc, pool, ld, x, 4)[0]
     assert_bit_equal(a, b, "second call")
+
+
+@pytest.mark.parametrize("family", FAMILIES)
+def test_q4_wide_hidden_takes_short_stages(ctxs, family):
+    """q4_0, H=4096 (Qwen3-235B hidden size): the streaming kernels fall back
+    to 4-block stages to fit two CTAs per SM; every token against the
+    oracle."""
+    tc, dp = ctxs[family], ctxs["dp4a"]
+    ld = fmt.SyntheticLayer(29, 16, 4096, 512, fmt.Q4_0)
+    x = ld.tokens(40)
+    out_tc, idx, renc = forward(tc, make_pool(tc, ld), ld, x, 8)
+    out_dp, _, _ = forward(dp, make_pool(dp, ld), ld, x, 8)
+    assert_bit_equal(out_tc, out_dp, "family vs dp4a")
+    want, _, _ = O.moe_forward(fmt.F32, renc, oracle_experts(ld), 8, True, x, native=True)
+    assert_bit_equal(out_tc, want, "every token")
