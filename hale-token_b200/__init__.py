@@ -28,6 +28,7 @@ E_OUT_OF_MEMORY = -12
 E_TIMEOUT = -13
 E_DEVICE_CHECK = -14
 E_UNSUPPORTED = -15
+E_NCCL = -16
 
 F32, F16, BF16, Q8_0, Q4_0 = 0, 1, 2, 3, 4
 
@@ -115,6 +116,10 @@ SIGNATURES = {
     "hale_ep_dispatch": (I32, [P, P, U32, P, U32, U32, P, P, P, C.POINTER(U64), P, P, P]),
     "hale_ep_experts": (I32, [P, P, U32, U32, P, P, P, U32, P, P]),
     "hale_ep_combine": (I32, [P, P, P, U32, U32, U32, P, P]),
+    "hale_comm_unique_id": (I32, [P]),
+    "hale_comm_create": (I32, [P, U32, U32, P, U32, U32, U32, U32, C.POINTER(P)]),
+    "hale_comm_destroy": (I32, [P]),
+    "hale_moe_forward_ep": (I32, [P, P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_decoder_create": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, C.POINTER(P)]),
     "hale_decoder_destroy": (None, [P]),
     "hale_decoder_forward": (I32, [P, P, U32, U32, P, P, P]),
@@ -477,6 +482,41 @@ def ep_combine(ctx, send_meta, y_back, m_tokens, top_k, hidden, out, stream=None
     """hale_ep_combine: out[t] = best-first weighted sum of the token's y rows."""
     ctx.call("hale_ep_combine", ctx.h, ptr(send_meta), ptr(y_back), m_tokens, top_k, hidden, ptr(out),
              _stream(stream))
+
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id():
+    """hale_comm_unique_id: a fresh communicator id (bytes) for hale_comm_create."""
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    _check(lib().hale_comm_unique_id(buf))
+    return buf.raw
+
+
+class Comm:
+    """hale_comm: this rank's place in an expert-parallel group of n_ranks
+    GPUs (collective create / close; one per process and GPU)."""
+
+    def __init__(self, ctx, n_ranks, rank, unique_id, hidden, n_experts, top_k, max_tokens):
+        h = P()
+        uid = C.create_string_buffer(bytes(unique_id), COMM_ID_BYTES) if unique_id is not None else None
+        ctx.call("hale_comm_create", ctx.h, n_ranks, rank, uid, hidden, n_experts, top_k, max_tokens,
+                 C.byref(h))
+        self.ctx, self.h = ctx, h
+        self.n_ranks, self.rank, self.hidden, self.n_experts, self.top_k = n_ranks, rank, hidden, n_experts, top_k
+        self.max_tokens = max_tokens
+
+    def close(self):
+        if self.h:
+            h, self.h = self.h, None
+            self.ctx.call("hale_comm_destroy", h)
+
+
+def moe_forward_ep(ctx, comm, pool, layer, x, out, topk_idx=None, topk_w=None, stream=None):
+    """hale_moe_forward_ep: this rank's tokens through the expert-parallel layer."""
+    ctx.call("hale_moe_forward_ep", ctx.h, comm.h, pool.h, C.byref(layer), ptr(x), x.shape[0], ptr(out),
+             ptr(topk_idx), ptr(topk_w), _stream(stream))
 
 
 def quantize_q8(ctx, x, scales, quants, stream=None):

@@ -25,7 +25,7 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "--fmad=false",
     "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden",
-    "-shared", "-cudart", "static",
+    "-shared", "-cudart", "static", "-ldl",
 ]
 
 

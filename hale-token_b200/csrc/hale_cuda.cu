@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <chrono>
@@ -16,6 +18,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -25,6 +28,7 @@
 #include "hale_stream.cuh"
 #include "hale_ws.cuh"
 #include "hale_ep.cuh"
+#include "hale_p2p.cuh"
 #include "hale_decoder.cuh"
 #include "hale_tier.h"
 
@@ -40,6 +44,12 @@ thread_local hale_status g_thread_status = HALE_OK;
 
 struct hale_ctx {
     int device = 0;
+    // objects made on this context; destroying the context detaches them
+    // (their own destroy then frees their memory on their device)
+    std::set<hale_matrix*> matrices;
+    std::set<hale_pool*> pools;
+    std::set<hale_decoder*> decoders;
+    std::set<hale_comm*> comms;
     int sm_count = 0;
     // expert kernel family (hale_ctx_set_expert_kernel): HALE_EXPERT_AUTO =
     // by batch shape, _TC = tcgen05 kernels, _DP4A = per-CTA kernels (dp4a /
@@ -86,6 +96,7 @@ struct hale_ctx {
 
 struct hale_matrix {
     hale_ctx* ctx;
+    int device = 0;
     hale_dtype dtype;
     uint32_t rows, cols, rows_pad;
     uint32_t nb;     // quantized: blocks per row; float: steps of 8
@@ -96,6 +107,7 @@ struct hale_matrix {
 
 struct hale_pool {
     hale_ctx* ctx;
+    int device = 0;
     hale_dtype dtype;
     uint32_t H, I, L, E;
     size_t expert_stride;   // tiled bytes per expert
@@ -300,8 +312,11 @@ static void drop_host_graphs(hale_ctx* ctx, const hale_pool* pool) {
     }
 }
 
+static void ctx_detach_children(hale_ctx* ctx);
+
 extern "C" void hale_ctx_destroy(hale_ctx* ctx) {
     if (!ctx) return;
+    ctx_detach_children(ctx);
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
     drop_host_graphs(ctx, nullptr);
@@ -498,6 +513,8 @@ extern "C" hale_status hale_matrix_create(hale_ctx* ctx, hale_dtype dtype, uint3
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     hale_matrix* m = new hale_matrix();
     m->ctx = ctx;
+    m->device = ctx->device;
+    ctx->matrices.insert(m);
     m->dtype = dtype;
     m->rows = rows;
     m->cols = cols;
@@ -534,7 +551,8 @@ extern "C" hale_status hale_matrix_create(hale_ctx* ctx, hale_dtype dtype, uint3
 
 extern "C" void hale_matrix_destroy(hale_matrix* m) {
     if (!m) return;
-    cudaSetDevice(m->ctx->device);
+    if (m->ctx) m->ctx->matrices.erase(m);
+    cudaSetDevice(m->device);
     cudaFree(m->data);
     delete m;
 }
@@ -792,6 +810,8 @@ extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     hale_pool* p = new hale_pool();
     p->ctx = ctx;
+    p->device = ctx->device;
+    ctx->pools.insert(p);
     p->dtype = dtype;
     p->H = hidden;
     p->I = inter;
@@ -820,8 +840,11 @@ extern "C" hale_status hale_pool_create(hale_ctx* ctx, hale_dtype dtype, uint32_
 
 extern "C" void hale_pool_destroy(hale_pool* p) {
     if (!p) return;
-    cudaSetDevice(p->ctx->device);
-    drop_host_graphs(p->ctx, p);
+    cudaSetDevice(p->device);
+    if (p->ctx) {
+        drop_host_graphs(p->ctx, p);
+        p->ctx->pools.erase(p);
+    }
     if (p->copy_st) cudaStreamSynchronize(p->copy_st);
     cudaFree(p->data);
     cudaFree(p->staging);
@@ -861,6 +884,8 @@ extern "C" hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, 
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     hale_pool* p = new hale_pool();
     p->ctx = ctx;
+    p->device = ctx->device;
+    ctx->pools.insert(p);
     p->dtype = dtype;
     p->H = hidden;
     p->I = inter;
@@ -976,6 +1001,7 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
                                                uint64_t record_bytes, int on_device, void* stream) {
     if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_upload_expert: pool is NULL");
     hale_ctx* ctx = p->ctx;
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "the pool's context was destroyed");
     if (layer >= p->L || expert >= p->E)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u out of range", layer, expert);
     if (!record) return fail(ctx, HALE_E_INVALID_ARGUMENT, "record is NULL");
@@ -1033,6 +1059,7 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
 extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys, uint64_t n, hale_expert_view* out) {
     if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: pool is NULL");
     hale_ctx* ctx = p->ctx;
+    if (!ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "the pool's context was destroyed");
     if (n && (!keys || !out)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: NULL buffer");
     if (p->tiered) {
         std::vector<int64_t> ks(n);
@@ -1090,6 +1117,7 @@ extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys
 
 extern "C" hale_status hale_pool_routing_counts(hale_pool* p, uint64_t* counts, uint64_t n) {
     if (!p || !counts) return fail(p ? p->ctx : nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_routing_counts: NULL");
+    if (!p->ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "the pool's context was destroyed");
     size_t total = (size_t)p->L * p->E;
     if (n < total) return fail(p->ctx, HALE_E_INVALID_ARGUMENT, "counts needs %zu entries", total);
     CUDA_TRY(p->ctx, cudaSetDevice(p->ctx->device));
@@ -1103,6 +1131,7 @@ extern "C" hale_status hale_pool_routing_counts(hale_pool* p, uint64_t* counts, 
 
 extern "C" hale_status hale_pool_stats(hale_pool* p, hale_cache_stats* out) {
     if (!p || !out) return fail(p ? p->ctx : nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_stats: NULL");
+    if (!p->ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "the pool's context was destroyed");
     size_t total = (size_t)p->L * p->E;
     std::vector<uint64_t> dev(total);
     CUDA_TRY(p->ctx, cudaSetDevice(p->ctx->device));
@@ -1715,6 +1744,356 @@ extern "C" hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, 
 }
 
 // ---------------------------------------------------------------------------
+// Expert parallelism over NVLink peer memory (hale_p2p.cuh)
+// ---------------------------------------------------------------------------
+// NCCL serves only the communicator's set-up: the ranks all-gather their
+// exchange blocks' CUDA IPC handles. It is loaded at run time, so the
+// library has no link-time dependency on it and one-GPU use never loads it.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+static const NcclApi& nccl_api() {
+    static std::once_flag once;
+    static NcclApi api;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(h, "ncclCommInitRank"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+        api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.init_rank && api.all_gather && api.destroy && api.error_string;
+    });
+    return api;
+}
+
+static_assert(sizeof(ncclUniqueId) == HALE_COMM_ID_BYTES, "ncclUniqueId size");
+
+struct hale_comm {
+    hale_ctx* ctx = nullptr;
+    int device = 0;
+    uint32_t R = 1, rank = 0, H = 0, E = 0, k = 0, max_tokens = 0, epr = 0;
+    P2pLayout L{};
+    uint8_t* block = nullptr;          // this rank's exchange block
+    P2pPeers peers{};
+    std::vector<uint8_t*> opened;      // peers' blocks mapped through IPC
+    ncclComm_t nccl = nullptr;
+    uint8_t* d_setup = nullptr;        // handle all-gather buffer
+    unsigned* d_done = nullptr;        // dispatch CTA counter
+    // owner-side lists of one call (kept apart from the ctx workspace, whose
+    // route arrays the home's combine still needs)
+    float* d_ones = nullptr;           // [R * cap]
+    float** d_out_rows = nullptr;      // [R * cap]
+    int* d_elist = nullptr;            // [R * cap]
+    int* d_lists = nullptr;            // elist_off [epr + 1], active [epr], n_active
+    unsigned long long epoch = 0;
+};
+
+extern "C" hale_status hale_comm_unique_id(void* id) {
+    if (!id) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_comm_unique_id: NULL buffer");
+    const NcclApi& api = nccl_api();
+    if (!api.ok) return fail(nullptr, HALE_E_UNSUPPORTED, "NCCL (libnccl.so.2) is not loadable");
+    ncclUniqueId u;
+    const ncclResult_t r = api.get_unique_id(&u);
+    if (r != ncclSuccess) return fail(nullptr, HALE_E_NCCL, "ncclGetUniqueId: %s", api.error_string(r));
+    std::memcpy(id, &u, sizeof u);
+    return HALE_OK;
+}
+
+static void comm_free(hale_comm* c) {
+    if (c->ctx) c->ctx->comms.erase(c);
+    for (uint8_t* p : c->opened) cudaIpcCloseMemHandle(p);
+    c->opened.clear();
+    cudaFree(c->block);
+    cudaFree(c->d_setup);
+    cudaFree(c->d_done);
+    cudaFree(c->d_ones);
+    cudaFree(c->d_out_rows);
+    cudaFree(c->d_elist);
+    cudaFree(c->d_lists);
+    if (c->nccl) nccl_api().destroy(c->nccl);
+    delete c;
+}
+
+// Per rank, in the set-up all-gather: the block's IPC handle and the shape
+// every rank must agree on.
+struct CommSlot {
+    cudaIpcMemHandle_t handle;
+    uint32_t shape[8];
+    uint8_t pad[32];
+};
+static_assert(sizeof(CommSlot) == 128, "CommSlot");
+
+extern "C" hale_status hale_comm_create(hale_ctx* ctx, uint32_t n_ranks, uint32_t rank, const void* unique_id,
+                                        uint32_t hidden, uint32_t n_experts, uint32_t top_k, uint32_t max_tokens,
+                                        hale_comm** out) {
+    if (!ctx || !out) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_comm_create: NULL argument");
+    *out = nullptr;
+    if (n_ranks == 0 || n_ranks > (uint32_t)kP2pMaxRanks || rank >= n_ranks)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "rank %u of %u ranks (1..%d ranks supported)", rank, n_ranks,
+                    kP2pMaxRanks);
+    if (n_experts == 0 || n_experts > 256 || n_experts % n_ranks)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "%u experts do not split evenly over %u ranks", n_experts, n_ranks);
+    if (hidden == 0 || hidden % 32 || top_k == 0 || top_k > n_experts || top_k > 32 || max_tokens == 0 ||
+        max_tokens > 65536)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "bad shape (hidden %u, top_k %u, max_tokens %u)", hidden, top_k,
+                    max_tokens);
+    if (n_ranks > 1 && !unique_id) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_comm_create: NULL unique id");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    hale_comm* c = new hale_comm();
+    c->ctx = ctx;
+    c->device = ctx->device;
+    ctx->comms.insert(c);
+    c->R = n_ranks;
+    c->rank = rank;
+    c->H = hidden;
+    c->E = n_experts;
+    c->k = top_k;
+    c->max_tokens = max_tokens;
+    c->epr = n_experts / n_ranks;
+    const int cap = (int)(max_tokens * std::min(top_k, c->epr));
+    c->L = p2p_layout((int)n_ranks, (int)hidden, aux_stride((int)hidden / 32), cap, (int)(max_tokens * top_k));
+    const size_t nrec = (size_t)n_ranks * cap;
+    bool ok = cudaMalloc(&c->block, c->L.total) == cudaSuccess && cudaMemset(c->block, 0, c->L.total) == cudaSuccess &&
+              cudaMalloc(&c->d_done, 4) == cudaSuccess && cudaMemset(c->d_done, 0, 4) == cudaSuccess &&
+              cudaMalloc(&c->d_ones, nrec * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_out_rows, nrec * sizeof(float*)) == cudaSuccess &&
+              cudaMalloc(&c->d_elist, nrec * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_lists, (2 * (size_t)c->epr + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_setup, (size_t)n_ranks * sizeof(CommSlot)) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        comm_free(c);
+        return fail(ctx, HALE_E_OUT_OF_MEMORY, "cannot allocate the %zu-byte exchange block", (size_t)c->L.total);
+    }
+    c->peers.base[rank] = c->block;
+    if (n_ranks > 1) {
+        const NcclApi& api = nccl_api();
+        if (!api.ok) {
+            comm_free(c);
+            return fail(ctx, HALE_E_UNSUPPORTED, "NCCL (libnccl.so.2) is not loadable");
+        }
+        ncclUniqueId uid;
+        std::memcpy(&uid, unique_id, sizeof uid);
+        ncclResult_t nr = api.init_rank(&c->nccl, (int)n_ranks, uid, (int)rank);
+        if (nr != ncclSuccess) {
+            c->nccl = nullptr;
+            comm_free(c);
+            return fail(ctx, HALE_E_NCCL, "ncclCommInitRank: %s", api.error_string(nr));
+        }
+        CommSlot mine{};
+        if (cudaIpcGetMemHandle(&mine.handle, c->block) != cudaSuccess) {
+            cudaGetLastError();
+            comm_free(c);
+            return fail(ctx, HALE_E_CUDA, "cudaIpcGetMemHandle of the exchange block failed");
+        }
+        const uint32_t shape[8] = {n_ranks, hidden, n_experts, top_k, max_tokens, 0x48414c45u, 1u, 0u};
+        std::memcpy(mine.shape, shape, sizeof shape);
+        std::vector<CommSlot> all(n_ranks);
+        cudaStream_t st = nullptr;
+        ok = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+             cudaMemcpy(c->d_setup + (size_t)rank * sizeof(CommSlot), &mine, sizeof mine, cudaMemcpyHostToDevice) ==
+                 cudaSuccess;
+        if (ok) {
+            nr = api.all_gather(c->d_setup + (size_t)rank * sizeof(CommSlot), c->d_setup, sizeof(CommSlot), ncclUint8,
+                                c->nccl, st);
+            ok = nr == ncclSuccess && cudaStreamSynchronize(st) == cudaSuccess &&
+                 cudaMemcpy(all.data(), c->d_setup, all.size() * sizeof(CommSlot), cudaMemcpyDeviceToHost) ==
+                     cudaSuccess;
+        }
+        if (st) cudaStreamDestroy(st);
+        if (!ok) {
+            cudaGetLastError();
+            comm_free(c);
+            return fail(ctx, HALE_E_NCCL, "exchange of IPC handles failed");
+        }
+        for (uint32_t r = 0; r < n_ranks; r++)
+            if (std::memcmp(all[r].shape, shape, sizeof shape) != 0) {
+                comm_free(c);
+                return fail(ctx, HALE_E_INVALID_ARGUMENT, "rank %u created its communicator with another shape", r);
+            }
+        for (uint32_t r = 0; r < n_ranks; r++) {
+            if (r == rank) continue;
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, all[r].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                comm_free(c);
+                return fail(ctx, HALE_E_CUDA, "cannot map rank %u's exchange block (peer access over NVLink)", r);
+            }
+            c->opened.push_back(static_cast<uint8_t*>(p));
+            c->peers.base[r] = static_cast<uint8_t*>(p);
+        }
+    }
+    // weight 1 for every record: the expert kernels' combine then stores y
+    std::vector<float> ones(nrec, 1.0f);
+    if (cudaMemcpy(c->d_ones, ones.data(), nrec * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        comm_free(c);
+        return fail(ctx, HALE_E_CUDA, "communicator set-up copy failed");
+    }
+    *out = c;
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_comm_destroy(hale_comm* c) {
+    if (!c) return HALE_OK;
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    hale_status r = HALE_OK;
+    if (c->R > 1 && c->nccl) {
+        // every rank is past its last call before any block goes away
+        const NcclApi& api = nccl_api();
+        cudaStream_t st = nullptr;
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess) {
+            const ncclResult_t nr = api.all_gather(c->d_setup + (size_t)c->rank * sizeof(CommSlot), c->d_setup,
+                                                   sizeof(CommSlot), ncclUint8, c->nccl, st);
+            if (nr != ncclSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+                r = fail(c->ctx, HALE_E_NCCL, "hale_comm_destroy: closing barrier failed");
+            cudaStreamDestroy(st);
+        }
+    }
+    comm_free(c);
+    return r;
+}
+
+extern "C" hale_status hale_moe_forward_ep(hale_ctx* ctx, hale_comm* c, hale_pool* p, const hale_moe_layer* ly,
+                                           const float* x, uint32_t M, float* out, int32_t* topk_idx, float* topk_w,
+                                           void* stream) {
+    if (!ctx || !c || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward_ep: NULL ctx, comm or pool");
+    if (c->ctx != ctx || p->ctx != ctx)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "communicator or pool belongs to another context");
+    hale_status r = check_layer(ctx, ly, p->H);
+    if (r) return r;
+    if (p->tiered) return fail(ctx, HALE_E_UNSUPPORTED, "expert parallelism needs an HBM-resident pool");
+    if (ly->n_experts != c->E || ly->top_k != c->k || p->H != c->H || p->E != c->epr)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT,
+                    "layer (%u experts, top-%u), pool (%u experts, hidden %u) and communicator (%u experts over %u "
+                    "ranks, top-%u, hidden %u) disagree",
+                    ly->n_experts, ly->top_k, p->E, p->H, c->E, c->R, c->k, c->H);
+    if (ly->layer >= p->L || p->layer_resident[ly->layer] != p->E)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: this rank's experts are not all resident", ly->layer);
+    if (M > c->max_tokens)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "%u tokens exceed the communicator's %u", M, c->max_tokens);
+    if (M > 0 && (!x || !out)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward_ep: NULL buffer");
+    if (M > 0 && !aligned16(x)) return fail(ctx, HALE_E_INVALID_ARGUMENT, "x must be 16-byte aligned");
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    const int H = (int)p->H, I = (int)p->I, k = (int)c->k, E = (int)c->E, El = (int)c->epr;
+    const int nrec = (int)c->R * c->L.cap;
+    // one workspace plan for both sides, so nothing reallocates mid-call
+    MoeLayout L;
+    if ((r = ensure_moe_ws(ctx, std::max<int>((int)M, nrec), E, k, H, I, stream, &L))) return r;
+    cudaStream_t st = S(stream);
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    const unsigned long long epoch = ++c->epoch;
+    const int half = (int)(epoch & 1);
+    // 1. home: route and quantize this rank's tokens, records to their owners
+    if (M > 0) {
+        if ((r = launch_router(ctx, ly, p->H, x, M, L, true, topk_idx, topk_w, nullptr, nullptr, st))) return r;
+    }
+    {
+        P2pDispatchArgs d{};
+        d.peers = c->peers;
+        d.L = c->L;
+        d.rank = (int)c->rank;
+        d.half = half;
+        d.k = k;
+        d.epr = El;
+        d.epoch = epoch;
+        d.n = (int)M * k;
+        d.elist = reinterpret_cast<const int*>(ws + L.elist);
+        d.elist_off = reinterpret_cast<const int*>(ws + L.elist_off);
+        d.topk_idx = reinterpret_cast<const int*>(ws + L.topk_idx);
+        d.topk_w = reinterpret_cast<const float*>(ws + L.topk_w);
+        d.xq = reinterpret_cast<const int8_t*>(ws + L.xq);
+        d.xaux = reinterpret_cast<const int2*>(ws + L.xaux);
+        d.done = c->d_done;
+        if (M == 0) {
+            // no routes: the counts are zero -- elist_off of an empty call
+            CUDA_TRY(ctx, cudaMemsetAsync(ws + L.elist_off, 0, (size_t)(E + 1) * 4, st));
+        }
+        ProfScope ps_(ctx, "ep_dispatch", st);
+        p2p_dispatch_kernel<<<std::max(1u, (unsigned)((d.n + 7) / 8)), 256, 0, st>>>(d);
+    }
+    if ((r = check_launch(ctx, "p2p_dispatch"))) return r;
+    // 2. owner: every home's records for this call, grouped by local expert
+    int* elist_off = c->d_lists;
+    int* active = c->d_lists + El + 1;
+    int* n_active = c->d_lists + 2 * El + 1;
+    {
+        P2pGatherArgs g{};
+        g.peers = c->peers;
+        g.L = c->L;
+        g.rank = (int)c->rank;
+        g.half = half;
+        g.k = k;
+        g.expert0 = (int)c->rank * El;
+        g.El = El;
+        g.epoch = epoch;
+        g.elist_off = elist_off;
+        g.elist = c->d_elist;
+        g.active = active;
+        g.n_active = n_active;
+        g.ones = c->d_ones;
+        g.out_rows = c->d_out_rows;
+        g.err = ctx->d_err;
+        CUDA_TRY(ctx, allow_smem(p2p_gather_kernel, (size_t)2 * El * 4));
+        ProfScope ps_(ctx, "ep_gather", st);
+        p2p_gather_kernel<<<1, 1024, (size_t)2 * El * 4, st>>>(g);
+    }
+    if ((r = check_launch(ctx, "p2p_gather"))) return r;
+    // 3. owner: the local experts at k = 1; each record's y goes to its home
+    {
+        ExpertArgs a{};
+        a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+        a.expert0 = (int)(ly->layer * p->E);
+        a.expert_stride = p->expert_stride;
+        a.H = H;
+        a.I = I;
+        a.k = 1;
+        a.M = nrec;
+        a.elist_off = elist_off;
+        a.elist = c->d_elist;
+        a.active = active;
+        a.n_active = n_active;
+        a.xq = reinterpret_cast<const int8_t*>(c->block + c->L.q + (size_t)half * nrec * H);
+        a.xaux = reinterpret_cast<const int2*>(c->block + c->L.a + (size_t)half * nrec * c->L.nbp * 8);
+        a.hq = reinterpret_cast<int8_t*>(ws + L.hq);
+        a.haux = reinterpret_cast<int2*>(ws + L.haux);
+        a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+        a.comb_cnt = reinterpret_cast<unsigned*>(ws + L.comb_cnt);
+        a.ws_cnt = reinterpret_cast<unsigned*>(ws + L.ws_cnt);
+        a.topk_w = c->d_ones;
+        a.out = nullptr;
+        a.out_rows = c->d_out_rows;
+        a.err = ctx->d_err;
+        // the families whose combine honours out_rows: streaming, else per-CTA
+        const int saved = ctx->expert_kernel;
+        ctx->expert_kernel = p->ws_maps ? HALE_EXPERT_WS : HALE_EXPERT_DP4A;
+        r = launch_experts(ctx, p, a, (uint32_t)nrec, 1, El, st);
+        ctx->expert_kernel = saved;
+        if (r) return r;
+    }
+    // 4. owner -> homes: this rank's y rows are all written
+    p2p_signal_kernel<<<1, 32, 0, st>>>(c->peers, c->L, (int)c->rank, half, epoch);
+    if ((r = check_launch(ctx, "p2p_signal"))) return r;
+    // 5. home: best-first combine once every owner has signalled
+    {
+        ProfScope ps_(ctx, "ep_combine", st);
+        p2p_combine_kernel<<<dim3((unsigned)((H + 255) / 256), std::max(1u, M)), 256, 0, st>>>(
+            c->block, c->L, half, epoch, reinterpret_cast<const float*>(ws + L.topk_w), (int)M, k, out, ctx->d_err);
+    }
+    return check_launch(ctx, "p2p_combine");
+}
+
+// ---------------------------------------------------------------------------
 // Decode step of the whole model (hale_decoder.cuh)
 // ---------------------------------------------------------------------------
 // A float matrix in the lane-major layout (fgemv_lanes_kernel): cols a
@@ -1726,6 +2105,8 @@ static hale_status matrix_create_lanes(hale_ctx* ctx, hale_dtype dt, uint32_t ro
     const int es = dt == HALE_F32 ? 4 : 2;
     hale_matrix* m = new hale_matrix();
     m->ctx = ctx;
+    m->device = ctx->device;
+    ctx->matrices.insert(m);
     m->dtype = dt;
     m->rows = rows;
     m->cols = cols;
@@ -1768,6 +2149,7 @@ struct hale_decoder {
         uint32_t pool_layer = 0, inter = 0;
     };
     hale_ctx* ctx = nullptr;
+    int device = 0;
     hale_pool* pool = nullptr;
     uint32_t H = 0, L = 0, nh = 0, nkv = 0, hd = 0, V = 0, E = 0, k = 0, max_len = 0;
     uint32_t n_seqs = 1, max_batch = 1;
@@ -1806,7 +2188,8 @@ struct hale_decoder {
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
     if (!d) return;
-    cudaSetDevice(d->ctx->device);
+    if (d->ctx) d->ctx->decoders.erase(d);
+    cudaSetDevice(d->device);
     cudaDeviceSynchronize();
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->cap) cudaStreamDestroy(d->cap);
@@ -1864,6 +2247,8 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     hale_decoder* d = new hale_decoder();
     d->ctx = ctx;
+    d->device = ctx->device;
+    ctx->decoders.insert(d);
     d->pool = pool;
     // a tiered pool resolves each MoE layer's routes on the host mid-step
     d->no_graph = pool && pool->tiered;
@@ -2360,4 +2745,17 @@ extern "C" hale_status hale_moe_route_noalloc(const void* router, hale_dtype rou
 // ---------------------------------------------------------------------------
 extern "C" void hale_expf_host(const float* x, float* y, uint64_t n) {
     for (uint64_t i = 0; i < n; i++) y[i] = hale::hale_expf(x[i]);
+}
+
+// Detaches every object made on ctx (hale_ctx_destroy): each keeps its own
+// device and frees its memory there when it is destroyed later.
+static void ctx_detach_children(hale_ctx* ctx) {
+    for (hale_matrix* m : ctx->matrices) m->ctx = nullptr;
+    for (hale_pool* p : ctx->pools) p->ctx = nullptr;
+    for (hale_decoder* d : ctx->decoders) d->ctx = nullptr;
+    for (hale_comm* c : ctx->comms) c->ctx = nullptr;
+    ctx->matrices.clear();
+    ctx->pools.clear();
+    ctx->decoders.clear();
+    ctx->comms.clear();
 }

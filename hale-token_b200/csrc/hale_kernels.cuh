@@ -917,10 +917,16 @@ struct ExpertArgs {
     unsigned* ws_cnt;         // [4]: streaming kernels' unit / retire counters
     const float* topk_w;      // [M, k]
     float* out;               // [M, H]
+    float* const* out_rows;   // nullable [M]: token t's output row (else out + t * H); NULL entry = drop
     int S1, S2;               // ring depths of the gate/up and down kernels
     int expert0;              // tensor-map slot of expert 0 of the layer (resident pools)
     uint32_t* err;
 };
+
+// Output row of token t of the combine.
+__device__ __forceinline__ float* out_row(const ExpertArgs& a, int t) {
+    return a.out_rows ? a.out_rows[t] : a.out + (size_t)t * a.H;
+}
 
 // Tiled weights of expert e: its own position in a resident pool's layer, or
 // the HBM slot a tiered pool placed it in for this forward.
@@ -1054,7 +1060,8 @@ __global__ void __launch_bounds__(128) expert_down_kernel(ExpertArgs a) {
                 float y = __ldcg(a.ybuf + ((size_t)tok * k + s2) * a.H + tile * kTileRows + lane);
                 o = fadd(o, fmul(w, y));
             }
-            a.out[(size_t)tok * a.H + tile * kTileRows + lane] = o;
+            float* orow = out_row(a, tok);
+            if (orow) orow[tile * kTileRows + lane] = o;
         }
     }
 }

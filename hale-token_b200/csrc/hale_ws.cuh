@@ -678,7 +678,8 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
                     const float y = __ldcg(a.ybuf + ((size_t)tok * k + s2) * a.H + col);
                     o = fadd(o, fmul(w, y));
                 }
-                a.out[(size_t)tok * a.H + col] = o;
+                float* orow = out_row(a, tok);
+                if (orow) orow[col] = o;
             }
         }
     }

@@ -59,6 +59,7 @@ typedef int32_t hale_status;
 #define HALE_E_TIMEOUT (-13)         /* a device-side wait hit its bound */
 #define HALE_E_DEVICE_CHECK (-14)    /* a device-side bounds check tripped */
 #define HALE_E_UNSUPPORTED (-15)     /* valid request this build does not serve */
+#define HALE_E_NCCL (-16)            /* an NCCL call failed (communicator set-up) */
 
 /* Storage formats, same discriminants as DType (src/tensor/dtype.rs:15-25). */
 typedef enum {
@@ -333,6 +334,50 @@ HALE_API hale_status hale_ep_experts(hale_ctx* ctx, hale_pool* pool, uint32_t la
 HALE_API hale_status hale_ep_combine(hale_ctx* ctx, const int32_t* send_meta, const float* y_back,
                                      uint32_t m_tokens, uint32_t top_k, uint32_t hidden, float* out,
                                      void* stream);
+
+/* ---- expert parallelism over NVLink, one call per layer --------------------
+ * MoeLayer::forward (moe.rs:56-70) with the layer's experts split over
+ * n_ranks GPUs of one node, one process (and hale_ctx) per GPU; rank r owns
+ * experts [r * E/R, (r+1) * E/R), held in a resident pool with local ids.
+ * Each rank brings its own tokens. hale_moe_forward_ep routes them, stores
+ * one record per route (the token's q8 row, its block aux and the route)
+ * straight into the owner rank's memory over NVLink, runs this rank's
+ * experts on what every rank sent, stores each y row straight back into its
+ * home rank's memory, and combines best-first -- kernels and peer stores
+ * only, no host synchronisation inside the call. out is bit-identical to
+ * hale_moe_forward with all E experts on one GPU. The reference runs on one
+ * host and has no such split; the surface it replaces is the same
+ * MoeLayer::forward / ExpertProvider::fetch (src/expert/mod.rs:128-137). */
+typedef struct hale_comm hale_comm;
+#define HALE_COMM_ID_BYTES 128
+
+/* A fresh communicator id (an ncclUniqueId, 128 bytes), made on one rank and
+ * handed to every rank by the caller's own means (a TCP store, MPI, ...). */
+HALE_API hale_status hale_comm_unique_id(void* id);
+
+/* Collective over the n_ranks ranks (every rank calls it with the same id
+ * and shape). Allocates this rank's exchange block -- two halves of
+ * n_ranks * max_tokens * min(top_k, E / n_ranks) record slots plus
+ * max_tokens * top_k f32 rows of `hidden` -- and maps every peer's block
+ * through CUDA IPC (NCCL all-gathers the handles; NCCL is loaded at run
+ * time, libnccl.so.2). With n_ranks = 1 there is no NCCL and id may be NULL.
+ * Up to 8 ranks; n_experts must divide by n_ranks. */
+HALE_API hale_status hale_comm_create(hale_ctx* ctx, uint32_t n_ranks, uint32_t rank, const void* id,
+                                      uint32_t hidden, uint32_t n_experts, uint32_t top_k, uint32_t max_tokens,
+                                      hale_comm** out);
+/* Collective: waits for every rank, then frees the block and unmaps peers. */
+HALE_API hale_status hale_comm_destroy(hale_comm* comm);
+
+/* One expert-parallel layer call on every rank (collective: each rank makes
+ * the same sequence of calls, with its own m_tokens <= max_tokens, possibly
+ * 0). pool: this rank's E / n_ranks experts (HBM-resident) at pool layer
+ * layer->layer; layer: the full router (all E experts), replicated.
+ * x, out: [m_tokens, hidden] f32 (device); topk_idx / topk_w (nullable) as
+ * hale_moe_forward. Waits on peers are bounded (about a second): a rank that
+ * never arrives shows up as HALE_E_TIMEOUT at the next hale_ctx_check. */
+HALE_API hale_status hale_moe_forward_ep(hale_ctx* ctx, hale_comm* comm, hale_pool* pool,
+                                         const hale_moe_layer* layer, const float* x, uint32_t m_tokens, float* out,
+                                         int32_t* topk_idx, float* topk_w, void* stream);
 
 /* ---- decode step of the whole model ----------------------------------------
  * Transformer::forward (transformer.rs:168-227) for one token: embedding

@@ -99,3 +99,60 @@ def test_ep_dispatch_rejects_uneven_split(ctx):
     with pytest.raises(hale.HaleError) as ei:
         hale.ep_dispatch(ctx, layer, 64, x, 5, q, aux, meta)
     assert ei.value.status == hale.E_INVALID_ARGUMENT
+
+
+# ---------------------------------------------------------------------------
+# hale_moe_forward_ep on one rank: the whole one-call path (records stored
+# into the exchange block, gathered, expert kernels writing y rows into the
+# y_back half, flags, combine) with this GPU as its own peer.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,H,I,E,k", [(fmt.Q4_0, 2048, 768, 128, 8), (fmt.Q8_0, 256, 128, 16, 4),
+                                           (fmt.Q4_0, 4096, 512, 16, 8)])
+def test_one_call_ep_on_one_rank_matches_the_layer(ctx, dtype, H, I, E, k):
+    ld = fmt.SyntheticLayer(91, E, H, I, dtype)
+    router = torch.from_numpy(fmt.encode(fmt.F32, ld.router)).cuda()
+    layer = hale.moe_layer(0, router, fmt.F32, E, k, True)
+    pool = pool_of(ctx, ld, range(E))
+    comm = hale.Comm(ctx, 1, 0, None, H, E, k, 64)
+    try:
+        # calls alternate between the block's halves; 0 tokens is a legal call
+        for m in (64, 1, 37, 0, 64, 5):
+            x = torch.from_numpy(ld.tokens(max(m, 1), seed=500 + m)).cuda()[:m]
+            out = torch.full((m, H), float("nan"), device="cuda")
+            idx = torch.zeros((m, k), dtype=torch.int32, device="cuda")
+            if m:
+                hale.moe_forward_ep(ctx, comm, pool, layer, x, out, idx)
+            else:
+                hale.moe_forward_ep(ctx, comm, pool, layer, torch.empty((0, H), device="cuda"), out)
+            want = torch.full((m, H), float("nan"), device="cuda")
+            widx = torch.zeros((m, k), dtype=torch.int32, device="cuda")
+            if m:
+                hale.moe_forward(ctx, pool, layer, x, want, widx)
+            ctx.check()
+            assert torch.equal(idx, widx)
+            assert np.array_equal(out.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32)), m
+    finally:
+        comm.close()
+
+
+def test_one_call_ep_rejects_mismatched_shapes(ctx):
+    ld = fmt.SyntheticLayer(92, 16, 256, 128, fmt.Q8_0)
+    router = torch.from_numpy(fmt.encode(fmt.F32, ld.router)).cuda()
+    layer = hale.moe_layer(0, router, fmt.F32, 16, 4, True)
+    pool = pool_of(ctx, ld, range(16))
+    with pytest.raises(hale.HaleError) as ei:
+        hale.Comm(ctx, 3, 0, None, 256, 16, 4, 8)          # 16 experts over 3 ranks
+    assert ei.value.status == hale.E_INVALID_ARGUMENT
+    comm = hale.Comm(ctx, 1, 0, None, 256, 16, 4, 8)
+    try:
+        x = torch.zeros((9, 256), device="cuda")
+        out = torch.empty((9, 256), device="cuda")
+        with pytest.raises(hale.HaleError) as ei:
+            hale.moe_forward_ep(ctx, comm, pool, layer, x, out)   # more than max_tokens
+        assert ei.value.status == hale.E_INVALID_ARGUMENT
+        other = hale.moe_layer(0, router, fmt.F32, 16, 2, True)
+        with pytest.raises(hale.HaleError) as ei:
+            hale.moe_forward_ep(ctx, comm, pool, other, x[:2], out[:2])   # top-2 vs the comm's top-4
+        assert ei.value.status == hale.E_INVALID_ARGUMENT
+    finally:
+        comm.close()

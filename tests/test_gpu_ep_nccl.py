@@ -1,9 +1,12 @@
-"""Expert parallelism over NCCL on several GPUs (skipped below 2 GPUs).
+"""Expert parallelism on several GPUs (skipped below 2 GPUs).
 
 One process per GPU; rank r holds only experts [r*E/R, (r+1)*E/R) of the
-layer and its own tokens; hale-token_b200/ep.py moves the records and y
-rows with NCCL all-to-all-v. Each rank's output must equal hale_moe_forward
-with the full expert pool on its own GPU bit for bit (moe.rs:56-70).
+layer and its own tokens. Two paths move the records and y rows:
+hale_moe_forward_ep (one C call per layer: stores into peer memory over
+NVLink, flags, no host synchronisation) and hale-token_b200/ep.py's NCCL
+all-to-all-v around the hale_ep_* device halves. Each rank's output must
+equal hale_moe_forward with the full expert pool on its own GPU bit for bit
+(moe.rs:56-70).
 """
 import datetime
 import importlib
@@ -18,7 +21,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, port, results):
+def _rank_main(rank, world, port, uid, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch
     import torch.distributed as dist
@@ -52,6 +55,22 @@ def _rank_main(rank, world, port, results):
             diff = int((out.cpu().numpy().view(np.uint32) != want.cpu().numpy().view(np.uint32)).sum())
             results.put((rank, m, diff))
         dist.barrier()
+        # the one-call path: ranks bring different token counts, 0 included
+        comm = hale.Comm(ctx, world, rank, uid, 2048, 128, 8, 64)
+        try:
+            for step in range(4):
+                m = (64, 1, 0, 37)[(step + rank) % 4]
+                x = torch.from_numpy(ld.tokens(max(m, 1), seed=3000 + 10 * rank + step)).cuda()[:m]
+                out = torch.full((m, 2048), float("nan"), device="cuda")
+                hale.moe_forward_ep(ctx, comm, local, layer, x, out)
+                want = torch.full((m, 2048), float("nan"), device="cuda")
+                if m:
+                    hale.moe_forward(ctx, full, layer, x, want)
+                ctx.check()
+                diff = int((out.cpu().numpy().view(np.uint32) != want.cpu().numpy().view(np.uint32)).sum())
+                results.put((rank, 100 + step, diff))
+        finally:
+            comm.close()
     except Exception as exc:
         results.put((rank, -1, repr(exc)))
     finally:
@@ -72,12 +91,13 @@ def test_ep_over_nccl_matches_single_gpu():
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, results)) for r in range(world)]
+    uid = importlib.import_module("hale-token_b200").comm_unique_id()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, uid, results)) for r in range(world)]
     for p in procs:
         p.start()
     got = []
     try:
-        for _ in range(world * 3):
+        for _ in range(world * 7):
             got.append(results.get(timeout=240))
             if got[-1][1] == -1:
                 break
@@ -89,4 +109,4 @@ def test_ep_over_nccl_matches_single_gpu():
     for rank, m, info in got:
         assert m != -1, f"rank {rank} failed: {info}"
         assert info == 0, f"rank {rank}, {m} tokens: {info} values differ from the 1-GPU layer"
-    assert len(got) == world * 3
+    assert len(got) == world * 7
