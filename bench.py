@@ -10,11 +10,13 @@ q4_0 MoE GEMV achieved HBM GB/s").
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M]
   python bench.py --impl reference ...   # the reference's CPU path (oracle port)
 
-Multi-GPU (torchrun): each rank runs its own batch against its own copy of
-the layer (per-GPU work fixed -> weak scaling); the step time is the max
-over ranks. The line also carries "ep": the same layer split over the N
-ranks by expert parallelism (each rank E/N experts and its own M tokens,
-records and y rows exchanged by NCCL all-to-all-v), timed the same way.
+Multi-GPU (torchrun): the layer is split over the N GPUs by expert
+parallelism -- each rank holds E/N experts and brings its own M tokens
+(per-GPU tokens fixed -> weak scaling); a step is one hale_moe_forward_ep
+per rank (records and y rows stored into peer memory over NVLink), timed
+with CUDA events, max over ranks. The line says whether every rank's output
+equals the 1-GPU layer bit for bit, and carries beside it the replicas time
+(every GPU all experts) and the host-driven NCCL all-to-all-v exchange.
 """
 import argparse
 import json
@@ -54,9 +56,11 @@ def parse():
 
 
 def config(m, n):
+    par = ("dp1" if n == 1 else
+           f"ep{n} (experts split over {n} GPUs, {E // n} each; records and y rows over NVLink peer memory)")
     return {"workload": WORKLOAD, "hidden": H, "experts": E, "top_k": K_TOP,
             "moe_intermediate": I, "expert_dtype": "q4_0", "router_dtype": "f32",
-            "tokens_per_gpu": m, "global_batch": m * n, "parallelism": f"dp{n} (experts replicated per GPU)",
+            "tokens_per_gpu": m, "global_batch": m * n, "parallelism": par,
             "inputs": "seeded synthetic: weights N(0,0.02), x N(0,1)",
             "l2": "flushed between timed steps (256 MiB write, untimed)"}
 
@@ -198,6 +202,83 @@ def measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush,
     return {"tok_s": world * m / (ms / 1e3), "ms_per_step": ms, "n_ranks": world, "experts_per_rank": epr,
             "tokens_per_rank": m, "exchange": "NCCL all-to-all-v via torch.distributed (counts, q8 rows, "
             "scales, route metadata; y rows back)", "bit_exact_vs_1gpu": "tests/test_gpu_ep*.py"}
+
+
+def measure_ep_p2p(hale, fmt, ctx, ld, encoded, router, full_pool, world, rank, m, args, flush, barrier,
+                   max_over_ranks, all_true, uid, clocks):
+    """The layer split over `world` GPUs by expert parallelism, one
+    hale_moe_forward_ep per step: this rank holds experts [rank*E/world,
+    (rank+1)*E/world) and brings its own m tokens; records and y rows move by
+    stores into peer memory. Device time per step by CUDA events on the
+    launch stream, L2 flushed before each step, max over ranks. Also: the
+    same call end to end from pinned host buffers (copies in the timed
+    region), and whether every rank's output equals hale_moe_forward over the
+    full pool on one GPU bit for bit."""
+    import torch
+    epr = E // world
+    pool = hale.Pool(ctx, fmt.Q4_0, H, I, 1, epr)
+    for le in range(epr):
+        pool.upload(0, le, fmt.pack_record(*encoded[rank * epr + le]))
+    layer = hale.moe_layer(0, router, fmt.F32, E, K_TOP, True)
+    comm = hale.Comm(ctx, world, rank, uid, H, E, K_TOP, m)
+    stream = torch.cuda.current_stream()
+    try:
+        x = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).cuda()
+        out = torch.empty((m, H), dtype=torch.float32, device="cuda")
+        launches0 = ctx.launches
+        for _ in range(max(args.warmup, 3)):
+            hale.moe_forward_ep(ctx, comm, pool, layer, x, out)
+        ctx.check()
+        per_call = (ctx.launches - launches0) // max(args.warmup, 3)
+        # parity with the 1-GPU layer, on this rank's tokens
+        want = torch.empty_like(out)
+        hale.moe_forward(ctx, full_pool, layer, x, want)
+        ctx.check()
+        exact = bool(torch.equal(out.view(torch.int32), want.view(torch.int32)))
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        clocks.start()
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            hale.moe_forward_ep(ctx, comm, pool, layer, x, out)
+            b.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        barrier()
+        ctx.check()
+        ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+        # end to end: pinned x in, the call, out back, synchronised
+        xh = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).pin_memory()
+        oh = torch.empty((m, H), dtype=torch.float32).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(3):
+            xd.copy_(xh, non_blocking=True)
+            hale.moe_forward_ep(ctx, comm, pool, layer, xd, out)
+            oh.copy_(out, non_blocking=True)
+            torch.cuda.synchronize()
+        barrier()
+        e2e_t = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            xd.copy_(xh, non_blocking=True)
+            hale.moe_forward_ep(ctx, comm, pool, layer, xd, out)
+            oh.copy_(out, non_blocking=True)
+            torch.cuda.synchronize()
+            e2e_t.append(time.perf_counter() - t0)
+        barrier()
+        e2e_s = max_over_ranks(float(np.mean(e2e_t)))
+        exact_all = all_true(exact)
+    finally:
+        comm.close()
+    return {"ms": ms, "per_call_launches": per_call, "bit_exact": exact_all, "clocks": clk,
+            "e2e": {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": world * m * H * 4,
+                    "d2h_bytes_per_step": world * m * H * 4, "ms_per_step": e2e_s * 1e3,
+                    "timing": "host wall clock around x H2D (pinned), hale_moe_forward_ep, out D2H and a "
+                              "synchronize on every rank; max over ranks"}}
 
 
 def run_decode(args):
@@ -461,15 +542,37 @@ def main():
         del g
         return ms, prof, launched, distinct
 
+    def all_true(flag):
+        if world == 1:
+            return bool(flag)
+        t = torch.tensor([1 if flag else 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
+
     m = args.tokens
-    # ---- headline: CUDA-graph replay of the layer call ------------------------
+    ep_p2p = None
     clocks = Clocks(local)
-    clocks.start()
-    time.sleep(0.3)
-    ms, _, launches, distinct = measure(m, args.steps, max(args.warmup, 3), graph=True)
-    clk = clocks.stop()
-    ms_max = max_over_ranks(ms)
-    value = world * m / (ms_max / 1e3)
+    if world > 1:
+        # ---- headline at N > 1: the layer split over the N GPUs (EP) -------
+        uid = [hale.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ep_p2p = measure_ep_p2p(hale, fmt, ctx, ld, encoded, router, pool, world, rank, m, args, flush, barrier,
+                                max_over_ranks, all_true, uid[0], clocks)
+        ms_max = ep_p2p["ms"]
+        value = world * m / (ms_max / 1e3)
+        launches = ep_p2p["per_call_launches"] * args.steps
+        clk = ep_p2p["clocks"]
+        # replicas (every GPU all experts, its own batch) beside it
+        ms_dp, _, _, distinct = measure(m, args.steps, max(args.warmup, 3), graph=True)
+        ms = ms_dp
+    else:
+        # ---- headline: CUDA-graph replay of the layer call --------------------
+        clocks.start()
+        time.sleep(0.3)
+        ms, _, launches, distinct = measure(m, args.steps, max(args.warmup, 3), graph=True)
+        clk = clocks.stop()
+        ms_max = max_over_ranks(ms)
+        value = world * m / (ms_max / 1e3)
     # eager calls with per-kernel events (roofline of the dominant kernel)
     ms_eager, prof, _, _ = measure(m, args.steps, 3, with_profile=True)
 
@@ -500,28 +603,31 @@ def main():
                           "frac": layer_bytes / (ms / 1e3) / 1e9 / peak_gbs}}
     kern = {k: {"launches": n, "avg_ms": (t / n if n else None)} for k, (n, t) in prof.items()}
 
-    # ---- end to end through the public host-buffer call ---------------------
-    xh = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).pin_memory()
-    oh = torch.empty((m, H), dtype=torch.float32).pin_memory()
-    for _ in range(3):
-        hale.moe_forward_host(ctx, pool, layer, xh, oh)
-    barrier()
-    e2e_t = []
-    for _ in range(args.steps):
-        flush.zero_()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        hale.moe_forward_host(ctx, pool, layer, xh, oh)   # H2D, layer, D2H, sync
-        e2e_t.append(time.perf_counter() - t0)
-    barrier()
-    e2e_s = max_over_ranks(float(np.mean(e2e_t)))
-    e2e = {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": m * H * 4,
-           "d2h_bytes_per_step": m * H * 4, "ms_per_step": e2e_s * 1e3,
-           "timing": "host wall clock around hale_moe_forward_host (pinned buffers), max over ranks"}
+    # ---- end to end through the public call with host buffers ---------------
+    if ep_p2p is not None:
+        e2e = ep_p2p["e2e"]
+    else:
+        xh = torch.from_numpy(ld.tokens(m, seed=1000 + rank)).pin_memory()
+        oh = torch.empty((m, H), dtype=torch.float32).pin_memory()
+        for _ in range(3):
+            hale.moe_forward_host(ctx, pool, layer, xh, oh)
+        barrier()
+        e2e_t = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            hale.moe_forward_host(ctx, pool, layer, xh, oh)   # H2D, layer, D2H, sync
+            e2e_t.append(time.perf_counter() - t0)
+        barrier()
+        e2e_s = max_over_ranks(float(np.mean(e2e_t)))
+        e2e = {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": m * H * 4,
+               "d2h_bytes_per_step": m * H * 4, "ms_per_step": e2e_s * 1e3,
+               "timing": "host wall clock around hale_moe_forward_host (pinned buffers), max over ranks"}
 
-    # ---- sweep of the other config-1 batch sizes ----------------------------
+    # ---- sweep of the other config-1 batch sizes (one GPU) ------------------
     sweep = {}
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1:
         for mm in (1, 8, 64, 512):
             s_ms, _, _, s_distinct = measure(mm, max(5, args.steps // 2), 3, graph=True)
             s_ms = max_over_ranks(s_ms)
@@ -530,7 +636,7 @@ def main():
                               "distinct_experts": s_distinct,
                               "layer_hbm_gbs": lb / (s_ms / 1e3) / 1e9}
 
-    # ---- expert parallelism over the N ranks (N > 1) --------------------------
+    # ---- the host-driven NCCL exchange (hale_ep_* halves), for comparison -----
     ep_line = None
     if world > 1 and not args.no_ep:
         ep_line = measure_ep(hale, fmt, ctx, ld, encoded, router, world, rank, m, args, flush, barrier,
@@ -552,11 +658,18 @@ def main():
             "dtype": "q4_0 weights x i8 activations, int32 block dots, f32 accumulate",
             "data": "synthetic", "config": config(m, world), "roofline": roofline,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "kernels": kern,
-            "ms_per_step_eager": ms_eager, "timing": "device: CUDA events around CUDA-graph replays of hale_moe_forward",
+            "ms_per_step_eager": ms_eager,
+            "timing": ("device: CUDA events around CUDA-graph replays of hale_moe_forward" if world == 1 else
+                       "device: CUDA events around each rank's hale_moe_forward_ep, max over ranks"),
             "clocks": clk, "sweep": sweep,
         }
+        if ep_p2p is not None:
+            line["bit_exact_vs_1gpu"] = ep_p2p["bit_exact"]
+            line["launches_per_call"] = ep_p2p["per_call_launches"]
+            line["replicas"] = {"tok_s": world * m / (ms / 1e3), "ms_per_step": ms,
+                                "note": "every GPU all experts and its own batch (no exchange); this rank's time"}
         if ep_line is not None:
-            line["ep"] = ep_line
+            line["ep_host_nccl"] = ep_line
         emit(line)
     ctx.close()
     if world > 1:
