@@ -9,6 +9,8 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cub/device/device_segmented_radix_sort.cuh>
+
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -2611,6 +2613,46 @@ extern "C" hale_status hale_lm_head(hale_ctx* ctx, const hale_matrix* lm_head, c
     return hale_matrix_matvec(ctx, lm_head, hidden, batch, logits, nullptr, stream);
 }
 
+// More than kSampleMaxK candidates: every row's candidates ranked by unique
+// 64-bit keys (logit total order, then index), sorted by CUB's segmented
+// radix sort (compiled from the toolkit's headers), then the reference's
+// exact sums over the sorted order (sample_exp_kernel, sample_tail_kernel).
+// Scratch: two key buffers, exp and probability rows, segment offsets and
+// the sort's temporary storage.
+static hale_status sample_full(hale_ctx* ctx, const SampleArgs& a, uint32_t batch, size_t bitmap_smem,
+                               cudaStream_t st) {
+    const size_t n = (size_t)batch * a.V;
+    if (n > (size_t)INT32_MAX) return fail(ctx, HALE_E_UNSUPPORTED, "batch x vocab above 2^31 candidates");
+    size_t temp = 0;
+    CUDA_TRY(ctx, cub::DeviceSegmentedRadixSort::SortKeysDescending(
+                      nullptr, temp, (const unsigned long long*)nullptr, (unsigned long long*)nullptr, (int)n,
+                      (int)batch, (const int*)nullptr, (const int*)nullptr, 0, 64, st));
+    const size_t o_keys2 = align_up(n * 8, 256), o_e = o_keys2 + align_up(n * 8, 256);
+    const size_t o_q = o_e + align_up(n * 4, 256), o_off = o_q + align_up(n * 4, 256);
+    const size_t o_tmp = o_off + align_up(((size_t)batch + 1) * 4, 256), total = o_tmp + temp;
+    hale_status r = ensure_scratch(ctx, total, st);
+    if (r) return r;
+    uint8_t* sc = static_cast<uint8_t*>(ctx->scratch);
+    auto* keys = reinterpret_cast<unsigned long long*>(sc);
+    auto* sorted = reinterpret_cast<unsigned long long*>(sc + o_keys2);
+    float* e = reinterpret_cast<float*>(sc + o_e);
+    float* q = reinterpret_cast<float*>(sc + o_q);
+    int* off = reinterpret_cast<int*>(sc + o_off);
+    if (bitmap_smem > 48 * 1024)
+        CUDA_TRY(ctx, cudaFuncSetAttribute(sample_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)bitmap_smem));
+    ProfScope ps_(ctx, "sample", st);
+    sample_keys_kernel<<<batch, 1024, bitmap_smem, st>>>(a, keys, off);
+    if ((r = check_launch(ctx, "sample_keys"))) return r;
+    CUDA_TRY(ctx, cub::DeviceSegmentedRadixSort::SortKeysDescending(sc + o_tmp, temp, keys, sorted, (int)n,
+                                                                    (int)batch, off, off + 1, 0, 64, st));
+    sample_exp_kernel<<<dim3((unsigned)((a.top_k + 255) / 256), batch), 256, 0, st>>>(sorted, a.V, a.top_k,
+                                                                                      a.temperature, e);
+    if ((r = check_launch(ctx, "sample_exp"))) return r;
+    sample_tail_kernel<<<batch, 1024, 0, st>>>(sorted, e, q, a.V, a.top_k, a.top_p, a.rng, a.out);
+    return check_launch(ctx, "sample_tail");
+}
+
 extern "C" hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t batch, uint32_t vocab,
                                    const hale_sampling_params* prm, uint64_t* rng_state, const int32_t* seen_ids,
                                    uint32_t n_seen, int32_t* out_tokens, void* stream) {
@@ -2624,9 +2666,6 @@ extern "C" hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t 
     if (prm->temperature > 0.0f) {
         if (!rng_state) return fail(ctx, HALE_E_INVALID_ARGUMENT, "rng_state is NULL");
         K = prm->top_k == 0 ? (int)vocab : (int)std::min<uint32_t>(prm->top_k, vocab);
-        if (K > kSampleMaxK)
-            return fail(ctx, HALE_E_UNSUPPORTED, "top_k=%u over vocab %u keeps %d candidates; this build sorts at most %d",
-                        prm->top_k, vocab, K, kSampleMaxK);
     }
     CUDA_TRY(ctx, cudaSetDevice(ctx->device));
     SampleArgs a{};
@@ -2642,6 +2681,7 @@ extern "C" hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t 
     a.out = out_tokens;
     size_t smem = (seen_ids && n_seen && pen != 1.0f) ? (size_t)((vocab + 31) / 32) * 4 : 0;
     if (smem > 200 * 1024) return fail(ctx, HALE_E_UNSUPPORTED, "vocab %u too large for the penalty bitmap", vocab);
+    if (prm->temperature > 0.0f && K > kSampleMaxK) return sample_full(ctx, a, batch, smem, S(stream));
     if (smem > 48 * 1024) CUDA_TRY(ctx, cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     ProfScope ps_(ctx, "sample", S(stream));
     sample_kernel<<<batch, kSampleThreads, smem, S(stream)>>>(a);

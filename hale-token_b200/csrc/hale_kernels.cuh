@@ -1576,4 +1576,163 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Sampling with more than kSampleMaxK candidates (top_k = 0 keeps the whole
+// vocabulary, sampler.rs:84-93): every candidate is ranked by a unique 64-bit
+// key -- the logit's total-order key, then the inverted index, so the
+// descending key order is the reference's (logit desc, index asc) order --
+// and the keys of each row are sorted by a segmented radix sort. The
+// reference's sums then run in that order, one thread per row, exactly:
+// softmax total over the K best, nucleus mass, kept mass, the draw.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float key_to_float(unsigned long long key) {
+    const int32_t k = (int32_t)((uint32_t)(key >> 32) ^ 0x80000000u);
+    return __int_as_float(k >= 0 ? k : (k ^ 0x7fffffff));
+}
+__device__ __forceinline__ int key_to_index(unsigned long long key) {
+    return 0x7fffffff - (int)(uint32_t)(key & 0xffffffffull);
+}
+
+// keys[row * V + i]; offsets[row] = row * V (segment starts, offsets[B] = B * V).
+__global__ void __launch_bounds__(1024) sample_keys_kernel(SampleArgs a, unsigned long long* __restrict__ keys,
+                                                           int* __restrict__ offsets) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int row = blockIdx.x, tid = threadIdx.x, V = a.V;
+    const float* lg = a.logits + (size_t)row * V;
+    uint32_t* bits = nullptr;
+    if (a.seen && a.n_seen > 0 && a.penalty != 1.0f) {
+        bits = reinterpret_cast<uint32_t*>(smem);
+        for (int i = tid; i < (V + 31) / 32; i += blockDim.x) bits[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < a.n_seen; i += blockDim.x) {
+            const int id = a.seen[(size_t)row * a.n_seen + i];
+            if (id >= 0 && id < V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < V; i += blockDim.x) {
+        const unsigned uk = (unsigned)total_key(penalized(lg, bits, i, a.penalty)) ^ 0x80000000u;
+        keys[(size_t)row * V + i] = ((unsigned long long)uk << 32) | (unsigned)(0x7fffffff - i);
+    }
+    if (tid == 0) {
+        offsets[row] = row * V;
+        if (row == gridDim.x - 1) offsets[row + 1] = (row + 1) * V;
+    }
+}
+
+// e[row * V + j] = exp((v_j - v_0) / T) over the K best (sampler.rs:96-101).
+__global__ void sample_exp_kernel(const unsigned long long* __restrict__ sorted, int V, int K, float temperature,
+                                  float* __restrict__ e) {
+    const int row = blockIdx.y, j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= K) return;
+    const unsigned long long* ks = sorted + (size_t)row * V;
+    const float mx = key_to_float(__ldg(ks));
+    e[(size_t)row * V + j] = hale_expf(fdiv(fsub(key_to_float(__ldg(ks + j)), mx), temperature));
+}
+
+constexpr int kSampleChunk = 4096;
+
+// Streams x[0 .. n) through shared memory in chunks (threads 1.. load the
+// next chunk while thread 0 folds the current one): thread 0 calls
+// step(value, j) in order until it returns false. All threads call this.
+template <class Step>
+__device__ void sample_scan(const float* __restrict__ x, int n, float (*buf)[kSampleChunk], Step step) {
+    const int tid = threadIdx.x;
+    // go[i & 1]: whether chunk i is still wanted; written by thread 0 one
+    // chunk ahead, read by everyone after the barrier that follows
+    __shared__ int s_go[2];
+    if (tid == 0) s_go[0] = 1;
+    for (int j = tid; j < min(n, kSampleChunk); j += blockDim.x) buf[0][j] = __ldcg(x + j);
+    __syncthreads();
+    for (int c0 = 0, it = 0; c0 < n; c0 += kSampleChunk, it++) {
+        if (!s_go[it & 1]) break;
+        const int c1 = c0 + kSampleChunk, ci = it & 1;
+        if (tid == 0) {
+            int go = 1;
+            const int m = min(kSampleChunk, n - c0);
+            for (int j = 0; j < m; j++)
+                if (!step(buf[ci][j], c0 + j)) {
+                    go = 0;
+                    break;
+                }
+            s_go[(it + 1) & 1] = go;
+        } else {
+            for (int j = c1 + tid - 1; j < min(n, c1 + kSampleChunk); j += blockDim.x - 1)
+                buf[ci ^ 1][j - c1] = __ldcg(x + j);
+        }
+        __syncthreads();
+    }
+    __syncthreads();
+}
+
+// One CTA per row: the reference's tail of TopPSampler::sample
+// (sampler.rs:96-123) over the sorted candidates, in its order.
+__global__ void __launch_bounds__(1024) sample_tail_kernel(const unsigned long long* __restrict__ sorted,
+                                                           float* __restrict__ e, float* __restrict__ q, int V,
+                                                           int K, float top_p, uint64_t* __restrict__ rng,
+                                                           int32_t* __restrict__ out) {
+    __shared__ float buf[2][kSampleChunk];
+    __shared__ float s_total;
+    __shared__ int s_keep;
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const float* er = e + (size_t)row * V;
+    float* qr = q + (size_t)row * V;
+    // total: sequential over the K best; once a term leaves the sum unchanged
+    // every later (smaller or equal) one does too
+    float total = 0.0f;
+    sample_scan(er, K, buf, [&](float v, int) {
+        const float t = fadd(total, v);
+        if (t == total) return false;
+        total = t;
+        return true;
+    });
+    if (tid == 0) s_total = total;
+    __syncthreads();
+    total = s_total;
+    for (int j = tid; j < K; j += blockDim.x) qr[j] = fdiv(__ldcg(er + j), total);
+    __syncthreads();
+    // nucleus cut (sampler.rs:103-112)
+    float mass = 0.0f;
+    int keep = K;
+    sample_scan(qr, K, buf, [&](float v, int j) {
+        mass = fadd(mass, v);
+        if (mass >= top_p) {
+            keep = j + 1;
+            return false;
+        }
+        return true;
+    });
+    if (tid == 0) s_keep = keep;
+    __syncthreads();
+    keep = s_keep;
+    float kept = -0.0f;
+    sample_scan(er, keep, buf, [&](float v, int) {
+        kept = fadd(kept, v);
+        return true;
+    });
+    // the draw (sampler.rs:114-122, XorShift64 :128-146)
+    __shared__ float s_r;
+    if (tid == 0) {
+        uint64_t st = rng[row];
+        st ^= st >> 12;
+        st ^= st << 25;
+        st ^= st >> 27;
+        rng[row] = st;
+        const uint64_t u = st * 0x2545F4914F6CDD1DULL;
+        s_r = fmul(fdiv((float)(u >> 40), 16777216.0f), kept);
+    }
+    __syncthreads();
+    float r = s_r;
+    int pick = keep - 1;
+    sample_scan(er, keep, buf, [&](float v, int j) {
+        r = fsub(r, v);
+        if (r <= 0.0f) {
+            pick = j;
+            return false;
+        }
+        return true;
+    });
+    if (tid == 0) out[row] = key_to_index(__ldg(sorted + (size_t)row * V + pick));
+}
+
 }  // namespace hale

@@ -467,7 +467,12 @@ typedef struct {
 } hale_sampling_params;
 
 /* Sampler::sample (sampler.rs:14-18, 80-123) for `batch` rows of logits
- * [batch, vocab] (device). rng_state [batch] u64 (device) holds each row's
+ * [batch, vocab] (device). Up to 1024 candidates (top_k <= 1024, or a vocab
+ * of at most 1024) are selected and sorted in one kernel per row; more
+ * (top_k = 0 with a larger vocab, which keeps every token, or a larger
+ * top_k) are ranked by a segmented radix sort in the ctx's scratch memory,
+ * with the reference's softmax, nucleus and draw sums run over the sorted
+ * order exactly. rng_state [batch] u64 (device) holds each row's
  * XorShift64 state (seed.max(1) initially, sampler.rs:131-133) and is
  * advanced in place. seen_ids [batch, n_seen] i32 (nullable; entries < 0
  * are ignored) feeds the repetition penalty. out_tokens [batch] i32. */

@@ -454,13 +454,37 @@ def test_repetition_penalty_matches_the_oracle(ctx):
         assert list(got[b]) == want
 
 
-def test_sampler_rejects_unsupported_full_sort(ctx):
-    lg = torch.zeros((1, 151936), device="cuda")
-    rng = torch.ones(1, dtype=torch.uint64, device="cuda")
-    out = torch.zeros(1, dtype=torch.int32, device="cuda")
-    with pytest.raises(hale.HaleError) as ei:
-        hale.sample(ctx, lg, hale.SamplingParams(0.7, 0.9, 0, 1.0), rng, out)
-    assert ei.value.status == hale.E_UNSUPPORTED
+@pytest.mark.parametrize("T,top_p,top_k,scale,steps", [(0.7, 0.9, 0, 3.0, 6), (1.0, 0.95, 0, 1.0, 3),
+                                                         (0.7, 0.8, 5000, 3.0, 6), (0.9, 1.0, 0, 8.0, 4)])
+def test_full_vocabulary_stream_matches_the_oracle(ctx, T, top_p, top_k, scale, steps):
+    """top_k = 0 keeps every candidate (sampler.rs:84-93: the whole
+    vocabulary sorted), and top_k above 1024 keeps thousands: the seeded
+    streams equal the oracle's at V = 151936, for a peaked (scale 8) and a
+    flat (scale 1) logit row and with no nucleus cut (top_p 1)."""
+    V, B = 151936, 2
+    rng = np.random.default_rng(int(T * 10) + top_k + int(scale))
+    lg = (rng.standard_normal((B, V)) * scale).astype(np.float32)
+    lg[0, 100] = lg[0, 90000] = float(lg[0].max())   # a tie at the top: lower index first
+    p = hale.SamplingParams(T, top_p, top_k, 1.0)
+    seeds = [5, 987654321]
+    got = gpu_sample(ctx, lg, p, seeds, steps=steps)
+    for b in range(B):
+        s = O.Sampler(temperature=T, top_p=top_p, top_k=top_k, seed=seeds[b])
+        want = [s.sample(lg[b]) for _ in range(steps)]
+        assert list(got[b]) == want, b
+
+
+def test_full_vocabulary_with_repetition_penalty(ctx):
+    V, B, steps = 32000, 3, 5
+    rng = np.random.default_rng(17)
+    lg = (rng.standard_normal((B, V)) * 2).astype(np.float32)
+    seen = np.argsort(-lg, axis=1)[:, :50].astype(np.int32)
+    p = hale.SamplingParams(0.8, 0.9, 0, 1.1)
+    got = gpu_sample(ctx, lg, p, [1, 2, 3], seen=seen, steps=steps)
+    for b in range(B):
+        s = O.Sampler(temperature=0.8, top_p=0.9, top_k=0, seed=[1, 2, 3][b])
+        want = [s.sample(lg[b], seen=seen[b], repetition_penalty=1.1) for _ in range(steps)]
+        assert list(got[b]) == want
 
 
 def test_kernels_were_launched_from_this_library(ctx):
