@@ -45,7 +45,9 @@ def parse():
     p.add_argument("--impl", default="hale", choices=["hale", "reference"])
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--no-ep", action="store_true", help="skip the expert-parallel measurement at N > 1")
+    p.add_argument("--no-ep", action="store_true", help="skip the host-driven NCCL exchange measurement at N > 1")
+    p.add_argument("--no-decode", action="store_true",
+                   help="skip the whole-model decode figures (config-2 shapes) carried in the N=1 line")
     p.add_argument("--decode", action="store_true",
                    help="whole-model decode tok/s (BASELINE config 2 shapes; --batch sequences) instead of the layer")
     p.add_argument("--layers", type=int, default=48, help="--decode: decoder layers")
@@ -239,12 +241,20 @@ def measure_ep_p2p(hale, fmt, ctx, ld, encoded, router, full_pool, world, rank, 
         barrier()
         torch.cuda.synchronize()
         clocks.start()
+        time.sleep(0.3)
+        # the timed steps, repeated (untimed) until the clock sampler has seen
+        # the GPU under load for a while
         for a, b in evs:
             flush.zero_()
             a.record(stream)
             hale.moe_forward_ep(ctx, comm, pool, layer, x, out)
             b.record(stream)
         torch.cuda.synchronize()
+        t_end = time.perf_counter() + 0.5
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                hale.moe_forward_ep(ctx, comm, pool, layer, x, out)
+            torch.cuda.synchronize()
         clk = clocks.stop()
         barrier()
         ctx.check()
@@ -281,27 +291,14 @@ def measure_ep_p2p(hale, fmt, ctx, ld, encoded, router, full_pool, world, rank, 
                               "synchronize on every rank; max over ranks"}}
 
 
-def run_decode(args):
-    """Whole-model decode with BASELINE config 2's shapes (Qwen3-30B-A3B:
-    hidden 2048, 32 q / 4 kv heads of 128, q/k norms, 128 experts top-8 of
-    intermediate 768 in q4_0, vocab 151936, bf16 attention, embedding and
-    lm_head). Synthetic weights: one layer's 128 expert records uploaded to
-    every layer (each layer its own copy in HBM), random bf16 dense weights
-    N(0, 0.02), norms 1.0. Each of `batch` sequences first prefills a
-    `prompt`-token random prompt in batched steps (timed: prefill tok/s);
-    then a step is one token of every sequence -> logits for each, timed
-    with CUDA events (device time, no L2 flush: the per-step working set is
-    3.5 GB and up). Batch 1 steps go through hale_decoder_forward (one
-    captured CUDA graph replayed), batch B through hale_decoder_step."""
-    import importlib
-
-    import torch
-    hale = importlib.import_module("hale-token_b200")
-    fmt = importlib.import_module("hale-token_b200.formats")
-    torch.cuda.set_device(0)
-    ctx = hale.Context(0)
-    L, Hd, nh, nkv, hd, V = args.layers, 2048, 32, 4, 128, 151936
-    B = max(1, args.batch)
+def build_decoder(hale, fmt, ctx, L, n_seqs, max_batch, max_len):
+    """A Qwen3-30B-A3B-shaped decoder: hidden 2048, 32 q /
+    4 kv heads of 128, q/k norms, 128 experts top-8 of intermediate 768 in
+    q4_0, vocab 151936, bf16 attention, embedding and lm_head. Synthetic
+    weights: one layer's 128 expert records uploaded to every layer (each
+    layer its own copy in HBM), random bf16 dense weights N(0, 0.02), norms
+    1.0."""
+    Hd, nh, nkv, hd, V = 2048, 32, 4, 128, 151936
     rng = np.random.default_rng(SEED)
 
     def bf16(rows, cols):
@@ -324,41 +321,58 @@ def run_decode(args):
                            router=router))
     dims = dict(hidden=Hd, n_layers=L, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, n_experts=E, top_k=K_TOP,
                 normalize_topk=1, eps=1e-6, rope_theta=1e6)
-    max_len = args.prompt + args.steps + args.warmup + 6   # + the profiled steps
-    chunk = max(B, min(args.prompt, 512))
-    dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len, n_seqs=B,
-                       max_batch=chunk)
+    dec = hale.Decoder(ctx, dims, layers, bf16(V, Hd), bf16(V, Hd), ones_h, pool, max_len, n_seqs=n_seqs,
+                       max_batch=max_batch)
+    shape = {"layers": L, "hidden": Hd, "heads": nh, "kv_heads": nkv, "head_dim": hd, "vocab": V, "experts": E,
+             "top_k": K_TOP, "moe_intermediate": I}
+    bytes_per_token = {"expert": 2 * I * fmt.row_bytes(fmt.Q4_0, Hd) + Hd * fmt.row_bytes(fmt.Q4_0, I),
+                       "attn": ((nh + 2 * nkv) * hd * Hd + Hd * nh * hd) * 2, "router": E * Hd * 4,
+                       "lm_head": V * Hd * 2}
+    return dec, pool, shape, bytes_per_token
+
+
+def decode_measure(hale, ctx, dec, shape, bpt, B, prompt, steps, warmup, seq0=0):
+    """Whole-model decode of B sequences (seq0 .. seq0+B-1): each first
+    prefills a `prompt`-token random prompt in batched steps (timed: prefill
+    tok/s); then a step is one token of every sequence -> logits for each,
+    timed with CUDA events (device time, no L2 flush: the per-step working
+    set is 3.5 GB and up). B = 1 steps go through hale_decoder_forward (one
+    captured CUDA graph replayed), B > 1 through hale_decoder_step."""
+    import torch
+    L, V = shape["layers"], shape["vocab"]
+    rng = np.random.default_rng(SEED + B)
+    chunk = max(B, min(prompt, 512))
     logits = torch.empty((B, V), dtype=torch.float32, device="cuda")
+    max_len = prompt + steps + warmup + 6
     toks = rng.integers(0, V, size=(B, max_len))
     stream = torch.cuda.current_stream()
-    # prefill: each sequence's prompt in steps of up to `chunk` consecutive positions
-    pre_ms = 0.0
+    pre_ms, pre_tokens = 0.0, 0
     for b in range(B):
-        for s0 in range(0, args.prompt, chunk):
-            s1 = min(args.prompt, s0 + chunk)
+        for s0 in range(0, prompt, chunk):
+            s1 = min(prompt, s0 + chunk)
             a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            dec.step(toks[b, s0:s1], np.arange(s0, s1), np.full(s1 - s0, b), logits=logits[:1],
+            dec.step(toks[b, s0:s1], np.arange(s0, s1), np.full(s1 - s0, seq0 + b), logits=logits[:1],
                      last_logits_only=True)
             e.record(stream)
             torch.cuda.synchronize()
             if b > 0 or s0 > 0 or B == 1:   # the very first step warms the kernels
                 pre_ms += a.elapsed_time(e)
-    pre_tokens = args.prompt * B - (0 if B == 1 else min(chunk, args.prompt))
-    pos = args.prompt
-    seq_ids = np.arange(B)
+                pre_tokens += s1 - s0
+    pos = prompt
+    seq_ids = np.arange(seq0, seq0 + B)
 
     def one_step(p):
-        if B == 1:
+        if B == 1 and seq0 == 0:
             dec.forward(int(toks[0, p]), p, logits[0])
         else:
             dec.step(toks[:, p], np.full(B, p), seq_ids, logits=logits)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         one_step(pos)
         pos += 1
     ctx.check()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     for a, b in evs:
         a.record(stream)
@@ -369,7 +383,7 @@ def run_decode(args):
     ctx.check()
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     # per-kernel device time of eager steps (hale_ctx_profile: CUDA events around each launch)
-    n_prof = min(5, max(1, args.steps))
+    n_prof = min(3, max(1, steps))
     ctx.profile(True)
     for _ in range(n_prof):
         dec.step(toks[:, pos], np.full(B, pos), seq_ids, logits=logits)
@@ -382,33 +396,59 @@ def run_decode(args):
         if cnt:
             kernels[nm] = {"launches_per_step": cnt / n_prof, "us_per_step": tot * 1e3 / n_prof}
     ctx.profile(False)
-    q4r_h, q4r_i = fmt.row_bytes(fmt.Q4_0, Hd), fmt.row_bytes(fmt.Q4_0, I)
-    expert_bytes = 2 * I * q4r_h + Hd * q4r_i
-    attn_bytes = ((nh + 2 * nkv) * hd * Hd + Hd * nh * hd) * 2
     # distinct experts a step reads: expected over B tokens' independent top-8 picks
     distinct = E * (1 - (1 - K_TOP / E) ** B)
-    per_step_bytes = L * (distinct * expert_bytes + attn_bytes + E * Hd * 4) + V * Hd * 2
-    line = {"metric": "decode_tok_s_full_model", "value": B * 1e3 / ms, "unit": "tok/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 experts, bf16 dense, f32 activations",
-            "data": "synthetic",
-            "config": {"workload": f"qwen3_30b_a3b_decode_b{B}", "layers": L, "hidden": Hd, "heads": nh,
-                       "kv_heads": nkv, "head_dim": hd, "vocab": V, "experts": E, "top_k": K_TOP,
-                       "moe_intermediate": I, "batch": B, "positions_before_timing": args.prompt},
+    per_step_bytes = L * (distinct * bpt["expert"] + bpt["attn"] + bpt["router"]) + bpt["lm_head"]
+    return {"tok_s": B * 1e3 / ms, "ms_per_step": ms, "batch": B, "positions_before_timing": prompt,
+            "steps": steps, "warmup": warmup,
             "timing": ("CUDA events around each step; steps after the first replay one captured CUDA graph "
                        "(token and position through device memory)") if B == 1 else
                       "CUDA events around each hale_decoder_step of B rows (one per sequence)",
-            "gpu_launches_per_step": 2 + L * 9,
-            "algorithmic_bytes_per_step": per_step_bytes,
-            "achieved_gbs": per_step_bytes / (ms / 1e3) / 1e9,
+            "algorithmic_bytes_per_step": per_step_bytes, "achieved_gbs": per_step_bytes / (ms / 1e3) / 1e9,
             "kernels": kernels,
             "kernels_timing": "eager hale_decoder_step calls with per-launch CUDA events (adds event overhead)",
-            "prefill": {"tok_s": pre_tokens / (pre_ms / 1e3) if pre_ms > 0 else None, "prompt": args.prompt,
+            "prefill": {"tok_s": pre_tokens / (pre_ms / 1e3) if pre_ms > 0 else None, "prompt": prompt,
                         "rows_per_step": chunk, "timed_tokens": pre_tokens,
                         "timing": "CUDA events around batched hale_decoder_step calls (first one untimed at B > 1)"}}
+
+
+def run_decode(args):
+    """bench.py --decode: the decode figures alone, as their own line."""
+    import importlib
+
+    import torch
+    hale = importlib.import_module("hale-token_b200")
+    fmt = importlib.import_module("hale-token_b200.formats")
+    torch.cuda.set_device(0)
+    ctx = hale.Context(0)
+    B = max(1, args.batch)
+    max_len = args.prompt + args.steps + args.warmup + 6
+    dec, pool, shape, bpt = build_decoder(hale, fmt, ctx, args.layers, B, max(B, min(args.prompt, 512)), max_len)
+    r = decode_measure(hale, ctx, dec, shape, bpt, B, args.prompt, args.steps, args.warmup)
+    line = {"metric": "decode_tok_s_full_model", "value": r["tok_s"], "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 experts, bf16 dense, f32 activations",
+            "data": "synthetic", "config": dict(workload=f"qwen3_30b_a3b_decode_b{B}", batch=B, **shape),
+            "decode": r}
     emit(line)
     dec.close()
     ctx.close()
+
+
+def decode_block(hale, fmt, ctx, steps, warmup):
+    """The whole-model decode figures carried in the headline line (BASELINE
+    config 2 shapes, 48 layers): batch 1 and batch 16 at position 512."""
+    prompt, L = 512, 48
+    max_len = prompt + steps + warmup + 8
+    dec, pool, shape, bpt = build_decoder(hale, fmt, ctx, L, 17, 512, max_len)
+    try:
+        b1 = decode_measure(hale, ctx, dec, shape, bpt, 1, prompt, steps, warmup)
+        b16 = decode_measure(hale, ctx, dec, shape, bpt, 16, prompt, steps, warmup, seq0=1)
+    finally:
+        dec.close()
+        del pool
+    return {"metric": "decode_tok_s_full_model", "unit": "tok/s",
+            "config": dict(workload="qwen3_30b_a3b_decode", **shape), "b1": b1, "b16": b16}
 
 
 def run_reference(args):
@@ -650,6 +690,11 @@ def main():
                "sample": f"{done} tokens of the same layer in {dt:.1f} s (batches of 8); "
                          f"oracle/hale_oracle.c -O2 -march=native, OpenMP {cores} threads, {cpu_model()}"}
 
+    # ---- whole-model decode, BASELINE config 2 shapes (rank 0, N=1 only) ----
+    decode = None
+    if rank == 0 and world == 1 and not args.no_decode:
+        decode = decode_block(hale, fmt, ctx, steps=16, warmup=3)
+
     if rank == 0:
         line = {
             "metric": "decode_tok_s_moe_layer", "value": value, "unit": "tok/s", "n_gpus": world,
@@ -663,6 +708,8 @@ def main():
                        "device: CUDA events around each rank's hale_moe_forward_ep, max over ranks"),
             "clocks": clk, "sweep": sweep,
         }
+        if decode is not None:
+            line["decode"] = decode
         if ep_p2p is not None:
             line["bit_exact_vs_1gpu"] = ep_p2p["bit_exact"]
             line["launches_per_call"] = ep_p2p["per_call_launches"]
