@@ -120,6 +120,7 @@ SIGNATURES = {
     "hale_comm_create": (I32, [P, U32, U32, P, U32, U32, U32, U32, C.POINTER(P)]),
     "hale_comm_destroy": (I32, [P]),
     "hale_moe_forward_ep": (I32, [P, P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
+    "hale_decoder_set_comm": (I32, [P, P]),
     "hale_decoder_create": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, C.POINTER(P)]),
     "hale_decoder_destroy": (None, [P]),
     "hale_decoder_forward": (I32, [P, P, U32, U32, P, P, P]),
@@ -444,6 +445,12 @@ class Decoder:
         self.ctx.call("hale_decoder_step", self.ctx.h, self.h, t.ctypes.data, p.ctypes.data,
                       None if sq is None else sq.ctypes.data, int(t.size), ptr(logits), int(bool(last_logits_only)),
                       ptr(hidden), _stream(stream))
+
+    def set_comm(self, comm):
+        """hale_decoder_set_comm: MoE layers expert-parallel over `comm` (this
+        decoder's pool holds the rank's share of the experts), or None."""
+        self.ctx.call("hale_decoder_set_comm", self.h, comm.h if comm is not None else None)
+        self.comm = comm
 
     def close(self):
         if getattr(self, "h", None):

@@ -2153,6 +2153,7 @@ struct hale_decoder {
     hale_ctx* ctx = nullptr;
     int device = 0;
     hale_pool* pool = nullptr;
+    hale_comm* comm = nullptr;  // set: MoE layers run expert-parallel (hale_moe_forward_ep)
     uint32_t H = 0, L = 0, nh = 0, nkv = 0, hd = 0, V = 0, E = 0, k = 0, max_len = 0;
     uint32_t n_seqs = 1, max_batch = 1;
     size_t seq_stride = 0;  // floats per sequence in one layer's K (or V) cache
@@ -2203,6 +2204,33 @@ extern "C" void hale_decoder_destroy(hale_decoder* d) {
     if (d->lm_head) hale_matrix_destroy(d->lm_head);
     for (void* p : d->allocs) cudaFree(p);
     delete d;
+}
+
+extern "C" hale_status hale_decoder_set_comm(hale_decoder* d, hale_comm* c) {
+    if (!d || !d->ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_decoder_set_comm: bad decoder");
+    hale_ctx* ctx = d->ctx;
+    if (!c) {
+        d->comm = nullptr;
+        return HALE_OK;
+    }
+    if (c->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "communicator belongs to another context");
+    if (!d->pool) return fail(ctx, HALE_E_INVALID_ARGUMENT, "decoder has no MoE layers");
+    if (c->E != d->E || c->k != d->k || c->H != d->H || d->pool->E != c->epr || d->pool->tiered)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT,
+                    "communicator (%u experts over %u ranks, top-%u, hidden %u) does not match the decoder "
+                    "(%u experts, top-%u, hidden %u) and its pool of %u resident experts per layer",
+                    c->E, c->R, c->k, c->H, d->E, d->k, d->H, d->pool->E);
+    if (c->max_tokens < d->max_batch)
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "communicator takes %u tokens per call, decoder steps up to %u",
+                    c->max_tokens, d->max_batch);
+    d->comm = c;
+    // every call advances the exchange's epoch: steps run eagerly
+    d->no_graph = true;
+    if (d->exec) {
+        cudaGraphExecDestroy(d->exec);
+        d->exec = nullptr;
+    }
+    return HALE_OK;
 }
 
 static hale_status dec_alloc(hale_ctx* ctx, hale_decoder* d, size_t bytes, void** out) {
@@ -2304,7 +2332,8 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
         if (s.k_norm && (r = dec_upload(ctx, d, s.k_norm, hd * 4, reinterpret_cast<void**>(&ly.k_norm)))) return bail(r);
         ly.is_moe = s.is_moe ? 1 : 0;
         if (ly.is_moe) {
-            if (!pool || pool->ctx != ctx || pool->H != H || pool->E != d->E || moe_layers >= pool->L)
+            // all E experts, or one rank's share of them (E / R, for hale_decoder_set_comm)
+            if (!pool || pool->ctx != ctx || pool->H != H || !pool->E || d->E % pool->E || moe_layers >= pool->L)
                 return bail(fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: the expert pool does not hold MoE layer %u "
                                  "(%u experts of hidden %u)", l, moe_layers, d->E, H));
             if (!is_float((hale_dtype)s.router.dtype) || s.router.rows != d->E || s.router.cols != H || !s.router.data)
@@ -2481,7 +2510,11 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             m.n_experts = d->E;
             m.top_k = d->k;
             m.normalize_topk = d->normalize;
-            if ((r = hale_moe_forward(ctx, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream))) return r;
+            if (d->comm)
+                r = hale_moe_forward_ep(ctx, d->comm, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream);
+            else
+                r = hale_moe_forward(ctx, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream);
+            if (r) return r;
         } else {
             if ((r = hale_matrix_matvec(ctx, ly.gate, d->normed, n, d->g, nullptr, stream))) return r;
             if ((r = hale_matrix_matvec(ctx, ly.up, d->normed, n, d->u, nullptr, stream))) return r;

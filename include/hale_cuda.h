@@ -449,6 +449,18 @@ HALE_API hale_status hale_decoder_step(hale_ctx* ctx, hale_decoder* dec, const u
                                        const uint32_t* positions, const uint32_t* seqs, uint32_t n,
                                        float* logits, int32_t last_logits_only, float* hidden, void* stream);
 
+/* Expert-parallel decoding: the decoder's MoE layers run through
+ * hale_moe_forward_ep over `comm`, with the decoder's pool holding this
+ * rank's n_experts / n_ranks experts of every MoE layer (HBM-resident);
+ * attention and the dense layers stay on this rank for its own sequences
+ * (data-parallel). Every rank must then make the same sequence of decoder
+ * calls (collective per MoE layer; its own rows each time), which run
+ * eagerly (no graph replay). comm NULL returns to single-GPU layers.
+ * comm's max_tokens must cover the decoder's max_batch. Such a decoder is
+ * created with the rank's pool (n_experts / n_ranks experts per layer);
+ * until its comm is set, its MoE calls fail with HALE_E_INVALID_ARGUMENT. */
+HALE_API hale_status hale_decoder_set_comm(hale_decoder* dec, hale_comm* comm);
+
 /* ---- sampling tail -------------------------------------------------------- */
 
 /* Transformer::logits (transformer.rs:217-221): logits[b, :] = lm_head .

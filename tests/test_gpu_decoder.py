@@ -40,9 +40,11 @@ def ctx():
     c.close()
 
 
-def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1):
+def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1, experts=None):
     """The fixture's tensors (same names and normalisation as the oracle
-    loader) as hale_decoder descriptors, experts encoded like the oracle's."""
+    loader) as hale_decoder descriptors, experts encoded like the oracle's.
+    experts: the global expert ids the pool holds (local ids 0..), default
+    all of them (an expert-parallel rank holds its own block)."""
     c = om.cfg
     expert_name, router_name, dense_name = OM._names(c["qwen"])
 
@@ -52,8 +54,9 @@ def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1):
 
     moe_layers = [l for l in range(c["layers"]) if l not in c["dense_layers"]]
     pool = None
+    ids = list(range(c["experts"] or 0)) if experts is None else list(experts)
     if moe_layers:
-        pool = hale.Pool(ctx, expert_dtype, c["hidden"], c["expert_inter"], len(moe_layers), c["experts"])
+        pool = hale.Pool(ctx, expert_dtype, c["hidden"], c["expert_inter"], len(moe_layers), len(ids))
     layers = []
     for l in range(c["layers"]):
         p = f"model.layers.{l}."
@@ -70,12 +73,12 @@ def build_decoder(ctx, om, expert_dtype, max_len, n_seqs=1, max_batch=1):
         else:
             L["router"] = hm(router_name(l))
             j = moe_layers.index(l)
-            for e in range(c["experts"]):
+            for le, e in enumerate(ids):
                 if om.expert_encoded is not None:
                     enc = [om.expert_encoded(l, e, pj) for pj in ("gate", "up", "down")]
                 else:
                     enc = [O.encode(expert_dtype, om.f32(expert_name(l, e, pj))) for pj in ("gate", "up", "down")]
-                pool.upload(j, e, fmt.pack_record(*enc))
+                pool.upload(j, le, fmt.pack_record(*enc))
         layers.append(L)
     embed = hm("model.embed_tokens.weight")
     head = embed if (c["tie"] or "lm_head.weight" not in om.t) else hm("lm_head.weight")
@@ -354,3 +357,38 @@ def test_wide_heads_take_the_decode_attention_kernel(ctx, head_dim):
     om = OM.OracleModel(expert_dtype=fmt.Q8_0, hf_config=hf, tensors=t, expert_encoded=enc)
     prompt = np.random.default_rng(5).integers(0, 256, 12).tolist()
     _decode_and_compare(ctx, om, fmt.Q8_0, prompt, 8)
+
+
+def test_expert_parallel_decoder_on_one_rank(ctx):
+    """hale_decoder_set_comm with a one-rank communicator: the MoE layers run
+    through hale_moe_forward_ep and every position's logits equal the
+    oracle's (batched prefill rows, then single rows, eagerly)."""
+    hf, t, enc = synth.qwen3_moe(6, 2, 256, 8, 2, 32, 16, 4, 128, 512, fmt.Q8_0, "F32")
+    om = OM.OracleModel(expert_dtype=fmt.Q8_0, hf_config=hf, tensors=t, expert_encoded=enc)
+    tokens = np.random.default_rng(8).integers(0, 512, 10).tolist()
+    want = om.teacher_forced_logits(tokens)
+    dec = build_decoder(ctx, om, fmt.Q8_0, len(tokens), max_batch=4)
+    comm = hale.Comm(ctx, 1, 0, None, 256, 16, 4, 4)
+    try:
+        dec.set_comm(comm)
+        logits = torch.empty((4, om.cfg["vocab"]), dtype=torch.float32, device="cuda")
+        got = []
+        dec.step(tokens[:4], list(range(4)), logits=logits)
+        got.append(logits.cpu().numpy().copy())
+        one = torch.empty(om.cfg["vocab"], dtype=torch.float32, device="cuda")
+        for i in range(4, len(tokens)):
+            dec.forward(tokens[i], i, one)
+            got.append(one.cpu().numpy()[None].copy())
+        ctx.check()
+        assert _bits_equal(np.concatenate(got), want)
+        with pytest.raises(hale.HaleError) as ei:     # a communicator of the wrong shape
+            small = hale.Comm(ctx, 1, 0, None, 256, 16, 4, 2)
+            try:
+                dec.set_comm(small)
+            finally:
+                small.close()
+        assert ei.value.status == hale.E_INVALID_ARGUMENT
+    finally:
+        dec.set_comm(None)
+        comm.close()
+        dec.close()

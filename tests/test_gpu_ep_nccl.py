@@ -21,7 +21,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, port, uid, results):
+def _rank_main(rank, world, port, uid, uid2, uid3, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch
     import torch.distributed as dist
@@ -71,6 +71,46 @@ def _rank_main(rank, world, port, uid, results):
                 results.put((rank, 100 + step, diff))
         finally:
             comm.close()
+        # whole-model decode with expert-parallel MoE layers: this rank's own
+        # sequence; its logits equal the one-GPU decoder's at every position
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        import synth
+        from oracle import model as OM
+        from test_gpu_decoder import build_decoder
+        cases = ((fmt.Q8_0, uid2, (0, 3, 256, 8, 2, 32, 16, 4, 128, 512)),   # config-0 form: 16 experts top-4
+                 (fmt.Q4_0, uid3, (3, 2, 512, 8, 2, 64, 8, 2, 256, 320)))    # Mixtral form: 8 experts top-2
+        for qt, duid, shape in cases:
+            seed, L, Hh, nh, nkv, hd, E2, k2, I2, V2 = shape
+            hf, tt, enc = synth.qwen3_moe(seed, L, Hh, nh, nkv, hd, E2, k2, I2, V2, qt, "F32")
+            om = OM.OracleModel(expert_dtype=qt, hf_config=hf, tensors=tt, expert_encoded=enc)
+            e_r = E2 // world
+            toks = np.random.default_rng(40 + rank).integers(0, V2, 9).tolist()
+            full_dec = build_decoder(ctx, om, qt, len(toks), max_batch=4)
+            ep_dec = build_decoder(ctx, om, qt, len(toks), max_batch=4, experts=range(rank * e_r, (rank + 1) * e_r))
+            dcomm = hale.Comm(ctx, world, rank, duid, Hh, E2, k2, 4)
+            try:
+                ep_dec.set_comm(dcomm)
+                got, want = [], []
+                lg = torch.empty((4, V2), dtype=torch.float32, device="cuda")
+                lw = torch.empty((4, V2), dtype=torch.float32, device="cuda")
+                ep_dec.step(toks[:4], list(range(4)), logits=lg)
+                full_dec.step(toks[:4], list(range(4)), logits=lw)
+                got.append(lg.cpu().numpy().copy())
+                want.append(lw.cpu().numpy().copy())
+                for i in range(4, len(toks)):
+                    ep_dec.step([toks[i]], [i], logits=lg[:1])
+                    full_dec.step([toks[i]], [i], logits=lw[:1])
+                    got.append(lg[:1].cpu().numpy().copy())
+                    want.append(lw[:1].cpu().numpy().copy())
+                ctx.check()
+                diff = int((np.concatenate(got).view(np.uint32) != np.concatenate(want).view(np.uint32)).sum())
+                results.put((rank, 200 + qt, diff))
+            finally:
+                ep_dec.set_comm(None)
+                dcomm.close()
+                ep_dec.close()
+                full_dec.close()
     except Exception as exc:
         results.put((rank, -1, repr(exc)))
     finally:
@@ -91,13 +131,14 @@ def test_ep_over_nccl_matches_single_gpu():
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    uid = importlib.import_module("hale-token_b200").comm_unique_id()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, uid, results)) for r in range(world)]
+    hl = importlib.import_module("hale-token_b200")
+    uid, uid2, uid3 = hl.comm_unique_id(), hl.comm_unique_id(), hl.comm_unique_id()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, uid, uid2, uid3, results)) for r in range(world)]
     for p in procs:
         p.start()
     got = []
     try:
-        for _ in range(world * 7):
+        for _ in range(world * 9):
             got.append(results.get(timeout=240))
             if got[-1][1] == -1:
                 break
@@ -109,4 +150,4 @@ def test_ep_over_nccl_matches_single_gpu():
     for rank, m, info in got:
         assert m != -1, f"rank {rank} failed: {info}"
         assert info == 0, f"rank {rank}, {m} tokens: {info} values differ from the 1-GPU layer"
-    assert len(got) == world * 7
+    assert len(got) == world * 9
