@@ -108,6 +108,7 @@ SIGNATURES = {
     "hale_pool_expert_bytes": (U64, [P]),
     "hale_pool_create_tiered": (I32, [P, C.c_int, U32, U32, U32, U32, C.POINTER(CachePolicyStruct), C.POINTER(P)]),
     "hale_pool_hbm_slots": (U64, [P]),
+    "hale_pool_set_source": (I32, [P, P, P]),
     "hale_moe_forward": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_forward_host": (I32, [P, P, C.POINTER(MoeLayer), P, U32, P, P, P, P]),
     "hale_moe_route": (I32, [P, C.POINTER(MoeLayer), U32, P, U32, P, P, P, P]),
@@ -325,6 +326,34 @@ class Pool:
         nbytes = record.numel() if hasattr(record, "numel") else record.nbytes
         self.ctx.call("hale_pool_upload_expert", self.h, layer, expert, ptr(record), nbytes,
                       int(on_dev), _stream(stream))
+
+    SOURCE_FN = C.CFUNCTYPE(I32, P, U32, U32, P, U64)
+
+    def set_source(self, fn):
+        """hale_pool_set_source (ExpertSource::load): fn(layer, expert) returns
+        the expert's pack record (bytes-like, expert_bytes long); raising (or
+        returning None) reports a failed load, which the forward surfaces as
+        HaleError E_IO. fn None removes the source."""
+        if fn is None:
+            self._source = None
+            self.ctx.call("hale_pool_set_source", self.h, None, None)
+            return
+
+        def load(_user, layer, expert, dst, nbytes):
+            try:
+                rec = fn(int(layer), int(expert))
+                if rec is None:
+                    return 1
+                mv = memoryview(rec).cast("B")
+                if len(mv) != nbytes:
+                    return 2
+                C.memmove(dst, (C.c_char * nbytes).from_buffer_copy(mv), nbytes)
+                return 0
+            except Exception:
+                return 3
+
+        self._source = self.SOURCE_FN(load)   # kept alive with the pool
+        self.ctx.call("hale_pool_set_source", self.h, C.cast(self._source, P), None)
 
     def fetch(self, keys):
         arr = (ExpertKey * len(keys))(*[ExpertKey(l, e) for l, e in keys])

@@ -135,6 +135,10 @@ struct hale_pool {
     cudaEvent_t ev_done = nullptr;         // after the last tiered forward's expert kernels
     bool done_recorded = false;
     bool timing_pending = false;
+    // ExpertSource (hale_pool_set_source): fills the host tier on first use
+    hale_expert_source_fn source = nullptr;
+    void* source_user = nullptr;
+    std::vector<uint8_t> source_buf;  // one pack record
     // TMA tensor maps over the tile layout of every expert slot (the
     // warp-specialised streaming kernels): gate/up tiles and down tiles
     bool ws_maps = false;
@@ -1058,6 +1062,8 @@ extern "C" hale_status hale_pool_upload_expert(hale_pool* p, uint32_t layer, uin
     return HALE_OK;
 }
 
+static hale_status source_fill(hale_pool* p, const int64_t* keys, size_t n, cudaStream_t st);
+
 extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys, uint64_t n, hale_expert_view* out) {
     if (!p) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_fetch: pool is NULL");
     hale_ctx* ctx = p->ctx;
@@ -1069,13 +1075,12 @@ extern "C" hale_status hale_pool_fetch(hale_pool* p, const hale_expert_key* keys
             if (keys[i].layer >= p->L || keys[i].expert >= p->E)
                 return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u out of range", keys[i].layer, keys[i].expert);
             ks[i] = (int64_t)keys[i].layer * p->E + keys[i].expert;
-            if (!p->resident[ks[i]])
-                return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u was never uploaded", keys[i].layer,
-                            keys[i].expert);
         }
         CUDA_TRY(ctx, cudaSetDevice(ctx->device));
         // the slots of the previous request may still be read by queued work
         CUDA_TRY(ctx, cudaDeviceSynchronize());
+        hale_status rs = source_fill(p, ks.data(), n, nullptr);
+        if (rs) return rs;
         tier_release(p);
         std::vector<std::pair<int32_t, int64_t>> loads;
         hale_status r = tier_request(p, ks.data(), n, loads);
@@ -1359,6 +1364,39 @@ static hale_status expert_go(hale_ctx* ctx, const ExpertArgs& a, unsigned max_ac
 static hale_status launch_experts(hale_ctx* ctx, const hale_pool* p, ExpertArgs& a, uint32_t M, int k, int E,
                                   cudaStream_t st);
 
+// ExpertSource::load (src/expert/mod.rs:110-124) for the keys of a request
+// whose experts were never uploaded: the source hands over the pack record,
+// which goes through hale_pool_upload_expert into the host tier. Runs before
+// the request touches the cache book, so a failed load leaves the pool as it
+// was; it comes back as HALE_E_IO (the reference's HaleError::Io).
+static hale_status source_fill(hale_pool* p, const int64_t* keys, size_t n, cudaStream_t st) {
+    hale_ctx* ctx = p->ctx;
+    for (size_t i = 0; i < n; i++) {
+        const int64_t key = keys[i];
+        if (p->resident[key]) continue;
+        const uint32_t layer = (uint32_t)(key / p->E), expert = (uint32_t)(key % p->E);
+        if (!p->source)
+            return fail(ctx, HALE_E_INVALID_ARGUMENT, "expert L%uE%u was never uploaded and the pool has no source",
+                        layer, expert);
+        p->source_buf.resize(p->record_bytes);
+        const int32_t rc = p->source(p->source_user, layer, expert, p->source_buf.data(), p->record_bytes);
+        if (rc != 0)
+            return fail(ctx, HALE_E_IO, "ExpertSource::load failed for L%uE%u (source returned %d)", layer, expert,
+                        rc);
+        hale_status r = hale_pool_upload_expert(p, layer, expert, p->source_buf.data(), p->record_bytes, 0, st);
+        if (r) return r;
+    }
+    return HALE_OK;
+}
+
+extern "C" hale_status hale_pool_set_source(hale_pool* p, hale_expert_source_fn fn, void* user) {
+    if (!p || !p->ctx) return fail(nullptr, HALE_E_INVALID_ARGUMENT, "hale_pool_set_source: bad pool");
+    if (!p->tiered) return fail(p->ctx, HALE_E_UNSUPPORTED, "an HBM-resident pool holds every expert; no source");
+    p->source = fn;
+    p->source_user = user;
+    return HALE_OK;
+}
+
 // A tiered pool's forward: read the routes back (the calling thread waits for
 // the router), resolve them one token at a time in top-k order, copy the
 // misses into HBM slots on the side stream and publish this layer's slot row
@@ -1377,6 +1415,16 @@ static hale_status tier_forward(hale_pool* p, uint32_t layer, const int* d_route
     CUDA_TRY(ctx, cudaMemcpyAsync(p->h_routes, d_routes, n * 4, cudaMemcpyDeviceToHost, st));
     // also completes every earlier forward's kernels, so held slots can go
     CUDA_TRY(ctx, cudaStreamSynchronize(st));
+    {
+        std::vector<int64_t> ks(n);
+        for (size_t i = 0; i < n; i++) {
+            const int e = p->h_routes[i];
+            if (e < 0 || (uint32_t)e >= p->E) return fail(ctx, HALE_E_DEVICE_CHECK, "route %d out of range", e);
+            ks[i] = (int64_t)layer * p->E + e;
+        }
+        hale_status r = source_fill(p, ks.data(), n, st);
+        if (r) return r;
+    }
     tier_release(p);
     std::vector<std::pair<int32_t, int64_t>> loads;
     std::vector<int64_t> keys(k);
@@ -1406,7 +1454,7 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     if (ly->layer >= p->L) return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u has no experts in the pool", ly->layer);
     if (ly->n_experts != p->E)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "router has %u experts, pool has %u", ly->n_experts, p->E);
-    if (p->layer_resident[ly->layer] != p->E)
+    if (p->layer_resident[ly->layer] != p->E && !(p->tiered && p->source))
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "layer %u: only %u of %u experts are resident", ly->layer,
                     p->layer_resident[ly->layer], p->E);
     if (M == 0) return HALE_OK;

@@ -232,6 +232,18 @@ typedef struct {
 HALE_API hale_status hale_pool_create_tiered(hale_ctx* ctx, hale_dtype dtype, uint32_t hidden, uint32_t inter,
                                     uint32_t n_layers, uint32_t n_experts, const hale_cache_policy* policy,
                                     hale_pool** out);
+/* ExpertSource::load (src/expert/mod.rs:110-124) for a tiered pool: when a
+ * request names an expert that was never uploaded, the pool calls
+ * fn(user, layer, expert, record, record_bytes) on the calling thread to
+ * fill `record` with that expert's pack record (gate | up | down, the bytes
+ * PackExpertSource::load returns, pack.rs:264-271) and return 0; the record
+ * then enters the host tier as hale_pool_upload_expert would put it there.
+ * A nonzero return fails the forward (or fetch) with HALE_E_IO before any
+ * cache counter or slot changes, and the next request asks the source again.
+ * fn NULL removes the source (never-uploaded experts are then an error). */
+typedef int32_t (*hale_expert_source_fn)(void* user, uint32_t layer, uint32_t expert, void* record,
+                                         uint64_t record_bytes);
+HALE_API hale_status hale_pool_set_source(hale_pool* pool, hale_expert_source_fn fn, void* user);
 /* Number of HBM expert slots of a pool (n_layers * n_experts when resident). */
 HALE_API uint64_t hale_pool_hbm_slots(const hale_pool* pool);
 

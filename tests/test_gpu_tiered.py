@@ -217,3 +217,58 @@ def test_streaming_decoder_is_bit_identical_to_resident(ctx, tmp_path, name):
     budget, b = run(expert_hbm_bytes=3 * one)
     assert b.pinned_experts == 3 and b.lru_capacity_bytes == 0
     assert (budget.view(np.uint32) == want.view(np.uint32)).all()
+
+
+def test_expert_source_fills_the_cold_tier_and_reports_io_errors(ctx):
+    """ExpertSource::load (src/expert/mod.rs:110-124) as a host callback:
+    a tiered pool with nothing uploaded asks the source for each expert the
+    first time a request names it -- the results equal the resident pool's.
+    A source that fails (like CountingSource's injected I/O error,
+    src/expert/cache.rs:211-244) makes the forward return E_IO before any
+    counter or slot changes; the pool then serves normally again."""
+    E, H, I, k = 16, 256, 128, 4
+    dtype = fmt.Q8_0
+    ld = fmt.SyntheticLayer(77, E, H, I, dtype)
+    res = hale.Pool(ctx, dtype, H, I, 1, E)
+    upload_all(res, [ld])
+    rb = res.expert_bytes
+    pool = hale.Pool(ctx, dtype, H, I, 1, E, policy=hale.CachePolicy([(0, 2)], 3 * rb))
+    records = {e: fmt.pack_record(*ld.expert_encoded(e)) for e in range(E)}
+    asked = []
+
+    def good(layer, expert):
+        asked.append((layer, expert))
+        return records[expert]
+
+    pool.set_source(good)
+    x = ld.tokens(6, seed=1)
+    want, want_idx = _forward(ctx, res, ld, 0, x, k, True)
+    got, got_idx = _forward(ctx, pool, ld, 0, x, k, True)
+    assert (got_idx == want_idx).all()
+    assert (got.view(np.uint32) == want.view(np.uint32)).all()
+    first = sorted(set(asked))
+    assert first == sorted({(0, int(e)) for e in want_idx.reshape(-1)})     # each expert asked once
+    before = pool.stats()
+    # a failing source: an expert no request has named yet
+    unseen = [e for e in range(E) if (0, e) not in set(asked)]
+    bad_expert = unseen[0]
+    pool.set_source(lambda layer, expert: None if expert == bad_expert else records[expert])
+    x2 = None
+    for seed in range(2, 400):             # tokens whose routes name the failing expert
+        cand = ld.tokens(4, seed=seed)
+        _, idx_c = _forward(ctx, res, ld, 0, cand, k, True)
+        if bad_expert in idx_c:
+            x2 = cand
+            break
+    assert x2 is not None
+    with pytest.raises(hale.HaleError) as ei:
+        _forward(ctx, pool, ld, 0, x2, k, True)
+    assert ei.value.status == hale.E_IO
+    after = pool.stats()
+    assert (after.pinned_hits, after.lru_hits, after.misses, after.lru_experts) == \
+        (before.pinned_hits, before.lru_hits, before.misses, before.lru_experts)
+    pool.set_source(good)
+    want2, _ = _forward(ctx, res, ld, 0, x2, k, True)
+    got2, _ = _forward(ctx, pool, ld, 0, x2, k, True)
+    assert (got2.view(np.uint32) == want2.view(np.uint32)).all()
+    ctx.check()
