@@ -451,6 +451,95 @@ def decode_block(hale, fmt, ctx, steps, warmup):
             "config": dict(workload="qwen3_30b_a3b_decode", **shape), "b1": b1, "b16": b16}
 
 
+def decode_ep_block(hale, fmt, ctx, world, rank, uid, barrier, max_over_ranks, layers=4, global_batch=32,
+                    prompt=256, steps=16, warmup=3):
+    """Whole-model decode across the N GPUs (BASELINE config 3's shapes:
+    Mixtral-8x7B -- hidden 4096, 32 q / 8 kv heads of 128, 8 experts top-2 of
+    intermediate 14336 in q8_0, vocab 32000, bf16 attention, embedding and
+    lm_head -- at `layers` decoder layers instead of 32). Experts are split
+    over the ranks (hale_decoder_set_comm: every MoE layer is one
+    hale_moe_forward_ep); attention is data-parallel: the global batch of
+    sequences is divided evenly and each rank decodes its own. Each sequence
+    first prefills a `prompt`-token random prompt (one step each), then a
+    step is one token of every sequence; CUDA events, max over ranks.
+    Synthetic weights: dense N(0, 0.02) from the same seed on every rank,
+    this rank's experts encoded from the seeded layer, one layer's records in
+    every layer (each its own HBM copy), norms 1.0."""
+    import torch
+    from concurrent.futures import ThreadPoolExecutor
+    Hd, nh, nkv, hd, V, Ex, kx, Ix = 4096, 32, 8, 128, 32000, 8, 2, 14336
+    epr, B = Ex // world, global_batch // world
+    rng = np.random.default_rng([SEED, 3])
+
+    def bf16(rows, cols):
+        out = np.empty((rows, cols), np.uint16)
+        for r0 in range(0, rows, 4096):
+            a = (rng.standard_normal((min(4096, rows - r0), cols), dtype=np.float32) * 0.02).view(np.uint32)
+            out[r0:r0 + 4096] = ((a + 0x7FFF + ((a >> 16) & 1)) >> 16).astype(np.uint16)
+        return (fmt.BF16, rows, cols, out.reshape(-1).view(np.uint8))
+
+    ld = fmt.SyntheticLayer(SEED + 3, Ex, Hd, Ix, fmt.Q8_0)
+    with ThreadPoolExecutor(4) as ex:
+        recs = list(ex.map(lambda e: fmt.pack_record(*ld.expert_encoded(e)), range(rank * epr, (rank + 1) * epr)))
+    pool = hale.Pool(ctx, fmt.Q8_0, Hd, Ix, layers, epr)
+    for l in range(layers):
+        for le in range(epr):
+            pool.upload(l, le, recs[le])
+    del recs
+    ones = np.ones(Hd, np.float32)
+    router = (fmt.F32, Ex, Hd, fmt.encode(fmt.F32, ld.router))
+    lys = [dict(input_norm=ones, post_norm=ones, q=bf16(nh * hd, Hd), k=bf16(nkv * hd, Hd), v=bf16(nkv * hd, Hd),
+                o=bf16(Hd, nh * hd), router=router) for _ in range(layers)]
+    dims = dict(hidden=Hd, n_layers=layers, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, n_experts=Ex,
+                top_k=kx, normalize_topk=1, eps=1e-5, rope_theta=1e6)
+    max_len = prompt + steps + warmup + 2
+    dec = hale.Decoder(ctx, dims, lys, bf16(V, Hd), bf16(V, Hd), ones, pool, max_len, n_seqs=B, max_batch=prompt)
+    comm = hale.Comm(ctx, world, rank, uid, Hd, Ex, kx, prompt)
+    stream = torch.cuda.current_stream()
+    try:
+        dec.set_comm(comm)
+        toks = np.random.default_rng([SEED, 4, rank]).integers(0, V, size=(B, max_len))
+        logits = torch.empty((B, V), dtype=torch.float32, device="cuda")
+        barrier()
+        for b in range(B):
+            dec.step(toks[b, :prompt], np.arange(prompt), np.full(prompt, b), logits=logits[:1],
+                     last_logits_only=True)
+        pos = prompt
+        seqs = np.arange(B)
+        for _ in range(warmup):
+            dec.step(toks[:, pos], np.full(B, pos), seqs, logits=logits)
+            pos += 1
+        ctx.check()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        for a, b in evs:
+            a.record(stream)
+            dec.step(toks[:, pos], np.full(B, pos), seqs, logits=logits)
+            b.record(stream)
+            pos += 1
+        torch.cuda.synchronize()
+        ctx.check()
+        ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+    finally:
+        dec.set_comm(None)
+        comm.close()
+        dec.close()
+    return {"metric": "decode_tok_s_full_model_ep", "tok_s": world * B / (ms / 1e3), "ms_per_step": ms,
+            "unit": "tok/s", "steps": steps, "warmup": warmup,
+            "config": {"workload": "mixtral_8x7b_decode_ep", "layers": layers, "layers_of_model": 32,
+                       "hidden": Hd, "heads": nh, "kv_heads": nkv, "head_dim": hd, "vocab": V, "experts": Ex,
+                       "top_k": kx, "moe_intermediate": Ix, "expert_dtype": "q8_0",
+                       "global_batch": global_batch, "sequences_per_rank": B, "positions_before_timing": prompt,
+                       "parallelism": f"ep{world} experts, data-parallel attention"},
+            "timing": "CUDA events around each rank's hale_decoder_step (one row per sequence), max over ranks"}
+
+
+def ep_decode_fits(world):
+    """Config 3's 8 experts and global batch of 32 divide over `world` ranks."""
+    return 8 % world == 0 and 32 % world == 0
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -676,6 +765,13 @@ def main():
                               "distinct_experts": s_distinct,
                               "layer_hbm_gbs": lb / (s_ms / 1e3) / 1e9}
 
+    # ---- whole-model decode across the N GPUs (config 3 shapes, reduced) -------
+    decode_ep = None
+    if world > 1 and not args.no_decode and ep_decode_fits(world):
+        uid2 = [hale.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid2, src=0)
+        decode_ep = decode_ep_block(hale, fmt, ctx, world, rank, uid2[0], barrier, max_over_ranks)
+
     # ---- the host-driven NCCL exchange (hale_ep_* halves), for comparison -----
     ep_line = None
     if world > 1 and not args.no_ep:
@@ -710,6 +806,8 @@ def main():
         }
         if decode is not None:
             line["decode"] = decode
+        if decode_ep is not None:
+            line["decode_ep"] = decode_ep
         if ep_p2p is not None:
             line["bit_exact_vs_1gpu"] = ep_p2p["bit_exact"]
             line["launches_per_call"] = ep_p2p["per_call_launches"]
