@@ -773,19 +773,33 @@ static bool pool_tensor_map(CUtensorMap* m, uint8_t* data, size_t offset, int re
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// CTAs per SM of the streaming kernels for these shapes: three where both
-// kernels' shared-memory plans fit a third of the SM, else two; 0 = the
-// shapes do not suit them.
-static int ws_ctas_per_sm(hale_dtype dt, int H, int I) {
+// CTAs per SM and activation buffers of the streaming kernels for these
+// shapes: the first configuration, in preference order, whose shared-memory
+// plans fit for both kernels with at least three weight stages in flight
+// (two for the last resort); cps 0 = the shapes do not suit them. Measured
+// on B200 at the Qwen3-30B layer shape: four CTAs per SM with one activation
+// buffer are fastest from ~2 routes per active expert on (M = 64: 71.5 vs
+// 72.9 us gate/up; M = 512: 248 vs 252 us gate/up, 176 vs 199 us down);
+// smaller batches, where a CTA sees about one unit, keep three CTAs with
+// double-buffered activations (M = 8: 45 vs 53 us gate/up).
+struct WsCfg {
+    int cps, xb;
+};
+static constexpr WsCfg kWsWide[] = {{4, 1}, {3, 2}, {3, 1}, {2, 2}, {2, 1}};
+static constexpr WsCfg kWsNarrow[] = {{3, 2}, {4, 1}, {3, 1}, {2, 2}, {2, 1}};
+
+static WsCfg ws_config(hale_dtype dt, int H, int I, bool narrow = false) {
     const int rec = 32 * block_bytes(dt);
-    for (int cps : {3, 2}) {
-        const int budget = ws_budget(cps);
-        if (ws_plan_ok(ws_plan(rec, 2, 2, kWsSB, H, budget), budget) &&
-            ws_plan_ok(ws_plan(rec, 1, 4, kWsSB, I, budget), budget))
-            return cps;
-    }
-    return 0;
+    for (int min_s : {3, 2})
+        for (const WsCfg& c : narrow ? kWsNarrow : kWsWide) {
+            const int budget = ws_budget(c.cps);
+            const WsPlan a = ws_plan(rec, 2, 2, kWsSB, H, budget, c.xb), b = ws_plan(rec, 1, 4, kWsSB, I, budget, c.xb);
+            if (ws_plan_ok(a, budget) && ws_plan_ok(b, budget) && a.S >= min_s && b.S >= min_s) return c;
+        }
+    return {0, 0};
 }
+
+static int ws_ctas_per_sm(hale_dtype dt, int H, int I) { return ws_config(dt, H, I).cps; }
 
 // Builds the pool's maps (gate/up: H/32 blocks per tile, 2 * I/32 tiles;
 // down: I/32 blocks per tile, H/32 tiles) when its shapes suit the
@@ -1317,27 +1331,41 @@ static bool use_ws(const hale_ctx* ctx, const hale_pool* p, uint32_t M, int k, i
     return ctx->expert_kernel == HALE_EXPERT_WS || M >= kWsMinTokens;
 }
 
-template <int QT, int CPS>
+template <int QT, int CPS, int NG>
 static hale_status expert_go_ws(hale_ctx* ctx, const hale_pool* p, const ExpertArgs& a, unsigned max_active,
-                                unsigned* ctr, cudaStream_t st) {
-    const int TI = a.I / 32, TH = a.H / 32, rec = 32 * QFmt<QT>::BB, budget = ws_budget(CPS);
-    const WsPlan P1 = ws_plan(rec, 2, 2, kWsSB, a.H, budget), P2 = ws_plan(rec, 1, 4, kWsSB, a.I, budget);
-    CUDA_TRY(ctx, allow_smem(expert_gate_up_ws_kernel<QT, CPS>, (size_t)P1.total));
-    CUDA_TRY(ctx, allow_smem(expert_down_ws_kernel<QT, CPS>, (size_t)P2.total));
+                                unsigned* ctr, int xb, cudaStream_t st) {
+    const int TI = a.I / 32, TH = a.H / 32, rec = 32 * QFmt<QT>::BB, budget = ws_budget(CPS), rows = kPassRows * NG;
+    const WsPlan P1 = ws_plan(rec, 2, 2, kWsSB, a.H, budget, xb, rows);
+    const WsPlan P2 = ws_plan(rec, 1, 4, kWsSB, a.I, budget, xb, rows);
+    CUDA_TRY(ctx, allow_smem(expert_gate_up_ws_kernel<QT, CPS, NG>, (size_t)P1.total));
+    CUDA_TRY(ctx, allow_smem(expert_down_ws_kernel<QT, CPS, NG>, (size_t)P2.total));
     const unsigned slots = (unsigned)(ctx->sm_count * CPS);
     const unsigned g1 = std::min(max_active * (unsigned)(TI / 2), slots);
     const unsigned g2 = std::min(max_active * (unsigned)(TH / 4), slots);
     {
         ProfScope ps_(ctx, "expert_gate_up", st);
-        expert_gate_up_ws_kernel<QT, CPS><<<g1, kWsThreads, P1.total, st>>>(p->map_gu, a, P1, ctr);
+        expert_gate_up_ws_kernel<QT, CPS, NG><<<g1, kWsThreads, P1.total, st>>>(p->map_gu, a, P1, ctr);
     }
     hale_status r = check_launch(ctx, "expert_gate_up_ws");
     if (r) return r;
     {
         ProfScope ps_(ctx, "expert_down", st);
-        expert_down_ws_kernel<QT, CPS><<<g2, kWsThreads, P2.total, st>>>(p->map_d, a, P2, ctr + 2);
+        expert_down_ws_kernel<QT, CPS, NG><<<g2, kWsThreads, P2.total, st>>>(p->map_d, a, P2, ctr + 2);
     }
     return check_launch(ctx, "expert_down_ws");
+}
+
+template <int QT>
+static hale_status expert_go_ws_cfg(hale_ctx* ctx, const hale_pool* p, const ExpertArgs& a, unsigned max_active,
+                                    uint32_t M, int k, int E, cudaStream_t st) {
+    // routes per active expert the batch can have on average
+    const long long routes = (long long)M * k, experts = std::min<long long>(E, routes);
+    const bool narrow = experts > 0 && routes < 2 * experts;
+    const WsCfg c = ws_config(p->dtype, a.H, a.I, narrow);
+    unsigned* ctr = a.ws_cnt;
+    if (c.cps == 4) return expert_go_ws<QT, 4, 1>(ctx, p, a, max_active, ctr, c.xb, st);
+    if (c.cps == 3) return expert_go_ws<QT, 3, 1>(ctx, p, a, max_active, ctr, c.xb, st);
+    return expert_go_ws<QT, 2, 1>(ctx, p, a, max_active, ctr, c.xb, st);
 }
 
 template <int QT, int RT>
@@ -1521,14 +1549,9 @@ static hale_status launch_experts(hale_ctx* ctx, const hale_pool* p, ExpertArgs&
     a.S1 = std::min(depth, (H / 32 + kStageBlocks - 1) / kStageBlocks);
     a.S2 = std::min(depth, (I / 32 + kStageBlocks - 1) / kStageBlocks);
     unsigned max_active = (unsigned)std::min<long long>(E, (long long)M * k);
-    if (use_ws(ctx, p, M, k, E)) {
-        const int cps = ws_ctas_per_sm(dt, H, I);
-        if (dt == HALE_Q4_0)
-            return cps == 3 ? expert_go_ws<0, 3>(ctx, p, a, max_active, a.ws_cnt, st)
-                            : expert_go_ws<0, 2>(ctx, p, a, max_active, a.ws_cnt, st);
-        return cps == 3 ? expert_go_ws<1, 3>(ctx, p, a, max_active, a.ws_cnt, st)
-                        : expert_go_ws<1, 2>(ctx, p, a, max_active, a.ws_cnt, st);
-    }
+    if (use_ws(ctx, p, M, k, E))
+        return dt == HALE_Q4_0 ? expert_go_ws_cfg<0>(ctx, p, a, max_active, M, k, E, st)
+                               : expert_go_ws_cfg<1>(ctx, p, a, max_active, M, k, E, st);
     if (use_tc(ctx, dt, M, H, I)) {
         // 16-token passes once experts average ~16 tokens; 8-token passes below
         const bool wide = (long long)M * k >= 16LL * E;

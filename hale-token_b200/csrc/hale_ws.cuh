@@ -44,32 +44,39 @@ constexpr int kWsSB = 4;  // blocks per tile per ring stage
 
 // Dynamic shared memory per CTA with `cps` CTAs per SM (228 KB per SM, less
 // the per-CTA reserve and the kernels' static arrays).
-__host__ __device__ inline int ws_budget(int cps) { return cps >= 3 ? 72 * 1024 : 110 * 1024; }
+__host__ __device__ inline int ws_budget(int cps) {
+    return cps >= 4 ? 55 * 1024 : cps == 3 ? 72 * 1024 : 110 * 1024;
+}
 
 // Shared-memory plan. boxes: TMA loads per stage (2 for gate/up, 1 for
 // down); tiles: 32-row tiles per box; SB: blocks per tile per stage; cols:
-// activation width.
+// activation width; XB: activation buffers (2: the next pass loads while the
+// current one is read; 1: it loads once the consumers release the buffer,
+// after the producer has already put the next pass's first weight stages in
+// flight -- less shared memory, so more CTAs fit per SM).
 struct WsPlan {
-    int SB, S, box_bytes, stage_bytes, xstride, astride, xq_bytes, xa_bytes;
+    int SB, S, XB, box_bytes, stage_bytes, xstride, astride, xq_bytes, xa_bytes;
     int ring_off, xq_off, xa_off, bar_off, ctl_off, total;
 };
 
-__host__ __device__ inline WsPlan ws_plan(int REC, int boxes, int tiles, int SB, int cols, int budget) {
+__host__ __device__ inline WsPlan ws_plan(int REC, int boxes, int tiles, int SB, int cols, int budget, int XB = 2,
+                                          int rows = kPassRows) {
     WsPlan p;
     p.SB = SB;
+    p.XB = XB;
     p.box_bytes = tiles * SB * REC;
     p.stage_bytes = boxes * p.box_bytes;
     p.xstride = xstage_stride(cols);
     p.astride = xaux_stride(aux_stride(cols / kQK));
-    p.xq_bytes = (kPassRows * p.xstride + 127) & ~127;
-    p.xa_bytes = (kPassRows * p.astride * 8 + 127) & ~127;
-    const int fixed = 2 * p.xq_bytes + 2 * p.xa_bytes + (2 * kWsMaxStages + 4) * 8 + 64;
+    p.xq_bytes = (rows * p.xstride + 127) & ~127;
+    p.xa_bytes = (rows * p.astride * 8 + 127) & ~127;
+    const int fixed = XB * p.xq_bytes + XB * p.xa_bytes + (2 * kWsMaxStages + 4) * 8 + 64;
     p.S = (budget - fixed) / p.stage_bytes;
     if (p.S > kWsMaxStages) p.S = kWsMaxStages;
     p.ring_off = 0;
     p.xq_off = p.S * p.stage_bytes;
-    p.xa_off = p.xq_off + 2 * p.xq_bytes;
-    p.bar_off = p.xa_off + 2 * p.xa_bytes;
+    p.xa_off = p.xq_off + XB * p.xq_bytes;
+    p.bar_off = p.xa_off + XB * p.xa_bytes;
     p.ctl_off = p.bar_off + (2 * kWsMaxStages + 4) * 8;
     p.total = p.ctl_off + 64;  // WsCtl
     return p;
@@ -141,8 +148,8 @@ struct WsCtl {
 
 struct WsCtx {
     uint8_t* ring;
-    uint8_t* xq;  // [2][xq_bytes]
-    uint8_t* xa;  // [2][xa_bytes]
+    uint8_t* xq;  // [XB][xq_bytes]
+    uint8_t* xa;  // [XB][xa_bytes]
     uint64_t *full, *empty, *xfull, *xempty;
     volatile WsCtl* ctl;
     WsPlan P;
@@ -186,13 +193,15 @@ __device__ __forceinline__ bool ws_wait(WsCtx& c, uint64_t* bar, uint32_t parity
 }
 
 // After an abort, waits (bounded) for the copies still landing: the last S
-// weight stages and the last two activation passes issued. All threads.
+// weight stages and the last XB activation passes issued. All threads.
 __device__ __forceinline__ void ws_teardown(WsCtx& c) {
     __syncthreads();
     if (c.ctl->abort && threadIdx.x == 0) {
         const int S = c.P.S, gs1 = c.ctl->stages, q1 = c.ctl->passes;
         for (int gs = max(0, gs1 - S); gs < gs1; gs++) mbar_wait(&c.full[gs % S], (gs / S) & 1, nullptr, 400000000LL);
-        for (int q = max(0, q1 - 2); q < q1; q++) mbar_wait(&c.xfull[q & 1], (q >> 1) & 1, nullptr, 400000000LL);
+        const int XB = c.P.XB;
+        for (int q = max(0, q1 - XB); q < q1; q++)
+            mbar_wait(&c.xfull[q % XB], (q / XB) & 1, nullptr, 400000000LL);
     }
     __syncthreads();
 }
@@ -211,13 +220,14 @@ __device__ __forceinline__ int ws_slot(const ExpertArgs& a, int e) {
 // current unit's stages are issued, so the producer does not wait on global
 // memory between units: step 0 claims a unit (atomic), 1 reads its expert,
 // 2 its route range and slot, 3 the rows of its first pass; 4 = ready.
+template <int PR>
 struct WsNext {
     int u, ai, e, beg, end, cs, step;
-    int rows[kPassRows];
+    int rows[PR];
 };
 
-template <class RowOf>
-__device__ __forceinline__ void ws_next_step(WsNext& nx, const ExpertArgs& a, unsigned* ctr, int n_units, int upe,
+template <int PR, class RowOf>
+__device__ __forceinline__ void ws_next_step(WsNext<PR>& nx, const ExpertArgs& a, unsigned* ctr, int n_units, int upe,
                                              int tpu, RowOf row_of) {
     if (nx.step == 0) {
         nx.u = (int)atomicAdd(ctr, 1u);
@@ -234,7 +244,7 @@ __device__ __forceinline__ void ws_next_step(WsNext& nx, const ExpertArgs& a, un
     } else if (nx.step == 3) {
         WsUnit U{nx.e, nx.beg, nx.end - nx.beg, nx.cs, tpu * (nx.u - nx.ai * upe)};
 #pragma unroll
-        for (int j = 0; j < kPassRows; j++)
+        for (int j = 0; j < PR; j++)
             if (j < U.T) nx.rows[j] = row_of(U, j);
         nx.step = 4;
     }
@@ -244,30 +254,49 @@ __device__ __forceinline__ void ws_next_step(WsNext& nx, const ExpertArgs& a, un
 // per unit and pass, the pass descriptor and activation rows (row_of(U, j)
 // of gq / ga, `cols` columns), then the unit's weight stages -- per stage
 // `boxes` TMA loads at tile coordinates tile_of(U, box). Ends with a
-// descriptor of n = -1. tpu: 32-row tiles per unit.
-template <class RowOf, class TileOf>
+// descriptor of n = -1. tpu: 32-row tiles per unit; PR: tokens per pass.
+template <int PR, class RowOf, class TileOf>
 __device__ void ws_produce(WsCtx& c, const ExpertArgs& a, const CUtensorMap* map, int n_units, int upe, int tpu,
                            unsigned* ctr, int nb, int boxes, int cols, const int8_t* __restrict__ gq,
                            const int2* __restrict__ ga, int nbp, RowOf row_of, TileOf tile_of, uint32_t* err) {
     const WsPlan& P = c.P;
     const int nst = (nb + P.SB - 1) / P.SB;
     int gs = 0, q = 0;
-    WsNext nx{};
+    WsNext<PR> nx{};
     while (nx.step < 4) ws_next_step(nx, a, ctr, n_units, upe, tpu, row_of);
     while (nx.u < n_units) {
         const WsUnit U{nx.e, nx.beg, nx.end - nx.beg, nx.cs, tpu * (nx.u - nx.ai * upe)};
-        int rows[kPassRows];
+        int rows[PR];
 #pragma unroll
-        for (int j = 0; j < kPassRows; j++) rows[j] = nx.rows[j];
+        for (int j = 0; j < PR; j++) rows[j] = nx.rows[j];
         nx.step = 0;
-        for (int base = 0; base < U.T; base += kPassRows, q++) {
-            const int n = min(kPassRows, U.T - base), xb = q & 1;
+        for (int base = 0; base < U.T; base += PR, q++) {
+            const int n = min(PR, U.T - base), xb = q % P.XB;
             if (base > 0) {
 #pragma unroll
-                for (int j = 0; j < kPassRows; j++)
+                for (int j = 0; j < PR; j++)
                     if (j < n) rows[j] = row_of(U, base + j);
             }
-            if (!ws_wait(c, &c.xempty[xb], ((q >> 1) & 1) ^ 1, err)) return;
+            auto stage = [&](int s) {
+                const int slot = gs % P.S;
+                if (!ws_wait(c, &c.empty[slot], ((gs / P.S) & 1) ^ 1, err)) return false;
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&c.full[slot], (uint32_t)P.stage_bytes);
+                for (int bx = 0; bx < boxes; bx++)
+                    tma_load_4d(c.ring + (size_t)slot * P.stage_bytes + (size_t)bx * P.box_bytes, map, s * P.SB,
+                                tile_of(U, bx), U.cs, &c.full[slot]);
+                c.ctl->stages = ++gs;
+                ws_next_step(nx, a, ctr, n_units, upe, tpu, row_of);  // the next unit, a step per stage
+                return true;
+            };
+            // one activation buffer: the pass's first weight stages go out
+            // before the wait for the buffer (their slots free up as the
+            // previous pass's stages are consumed, which needs no activations)
+            int s = 0;
+            if (P.XB == 1)
+                for (; s < min(P.S, nst); s++)
+                    if (!stage(s)) return;
+            if (!ws_wait(c, &c.xempty[xb], ((q / P.XB) & 1) ^ 1, err)) return;
             c.ctl->pass_beg[xb] = U.beg;
             c.ctl->pass_base[xb] = base;
             c.ctl->pass_n[xb] = n;
@@ -277,7 +306,7 @@ __device__ void ws_produce(WsCtx& c, const ExpertArgs& a, const CUtensorMap* map
             int8_t* xq = reinterpret_cast<int8_t*>(c.xq + (size_t)xb * P.xq_bytes);
             int2* xa = reinterpret_cast<int2*>(c.xa + (size_t)xb * P.xa_bytes);
 #pragma unroll
-            for (int j = 0; j < kPassRows; j++) {
+            for (int j = 0; j < PR; j++) {
                 if (j < n) {
                     bulk_g2s(xq + (size_t)j * P.xstride, gq + (size_t)rows[j] * cols, (uint32_t)cols, &c.xfull[xb]);
                     bulk_g2s(xa + (size_t)j * P.astride, ga + (size_t)rows[j] * nbp, (uint32_t)(nbp * 8),
@@ -285,22 +314,13 @@ __device__ void ws_produce(WsCtx& c, const ExpertArgs& a, const CUtensorMap* map
                 }
             }
             c.ctl->passes = q + 1;
-            for (int s = 0; s < nst; s++, gs++) {
-                const int slot = gs % P.S;
-                if (!ws_wait(c, &c.empty[slot], ((gs / P.S) & 1) ^ 1, err)) return;
-                fence_proxy_async_smem();
-                mbar_arrive_expect_tx(&c.full[slot], (uint32_t)P.stage_bytes);
-                for (int bx = 0; bx < boxes; bx++)
-                    tma_load_4d(c.ring + (size_t)slot * P.stage_bytes + (size_t)bx * P.box_bytes, map, s * P.SB,
-                                tile_of(U, bx), U.cs, &c.full[slot]);
-                c.ctl->stages = gs + 1;
-                ws_next_step(nx, a, ctr, n_units, upe, tpu, row_of);  // the next unit, a step per stage
-            }
+            for (; s < nst; s++)
+                if (!stage(s)) return;
         }
         while (nx.step < 4) ws_next_step(nx, a, ctr, n_units, upe, tpu, row_of);
     }
-    const int xb = q & 1;
-    if (!ws_wait(c, &c.xempty[xb], ((q >> 1) & 1) ^ 1, err)) return;
+    const int xb = q % P.XB;
+    if (!ws_wait(c, &c.xempty[xb], ((q / P.XB) & 1) ^ 1, err)) return;
     c.ctl->pass_n[xb] = -1;
     mbar_arrive(&c.xfull[xb]);
 }
@@ -313,8 +333,8 @@ struct WsPass {
 // Consumers: waits for pass q's descriptor and activations; false (for all
 // consumer warps alike) when there is no more work or a wait timed out.
 __device__ __forceinline__ bool ws_next_pass(WsCtx& c, int q, uint32_t* err, WsPass& d) {
-    const int xb = q & 1;
-    bool ok = __all_sync(0xffffffffu, ws_wait(c, &c.xfull[xb], (q >> 1) & 1, err));
+    const int xb = q % c.P.XB;
+    bool ok = __all_sync(0xffffffffu, ws_wait(c, &c.xfull[xb], (q / c.P.XB) & 1, err));
     if (ok) {
         d.beg = c.ctl->pass_beg[xb];
         d.base = c.ctl->pass_base[xb];
@@ -407,13 +427,20 @@ __device__ __forceinline__ void ws_epilogue(float (&acc)[2][2], const int (&d)[4
 // ---------------------------------------------------------------------------
 // gate/up
 // ---------------------------------------------------------------------------
-// ctr: two counters (units claimed, CTAs retired), zero at launch.
-template <int QT, int CPS>
+// ctr: two counters (units claimed, CTAs retired), zero at launch. NG token
+// groups of 8 per pass: the A fragments and weight scales of a block are
+// loaded once and feed NG pairs of MMAs. The library builds NG = 1: wider
+// passes stream each weight tile once for more tokens but need the shared
+// memory of more CTAs per SM, and measured slower on B200 (Qwen3-30B layer,
+// 512 tokens: 306 us gate/up at NG = 4 with two CTAs per SM, 253 us at
+// NG = 2 with three, 248 us at NG = 1 with four).
+template <int QT, int CPS, int NG>
 __global__ void __launch_bounds__(kWsThreads, CPS)
     expert_gate_up_ws_kernel(const __grid_constant__ CUtensorMap map, ExpertArgs a, WsPlan P, unsigned* ctr) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float s_amax[2][2][kPassRows];  // [tile][half][token]
-    __shared__ int s_qsum[2][2][kPassRows];
+    constexpr int PR = kPassRows * NG;
+    __shared__ float s_amax[2][2][PR];  // [tile][half][token]
+    __shared__ int s_qsum[2][2][PR];
     constexpr int QB = QFmt<QT>::QB, REC = kTileRows * QFmt<QT>::BB, SB = kWsSB;
     constexpr unsigned FULL = 0xffffffffu;
     const int TI = a.I / kTileRows, nbh = a.H / kQK, nbph = aux_stride(nbh), nbpi = aux_stride(a.I / kQK);
@@ -426,7 +453,7 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
     if (warp == kWsConsumers) {
         if (lane == 0) {
             tma_prefetch_desc(&map);
-            ws_produce(
+            ws_produce<PR>(
                 c, a, &map, n_units, upe, 2, ctr, nbh, 2, a.H, a.xq, a.xaux, nbph,
                 [&](const WsUnit& U, int j) { return __ldcg(a.elist + U.beg + j) / k; },
                 [&](const WsUnit& U, int bx) { return bx * TI + U.tile0; }, a.err);
@@ -439,14 +466,18 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
         int gs = 0;
         WsPass d;
         for (int q = 0; ws_next_pass(c, q, a.err, d); q++) {
-            const int base = d.base, n = d.n, xb = q & 1;
+            const int base = d.base, n = d.n, xb = q % P.XB;
             // B fragment rows: token (lane & 7), K half (lane >> 3) & 1
             const int8_t* xrow = reinterpret_cast<const int8_t*>(c.xq + (size_t)xb * P.xq_bytes) +
                                  (lane & 7) * P.xstride + ((lane >> 3) & 1) * 16;
             const int2* xa = reinterpret_cast<const int2*>(c.xa + (size_t)xb * P.xa_bytes);
             const int2* a0row = xa + (2 * t) * P.astride;
             const int2* a1row = xa + (2 * t + 1) * P.astride;
-            float ag[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}}, au[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+            float ag[NG][2][2], au[NG][2][2];
+#pragma unroll
+            for (int gi = 0; gi < NG; gi++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) (&ag[gi][0][0])[i] = (&au[gi][0][0])[i] = 0.0f;
             for (int s = 0; s < nst; s++, gs++) {
                 const int slot = gs % P.S;
                 live = live && __all_sync(FULL, ws_wait(c, &c.full[slot], (gs / P.S) & 1, a.err));
@@ -458,19 +489,25 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
                         const int b = s * SB + bi;
                         const uint8_t* rg = gst + bi * REC;
                         const uint8_t* ru = ust + bi * REC;
-                        uint32_t bf[2];
-                        ldsm_x2(bf, xrow + b * kQK);
-                        const int2 x0 = a0row[b], x1 = a1row[b];
-                        const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
                         uint32_t fg[4], fu[4];
                         ws_a16<QT>(fg, rg, half, lane);
                         ws_a16<QT>(fu, ru, half, lane);
-                        int dg[4], du[4];
-                        mma_s8_16832(dg, fg, bf[0], bf[1], c0, c1);
-                        mma_s8_16832(du, fu, bf[0], bf[1], c0, c1);
-                        const uint64_t xs01 = f2_pack(__int_as_float(x0.x), __int_as_float(x1.x));
-                        ws_epilogue(ag, dg, ws_scale(rg, QB, r0), ws_scale(rg, QB, r1), xs01);
-                        ws_epilogue(au, du, ws_scale(ru, QB, r0), ws_scale(ru, QB, r1), xs01);
+                        const float wg0 = ws_scale(rg, QB, r0), wg1 = ws_scale(rg, QB, r1);
+                        const float wu0 = ws_scale(ru, QB, r0), wu1 = ws_scale(ru, QB, r1);
+#pragma unroll
+                        for (int gi = 0; gi < NG; gi++) {
+                            uint32_t bf[2];
+                            ldsm_x2(bf, xrow + gi * kPassRows * P.xstride + b * kQK);
+                            const int2 x0 = a0row[gi * kPassRows * P.astride + b];
+                            const int2 x1 = a1row[gi * kPassRows * P.astride + b];
+                            const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
+                            int dg[4], du[4];
+                            mma_s8_16832(dg, fg, bf[0], bf[1], c0, c1);
+                            mma_s8_16832(du, fu, bf[0], bf[1], c0, c1);
+                            const uint64_t xs01 = f2_pack(__int_as_float(x0.x), __int_as_float(x1.x));
+                            ws_epilogue(ag[gi], dg, wg0, wg1, xs01);
+                            ws_epilogue(au[gi], du, wu0, wu1, xs01);
+                        }
                     };
                     if (nblk == SB) {
 #pragma unroll
@@ -486,55 +523,57 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
             if (lane == 0 && live) mbar_arrive(&c.xempty[xb]);
             // h = silu(g) * u (expert/mod.rs:100-102) and its q8 quantization
             // per token over the tile's 32 rows (quant.rs:77-93)
-            float h[2][2], m[2];
-            int qv[2][2], qs[2];
+            float h[NG][2][2], scale[NG][2];
+            int qv[NG][2][2], qs[NG][2];
 #pragma unroll
-            for (int i = 0; i < 2; i++)
+            for (int gi = 0; gi < NG; gi++) {
 #pragma unroll
-                for (int j = 0; j < 2; j++) h[i][j] = fmul(silu(ag[i][j]), au[i][j]);
+                for (int i = 0; i < 2; i++)
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                m[j] = fmaxf(fmaxf(0.0f, fabsf(h[0][j])), fabsf(h[1][j]));
+                    for (int j = 0; j < 2; j++) h[gi][i][j] = fmul(silu(ag[gi][i][j]), au[gi][i][j]);
 #pragma unroll
-                for (int o = 4; o < 32; o <<= 1) m[j] = fmaxf(m[j], __shfl_xor_sync(FULL, m[j], o));
-            }
-            if (g == 0) {
-                s_amax[tw][half][2 * t] = m[0];
-                s_amax[tw][half][2 * t + 1] = m[1];
+                for (int j = 0; j < 2; j++) {
+                    float m = fmaxf(fmaxf(0.0f, fabsf(h[gi][0][j])), fabsf(h[gi][1][j]));
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
+                    scale[gi][j] = m;  // this warp's 16-row amax, for now
+                    if (g == 0) s_amax[tw][half][gi * kPassRows + 2 * t + j] = m;
+                }
             }
             ws_sync_pair(tw);
-            float scale[2];
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const float amax = fmaxf(m[j], s_amax[tw][half ^ 1][2 * t + j]);
-                scale[j] = fdiv(amax, 127.0f);
-                const float inv = scale[j] > 0.0f ? fdiv(1.0f, scale[j]) : 0.0f;
-                qv[0][j] = sat_i8(roundf(fmul(h[0][j], inv)));
-                qv[1][j] = sat_i8(roundf(fmul(h[1][j], inv)));
-                qs[j] = qv[0][j] + qv[1][j];
+            for (int gi = 0; gi < NG; gi++)
 #pragma unroll
-                for (int o = 4; o < 32; o <<= 1) qs[j] += __shfl_xor_sync(FULL, qs[j], o);
-            }
-            if (g == 0) {
-                s_qsum[tw][half][2 * t] = qs[0];
-                s_qsum[tw][half][2 * t + 1] = qs[1];
-            }
+                for (int j = 0; j < 2; j++) {
+                    const float amax = fmaxf(scale[gi][j], s_amax[tw][half ^ 1][gi * kPassRows + 2 * t + j]);
+                    scale[gi][j] = fdiv(amax, 127.0f);
+                    const float inv = scale[gi][j] > 0.0f ? fdiv(1.0f, scale[gi][j]) : 0.0f;
+                    qv[gi][0][j] = sat_i8(roundf(fmul(h[gi][0][j], inv)));
+                    qv[gi][1][j] = sat_i8(roundf(fmul(h[gi][1][j], inv)));
+                    int sq = qv[gi][0][j] + qv[gi][1][j];
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) sq += __shfl_xor_sync(FULL, sq, o);
+                    qs[gi][j] = sq;
+                    if (g == 0) s_qsum[tw][half][gi * kPassRows + 2 * t + j] = sq;
+                }
             ws_sync_pair(tw);
             if (live) {
                 const int itile = d.tile0 + tw;
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    const int tok = 2 * t + j;
-                    if (tok < n) {
-                        const size_t slot = (size_t)d.beg + base + tok;
-                        int8_t* hrow = a.hq + slot * a.I + itile * kTileRows;
-                        hrow[r0] = (int8_t)qv[0][j];
-                        hrow[r1] = (int8_t)qv[1][j];
-                        if (g == 0 && half == 0)
-                            a.haux[slot * nbpi + itile] =
-                                make_int2(__float_as_int(scale[j]), -8 * (qs[j] + s_qsum[tw][1][tok]));
+                for (int gi = 0; gi < NG; gi++)
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int tok = gi * kPassRows + 2 * t + j;
+                        if (tok < n) {
+                            const size_t slot = (size_t)d.beg + base + tok;
+                            int8_t* hrow = a.hq + slot * a.I + itile * kTileRows;
+                            hrow[r0] = (int8_t)qv[gi][0][j];
+                            hrow[r1] = (int8_t)qv[gi][1][j];
+                            if (g == 0 && half == 0)
+                                a.haux[slot * nbpi + itile] =
+                                    make_int2(__float_as_int(scale[gi][j]), -8 * (qs[gi][j] + s_qsum[tw][1][tok]));
+                        }
                     }
-                }
             }
         }
     }
@@ -545,11 +584,12 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
 // ---------------------------------------------------------------------------
 // down + best-first combine
 // ---------------------------------------------------------------------------
-template <int QT, int CPS>
+template <int QT, int CPS, int NG>
 __global__ void __launch_bounds__(kWsThreads, CPS)
     expert_down_ws_kernel(const __grid_constant__ CUtensorMap map, ExpertArgs a, WsPlan P, unsigned* ctr) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_last[2][kPassRows];
+    constexpr int PR = kPassRows * NG;
+    __shared__ int s_last[2][PR];
     constexpr int QB = QFmt<QT>::QB, REC = kTileRows * QFmt<QT>::BB, SB = kWsSB;
     constexpr unsigned FULL = 0xffffffffu;
     const int TH = a.H / kTileRows, nbi = a.I / kQK, nbpi = aux_stride(nbi);
@@ -562,7 +602,7 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
     if (warp == kWsConsumers) {
         if (lane == 0) {
             tma_prefetch_desc(&map);
-            ws_produce(
+            ws_produce<PR>(
                 c, a, &map, n_units, upe, 4, ctr, nbi, 1, a.I, a.hq, a.haux, nbpi,
                 [&](const WsUnit& U, int j) { return U.beg + j; }, [&](const WsUnit& U, int) { return U.tile0; },
                 a.err);
@@ -574,20 +614,28 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
         int gs = 0;
         WsPass d;
         for (int q = 0; ws_next_pass(c, q, a.err, d); q++) {
-            const int base = d.base, n = d.n, xb = q & 1;
+            const int base = d.base, n = d.n, xb = q % P.XB;
             const int grp = d.tile0 / 4;
             const int* routes = a.elist + d.beg + base;
-            // route ids of this lane's y rows (tokens 2t, 2t+1) and of the
+            // route ids of this lane's y rows (tokens gi*8 + 2t + j) and of the
             // combine thread's token, loaded ahead of the stage loop
-            const int rt0 = 2 * t < n ? __ldcg(routes + 2 * t) : 0;
-            const int rt1 = 2 * t + 1 < n ? __ldcg(routes + 2 * t + 1) : 0;
+            int rt[NG][2];
+#pragma unroll
+            for (int gi = 0; gi < NG; gi++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int tok = gi * kPassRows + 2 * t + j;
+                    rt[gi][j] = tok < n ? __ldcg(routes + tok) : 0;
+                }
             const int rct = ct < n ? __ldcg(routes + ct) : 0;
             const int8_t* xrow = reinterpret_cast<const int8_t*>(c.xq + (size_t)xb * P.xq_bytes) +
                                  (lane & 7) * P.xstride + ((lane >> 3) & 1) * 16;
             const int2* xa = reinterpret_cast<const int2*>(c.xa + (size_t)xb * P.xa_bytes);
             const int2* a0row = xa + (2 * t) * P.astride;
             const int2* a1row = xa + (2 * t + 1) * P.astride;
-            float acc[2][2][2] = {};  // [16-row half][row g / g+8][token 2t / 2t+1]
+            float acc[NG][2][2][2];  // [group][16-row half][row g / g+8][token 2t / 2t+1]
+#pragma unroll
+            for (int i = 0; i < NG * 8; i++) (&acc[0][0][0][0])[i] = 0.0f;
             for (int s = 0; s < nst; s++, gs++) {
                 const int slot = gs % P.S;
                 live = live && __all_sync(FULL, ws_wait(c, &c.full[slot], (gs / P.S) & 1, a.err));
@@ -597,11 +645,6 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
                     auto block = [&](int bi) {
                         const int b = s * SB + bi;
                         const uint8_t* rec = st + bi * REC;
-                        uint32_t bf[2];
-                        ldsm_x2(bf, xrow + b * kQK);
-                        const int2 x0 = a0row[b], x1 = a1row[b];
-                        const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
-                        const uint64_t xs01 = f2_pack(__int_as_float(x0.x), __int_as_float(x1.x));
                         uint32_t fr[2][4];
                         if (QT == 0) {
                             // words t of rows g, g+8, g+16, g+24
@@ -618,12 +661,26 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
                             ws_a16<QT>(fr[0], rec, 0, lane);
                             ws_a16<QT>(fr[1], rec, 1, lane);
                         }
+                        float wsc[2][2];
 #pragma unroll
                         for (int mt = 0; mt < 2; mt++) {
-                            int dd[4];
-                            mma_s8_16832(dd, fr[mt], bf[0], bf[1], c0, c1);
-                            ws_epilogue(acc[mt], dd, ws_scale(rec, QB, mt * 16 + g), ws_scale(rec, QB, mt * 16 + 8 + g),
-                                        xs01);
+                            wsc[mt][0] = ws_scale(rec, QB, mt * 16 + g);
+                            wsc[mt][1] = ws_scale(rec, QB, mt * 16 + 8 + g);
+                        }
+#pragma unroll
+                        for (int gi = 0; gi < NG; gi++) {
+                            uint32_t bf[2];
+                            ldsm_x2(bf, xrow + gi * kPassRows * P.xstride + b * kQK);
+                            const int2 x0 = a0row[gi * kPassRows * P.astride + b];
+                            const int2 x1 = a1row[gi * kPassRows * P.astride + b];
+                            const int c0 = ((QT == 0) ? x0.y : 0) + kMagicI, c1 = ((QT == 0) ? x1.y : 0) + kMagicI;
+                            const uint64_t xs01 = f2_pack(__int_as_float(x0.x), __int_as_float(x1.x));
+#pragma unroll
+                            for (int mt = 0; mt < 2; mt++) {
+                                int dd[4];
+                                mma_s8_16832(dd, fr[mt], bf[0], bf[1], c0, c1);
+                                ws_epilogue(acc[gi][mt], dd, wsc[mt][0], wsc[mt][1], xs01);
+                            }
                         }
                     };
                     if (nblk == SB) {
@@ -640,17 +697,19 @@ __global__ void __launch_bounds__(kWsThreads, CPS)
             if (lane == 0 && live) mbar_arrive(&c.xempty[xb]);
             if (live) {
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    const int tok = 2 * t + j;
-                    if (tok < n) {
-                        float* yrow = a.ybuf + (size_t)(j ? rt1 : rt0) * a.H + (d.tile0 + warp) * kTileRows;
+                for (int gi = 0; gi < NG; gi++)
 #pragma unroll
-                        for (int mt = 0; mt < 2; mt++) {
-                            yrow[mt * 16 + g] = acc[mt][0][j];
-                            yrow[mt * 16 + 8 + g] = acc[mt][1][j];
+                    for (int j = 0; j < 2; j++) {
+                        const int tok = gi * kPassRows + 2 * t + j;
+                        if (tok < n) {
+                            float* yrow = a.ybuf + (size_t)rt[gi][j] * a.H + (d.tile0 + warp) * kTileRows;
+#pragma unroll
+                            for (int mt = 0; mt < 2; mt++) {
+                                yrow[mt * 16 + g] = acc[gi][mt][0][j];
+                                yrow[mt * 16 + 8 + g] = acc[gi][mt][1][j];
+                            }
                         }
                     }
-                }
             }
             ws_sync_consumers();  // every y row of the pass is written
             // the last of a token's k routes to land for this 128-row group
