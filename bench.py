@@ -34,6 +34,11 @@ import numpy as np  # noqa: E402
 SEED = 2026
 E, H, I, K_TOP = 128, 2048, 768, 8
 WORKLOAD = "moe_layer_qwen3_30b_a3b_q4_0"
+# DRAM bytes (read + write) of one expert_gate_up_ws_kernel<q4_0, 4, 1> launch on this
+# bench's seeded 64-token step (126 distinct experts), from one ncu --set full capture:
+# dram__bytes_read.sum 224.354 MB + dram__bytes_write.sum 4.644 MB. Reported only for
+# that token count.
+NCU_GATE_UP_TRAFFIC = {64: 224354048 + 4643840}
 
 
 def parse():
@@ -723,7 +728,10 @@ def main():
     layer_bytes = distinct * fmt.row_bytes(fmt.Q4_0, H) * 2 * I + distinct * H * fmt.row_bytes(fmt.Q4_0, I)
     layer_bytes += E * H * 4 + 2 * m * H * 4
     roofline = {"bound": "hbm", "kernel": "expert_gate_up", "achieved": achieved, "peak": peak_gbs,
-                "unit": "GB/s", "frac": (achieved / peak_gbs) if achieved else None, "traffic": None,
+                "unit": "GB/s", "frac": (achieved / peak_gbs) if achieved else None,
+                "traffic": NCU_GATE_UP_TRAFFIC.get(m) if world == 1 else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch"
+                if world == 1 and m in NCU_GATE_UP_TRAFFIC else None,
                 "peak_source": peak_src, "algorithmic_bytes_per_launch": gate_up_bytes,
                 "avg_launch_ms": gu_ms, "distinct_experts": distinct,
                 "timing": "per-kernel CUDA events over an eager timed loop of the same steps",
