@@ -394,7 +394,7 @@ def decode_measure(hale, ctx, dec, shape, bpt, B, prompt, steps, warmup, seq0=0)
         dec.step(toks[:, pos], np.full(B, pos), seq_ids, logits=logits)
         pos += 1
     names = ("embed", "rmsnorm", "fgemv", "lm_head", "qk_rope", "attention", "router", "expert_gate_up",
-             "expert_down", "silu_mul")
+             "expert_down", "moe_token", "silu_mul")
     kernels = {}
     for nm in names:
         cnt, tot = ctx.profile_read(nm)
@@ -665,7 +665,7 @@ def main():
         prof = {}
         if with_profile:
             ctx.profile(False)
-            for kname in ("router", "expert_gate_up", "expert_down"):
+            for kname in ("router", "expert_gate_up", "expert_down", "moe_token"):
                 prof[kname] = ctx.profile_read(kname)
         ctx.check()
         ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))

@@ -29,6 +29,7 @@
 #include "hale_tc.cuh"
 #include "hale_stream.cuh"
 #include "hale_ws.cuh"
+#include "hale_token.cuh"
 #include "hale_ep.cuh"
 #include "hale_p2p.cuh"
 #include "hale_decoder.cuh"
@@ -378,7 +379,7 @@ extern "C" uint64_t hale_ctx_launch_count(const hale_ctx* ctx) { return ctx ? ct
 
 // Counter region of the MoE workspace (zero between calls).
 struct MoeLayout {
-    size_t tile_cnt, grid_cnt, comb_cnt, ws_cnt, counters_end;
+    size_t tile_cnt, grid_cnt, comb_cnt, ws_cnt, tok_bar, counters_end;
     size_t logits, topk_idx, topk_w, xq, xaux, elist_off, elist, active, n_active;
     size_t hq, haux, ybuf, total;
 };
@@ -396,6 +397,7 @@ static MoeLayout moe_layout(int M, int E, int k, int H, int I) {
     L.grid_cnt = take(4);
     L.comb_cnt = take((size_t)M * ((H + 127) / 128) * 4);
     L.ws_cnt = take(4 * 4);
+    L.tok_bar = take(4 * 4);
     L.counters_end = o;
     L.logits = take((size_t)M * E * 4);
     L.topk_idx = take((size_t)M * k * 4);
@@ -1473,6 +1475,100 @@ static hale_status tier_forward(hale_pool* p, uint32_t layer, const int* d_route
     return HALE_OK;
 }
 
+// One token through an HBM-resident pool: the whole layer in one launch
+// (moe_token_kernel). "auto" only; the other families keep their kernels.
+static bool use_token(const hale_ctx* ctx, const hale_pool* p, const hale_moe_layer* ly, uint32_t M) {
+    return M == 1 && !p->tiered && ctx->expert_kernel == HALE_EXPERT_AUTO && p->H % 128 == 0 && p->I % 32 == 0 &&
+           aligned16(ly->router) && ly->top_k <= 32 && ly->n_experts <= 256 &&
+           (p->dtype == HALE_Q4_0 || p->dtype == HALE_Q8_0);
+}
+
+// CTAs of moe_token_kernel one SM holds at `smem` bytes (cached per device
+// and size; the grid must never exceed what the GPU holds at once, since its
+// CTAs wait for one another).
+template <class F>
+static int token_occupancy(F* kern, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, std::pair<const void*, size_t>>, int> memo;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_pair(dev, std::make_pair(reinterpret_cast<const void*>(kern), smem));
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kTokThreads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    memo[key] = n;
+    return n;
+}
+
+template <int QT, int DT>
+static hale_status token_go(hale_ctx* ctx, TokenArgs a, cudaStream_t st, bool* done) {
+    auto* kern = moe_token_kernel<QT, DT>;
+    constexpr int wb = DT == 0 ? 4 : 2;
+    const int need = std::max(std::max(a.k * (a.I / 32), a.H / kTokDownRows), a.E);
+    int rpc = 1, G = 0;
+    size_t smem = 0;
+    for (int pass = 0; pass < 3; pass++) {
+        smem = (size_t)tok_plan(QFmt<QT>::BB, wb, a.H, a.I, a.k, rpc).total;
+        if (smem > 200 * 1024) return HALE_OK;  // not this kernel's shapes: the three-launch path
+        CUDA_TRY(ctx, allow_smem(kern, smem));
+        const int occ = token_occupancy(kern, smem);
+        G = std::min(need, ctx->sm_count * occ);
+        if (G <= 0) return HALE_OK;
+        const int r2 = (a.E + G - 1) / G;
+        if (r2 == rpc) break;
+        rpc = r2;
+        G = 0;
+    }
+    if (G <= 0 || rpc > 32) return HALE_OK;
+    a.rpc = rpc;
+    a.prefetch_all = a.k * (a.I / 32) > G ? 1 : 0;
+    {
+        ProfScope ps_(ctx, "moe_token", st);
+        kern<<<G, kTokThreads, smem, st>>>(a);
+    }
+    hale_status r = check_launch(ctx, "moe_token");
+    if (!r) *done = true;
+    return r;
+}
+
+static hale_status launch_token(hale_ctx* ctx, const hale_pool* p, const hale_moe_layer* ly, const float* x,
+                                const MoeLayout& L, float* out, int32_t* topk_idx, float* topk_w, cudaStream_t st,
+                                bool* done) {
+    uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
+    TokenArgs a{};
+    a.router = ly->router;
+    a.E = (int)p->E;
+    a.H = (int)p->H;
+    a.I = (int)p->I;
+    a.k = (int)ly->top_k;
+    a.normalize = ly->normalize_topk ? 1 : 0;
+    a.x = x;
+    a.logits = reinterpret_cast<float*>(ws + L.logits);
+    a.topk_idx = reinterpret_cast<int*>(ws + L.topk_idx);
+    a.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+    a.user_idx = topk_idx;
+    a.user_w = topk_w;
+    a.routing_counts = p->d_routing + (size_t)ly->layer * p->E;
+    a.experts = p->data + (size_t)ly->layer * p->E * p->expert_stride;
+    a.expert_stride = p->expert_stride;
+    a.hq = reinterpret_cast<int8_t*>(ws + L.hq);
+    a.haux = reinterpret_cast<int2*>(ws + L.haux);
+    a.out = out;
+    a.bar = reinterpret_cast<unsigned*>(ws + L.tok_bar);
+    a.err = ctx->d_err;
+    const int dt = float_code(ly->router_dtype);
+    if (p->dtype == HALE_Q4_0)
+        return dt == 0 ? token_go<0, 0>(ctx, a, st, done)
+                       : (dt == 1 ? token_go<0, 1>(ctx, a, st, done) : token_go<0, 2>(ctx, a, st, done));
+    return dt == 0 ? token_go<1, 0>(ctx, a, st, done)
+                   : (dt == 1 ? token_go<1, 1>(ctx, a, st, done) : token_go<1, 2>(ctx, a, st, done));
+}
+
 extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
                                         uint32_t M, float* out, int32_t* topk_idx, float* topk_w, void* stream) {
     if (!ctx || !p) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_moe_forward: NULL ctx or pool");
@@ -1495,6 +1591,11 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
     cudaStream_t st = S(stream);
     if (p->tiered && stream_capturing(stream))
         return fail(ctx, HALE_E_UNSUPPORTED, "a tiered pool resolves routes on the host; its forward cannot be captured");
+    if (use_token(ctx, p, ly, M)) {
+        bool done = false;
+        if ((r = launch_token(ctx, p, ly, x, L, out, topk_idx, topk_w, st, &done))) return r;
+        if (done) return HALE_OK;
+    }
     if ((r = launch_router(ctx, ly, p->H, x, M, L, true, topk_idx, topk_w, nullptr,
                            p->tiered ? nullptr : p->d_routing + (size_t)ly->layer * p->E, st)))
         return r;
