@@ -46,6 +46,7 @@ constexpr int kTokWarps = kTokThreads / 32;
 constexpr int kTokDownRows = 8;            // output rows per down unit
 constexpr int kTokChunk = 8;               // blocks per gate/up bulk copy
 constexpr uint32_t kTokPrefetch = 16384;   // bytes per L2 prefetch
+constexpr int kTokDownLoads = 8;           // down products per thread with loads in flight
 
 struct TokenArgs {
     const void* router;        // [E, H] f32 / f16 / bf16, row-major
@@ -118,15 +119,15 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Grid-wide barrier on a counter that is 0 when the launch starts: each CTA
-// adds one once its writes are done, then waits (bounded, ~1 s) for all
-// gridDim.x arrivals. Returns false (the same verdict in every thread of the
+// Grid-wide barrier on a counter that is 0 when the launch starts: after a
+// CTA barrier, thread 0 publishes the CTA's writes (fence.acq_rel + relaxed
+// add), then polls with acquire loads (bounded, ~1 s) until all gridDim.x
+// CTAs have arrived. Returns false (the same verdict in every thread of the
 // CTA) if the wait ran out.
 __device__ __forceinline__ bool tok_grid_sync(unsigned* cnt, uint32_t* err, int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        tok_add_acq_rel(cnt, 1u);
+        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         int ok = 1;
         const long long t0 = clock64();
         while (tok_ld_acquire(cnt) < gridDim.x) {
@@ -135,9 +136,7 @@ __device__ __forceinline__ bool tok_grid_sync(unsigned* cnt, uint32_t* err, int*
                 ok = 0;
                 break;
             }
-            __nanosleep(64);
         }
-        __threadfence();
         *s_ok = ok;
     }
     __syncthreads();
@@ -180,7 +179,7 @@ __device__ __forceinline__ int tok_block_sum(const uint4* w4, const int8_t* xb, 
 }
 
 template <int QT, int DT>
-__global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
+__global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(TokenArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t s_tab[32];
     __shared__ __align__(16) float s_e[256];
@@ -223,8 +222,9 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
     }
     __syncthreads();
     HALE_TOK_MARK(1);
-    // Q8Activations::quantize (quant.rs:77-93), each CTA for its own use
-    for (int b = tid; b < nbh; b += kTokThreads) {
+    // Q8Activations::quantize (quant.rs:77-93), each CTA for its own use, on
+    // warps 2.. first so that warp 0 starts the logit chains at once
+    for (int b = (tid + kTokThreads - 64) % kTokThreads; b < nbh; b += kTokThreads) {
         float sc;
         int sm;
         quantize_block<true>(xf + b * kQK, xq + b * kQK, &sc, &sm);
@@ -238,9 +238,21 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
         const bool valid = g < a.rpc && e < E;
         float acc = 0.0f;
         if (valid) {
+            // operands of 16 chain steps into registers, then the 16 steps
             const uint8_t* row = stage + (size_t)g * H * wb;
-#pragma unroll 8
-            for (int i = 0; i < H / 8; i++) acc = fadd(acc, fmul(smem_w<DT>(row, 8 * i + lane8), xf[8 * i + lane8]));
+            const int steps = H / 8;
+            int i = 0;
+            for (; i + 16 <= steps; i += 16) {
+                float wv[16], xv[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) {
+                    wv[u] = smem_w<DT>(row, 8 * (i + u) + lane8);
+                    xv[u] = xf[8 * (i + u) + lane8];
+                }
+#pragma unroll
+                for (int u = 0; u < 16; u++) acc = fadd(acc, fmul(wv[u], xv[u]));
+            }
+            for (; i < steps; i++) acc = fadd(acc, fmul(smem_w<DT>(row, 8 * i + lane8), xf[8 * i + lane8]));
         }
         const float s = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
         const float p = fadd(s, __shfl_down_sync(0xffffffffu, s, 1, 8));
@@ -341,7 +353,9 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
     {
         const int m = warp >> 2, q = warp & 3;   // m: 0 gate, 1 up; q: quarter of the blocks
         const int nbq = nbh / 4;
-        const int nch = (nbq + kTokChunk - 1) / kTokChunk;
+        // a warp's blocks fit both slots: one copy; else a ring of 8-block chunks
+        const int chb = nbq <= 2 * kTokChunk ? nbq : kTokChunk;
+        const int nch = (nbq + chb - 1) / chb;
         uint8_t* wbuf = stage + (size_t)warp * 2 * kTokChunk * REC;
         uint64_t* wbar = bars + warp * 2;
         float* tg = terms;                        // [2][nbh][32]
@@ -352,11 +366,11 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
             const uint8_t* src = a.experts + (size_t)s_sel[s] * a.expert_stride + (size_t)(m * TI + t) * tbh +
                                  (size_t)q * nbq * REC;
             auto issue = [&](int ch) {
-                const int nb = min(kTokChunk, nbq - ch * kTokChunk);
+                const int nb = min(chb, nbq - ch * chb);
                 const int slot = ch & 1;
                 mbar_arrive_expect_tx(&wbar[slot], (uint32_t)(nb * REC));
-                bulk_g2s(wbuf + (size_t)slot * kTokChunk * REC, src + (size_t)ch * kTokChunk * REC,
-                         (uint32_t)(nb * REC), &wbar[slot]);
+                bulk_g2s(wbuf + (size_t)slot * kTokChunk * REC, src + (size_t)ch * chb * REC, (uint32_t)(nb * REC),
+                         &wbar[slot]);
             };
             if (lane == 0) {
                 fence_proxy_async_smem();  // the stage held router rows / earlier chunks
@@ -374,10 +388,10 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
                 }
                 ph ^= 1u << slot;
                 const uint8_t* sb = wbuf + (size_t)slot * kTokChunk * REC;
-                const int nb = min(kTokChunk, nbq - ch * kTokChunk);
+                const int nb = min(chb, nbq - ch * chb);
 #pragma unroll 4
                 for (int bi = 0; bi < nb; bi++) {
-                    const int b = q * nbq + ch * kTokChunk + bi;
+                    const int b = q * nbq + ch * chb + bi;
                     const uint8_t* rec = sb + bi * REC;
                     const float ws =
                         half_bits_to_float(*reinterpret_cast<const uint16_t*>(rec + kTileRows * QB + lane * 2));
@@ -426,31 +440,50 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
     if (c < units_d) {
         int8_t* hs = reinterpret_cast<int8_t*>(stage);
         int2* ha = reinterpret_cast<int2*>(stage + (size_t)k * I);
-        for (int i = tid; i < k * I / 16; i += kTokThreads)
-            reinterpret_cast<uint4*>(hs)[i] = __ldcg(reinterpret_cast<const uint4*>(a.hq) + i);
-        for (int i = tid; i < k * nbi; i += kTokThreads) ha[i] = __ldcg(a.haux + i);
-        __syncthreads();
-        HALE_TOK_MARK(8);
-        float* dt = terms;                               // [k][nbi][8]
+        float* dt = terms;                                   // [k][nbi][8]
         float* ys = terms + (size_t)k * nbi * kTokDownRows;  // [k][8]
-        const int items = k * nbi * kTokDownRows;
+        const int items = k * nbi * kTokDownRows;             // (slot, block, row) products
+        bool staged = false;
         for (int u = c; u < units_d; u += G) {
             const int r0 = u * kTokDownRows;
-#pragma unroll 4
-            for (int it = tid; it < items; it += kTokThreads) {
-                const int rr = it & (kTokDownRows - 1), sb = it / kTokDownRows;
-                const int s = sb / nbi, b = sb - s * nbi;
-                const int r = r0 + rr;
-                const uint8_t* rec = a.experts + (size_t)s_sel[s] * a.expert_stride + down_off +
-                                     (size_t)(r / kTileRows) * tbd + (size_t)b * REC;
-                const int ri = r % kTileRows;
-                const float ws = half_bits_to_float(__ldg(reinterpret_cast<const unsigned short*>(rec + kTileRows * QB) + ri));
-                uint4 w4[2];
-                w4[0] = __ldg(reinterpret_cast<const uint4*>(rec + ri * QB));
-                if (QT == 1) w4[1] = __ldg(reinterpret_cast<const uint4*>(rec + ri * QB) + 1);
-                const int2 ax = ha[s * nbi + b];
-                const int is = tok_block_sum<QT>(w4, hs + (size_t)s * I + b * kQK, ax.y);
-                dt[it] = fmul(fmul(ws, __int_as_float(ax.x)), __int2float_rn(is));
+            for (int base = 0; base < items; base += kTokDownLoads * kTokThreads) {
+                // this thread's weight words first (L2 prefetched), then the
+                // h rows (first group only), then the products
+                uint4 wq[kTokDownLoads][QT == 1 ? 2 : 1];
+                unsigned short wsb[kTokDownLoads];
+#pragma unroll
+                for (int j = 0; j < kTokDownLoads; j++) {
+                    const int it = base + j * kTokThreads + tid;
+                    if (it < items) {
+                        const int rr = it % kTokDownRows, sb = it / kTokDownRows;
+                        const int s = sb / nbi, b = sb - s * nbi;
+                        const int r = r0 + rr, ri = r % kTileRows;
+                        const uint8_t* rec = a.experts + (size_t)s_sel[s] * a.expert_stride + down_off +
+                                             (size_t)(r / kTileRows) * tbd + (size_t)b * REC;
+                        wsb[j] = __ldg(reinterpret_cast<const unsigned short*>(rec + kTileRows * QB) + ri);
+                        wq[j][0] = __ldg(reinterpret_cast<const uint4*>(rec + ri * QB));
+                        if (QT == 1) wq[j][QT] = __ldg(reinterpret_cast<const uint4*>(rec + ri * QB) + 1);
+                    }
+                }
+                if (!staged) {
+                    for (int i = tid; i < k * I / 16; i += kTokThreads)
+                        reinterpret_cast<uint4*>(hs)[i] = __ldcg(reinterpret_cast<const uint4*>(a.hq) + i);
+                    for (int i = tid; i < k * nbi; i += kTokThreads) ha[i] = __ldcg(a.haux + i);
+                    __syncthreads();
+                    HALE_TOK_MARK(8);
+                    staged = true;
+                }
+#pragma unroll
+                for (int j = 0; j < kTokDownLoads; j++) {
+                    const int it = base + j * kTokThreads + tid;
+                    if (it < items) {
+                        const int sb = it / kTokDownRows;
+                        const int s = sb / nbi, b = sb - s * nbi;
+                        const int2 ax = ha[s * nbi + b];
+                        const int is = tok_block_sum<QT>(wq[j], hs + (size_t)s * I + b * kQK, ax.y);
+                        dt[it] = fmul(fmul(half_bits_to_float(wsb[j]), __int_as_float(ax.x)), __int2float_rn(is));
+                    }
+                }
             }
             __syncthreads();
             if (tid < k * kTokDownRows) {
@@ -472,7 +505,6 @@ __global__ void __launch_bounds__(kTokThreads) moe_token_kernel(TokenArgs a) {
     __syncthreads();
     HALE_TOK_MARK(9);
     if (tid == 0) {
-        __threadfence();
         if (tok_add_acq_rel(&a.bar[2], 1u) == (unsigned)G - 1) {
             // every CTA has passed both barriers: reset for the next launch
             a.bar[0] = 0u;
