@@ -33,6 +33,7 @@
 #include "hale_ep.cuh"
 #include "hale_p2p.cuh"
 #include "hale_decoder.cuh"
+#include "hale_attn.cuh"
 #include "hale_tier.h"
 
 using namespace hale;
@@ -252,6 +253,8 @@ static bool stream_capturing(void* stream) {
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+// Dynamic shared memory one CTA may ask for on sm_100 (227 KB).
+static constexpr size_t kMaxDynSmem = 227 * 1024;
 
 static bool is_quant(hale_dtype d) { return d == HALE_Q8_0 || d == HALE_Q4_0; }
 static bool is_float(hale_dtype d) { return d == HALE_F32 || d == HALE_F16 || d == HALE_BF16; }
@@ -2359,6 +2362,12 @@ struct hale_decoder {
     int gc_one = 1, gc_batch = 1;
     int gqa_cap[9] = {0};
     size_t gqa_smem[9] = {0};
+    // single-row attention over the whole GPU (attn_split_kernel)
+    bool split = false;
+    int split_grid = 0, split_npm = 0;
+    size_t split_smem = 0;
+    float *split_sc = nullptr, *split_pm = nullptr;
+    unsigned* split_bar = nullptr;
 };
 
 extern "C" void hale_decoder_destroy(hale_decoder* d) {
@@ -2569,18 +2578,49 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
             if (G % g == 0) { gmax = g; break; }
         d->gc_batch = gmax;
         d->gc_one = 0;  // 0: chosen per step from the row count
+        // group sizes whose shared-memory plan fits (wide heads may fit none:
+        // then attn_decode_kernel serves every step)
+        int fit = 0;
         for (int gc : {1, 2, 4, 8}) {
             if (G % gc != 0 || gc > gmax) continue;
             const int cap = (int)std::min<uint32_t>((uint32_t)gqa_score_cap(gc), (max_len + 3) & ~3u);
-            d->gqa_cap[gc] = cap;
-            d->gqa_smem[gc] = gqa_smem_floats(gc, cap, (int)hd) * 4;
-            cudaError_t e = gc == 1 ? allow_smem(attn_gqa_kernel<1>, d->gqa_smem[gc])
-                          : gc == 2 ? allow_smem(attn_gqa_kernel<2>, d->gqa_smem[gc])
-                          : gc == 4 ? allow_smem(attn_gqa_kernel<4>, d->gqa_smem[gc])
-                                    : allow_smem(attn_gqa_kernel<8>, d->gqa_smem[gc]);
+            const size_t sm = gqa_smem_floats(gc, cap, (int)hd) * 4;
+            if (sm > kMaxDynSmem) break;
+            cudaError_t e = gc == 1 ? allow_smem(attn_gqa_kernel<1>, sm)
+                          : gc == 2 ? allow_smem(attn_gqa_kernel<2>, sm)
+                          : gc == 4 ? allow_smem(attn_gqa_kernel<4>, sm)
+                                    : allow_smem(attn_gqa_kernel<8>, sm);
             if (e != cudaSuccess)
-                return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", d->gqa_smem[gc]));
+                return bail(fail(ctx, HALE_E_CUDA, "decoder: attention needs %zu bytes of shared memory", sm));
+            d->gqa_cap[gc] = cap;
+            d->gqa_smem[gc] = sm;
             min_cap = std::min<uint32_t>(min_cap, (uint32_t)cap);
+            fit = gc;
+        }
+        if (fit == 0) d->gqa = false;
+        d->gc_batch = std::min(d->gc_batch, std::max(fit, 1));
+    }
+    // one-row steps: attention spread over the GPU when the group fits its
+    // shared-memory plan (up to 32 query heads per kv head, head_dim % 8 == 0)
+    if (nh % nkv == 0 && nh / nkv <= 32 && hd % kSplitD == 0 &&
+        (size_t)split_plan((int)(nh / nkv), (int)hd).total * 4 <= kMaxDynSmem) {
+        const int G = (int)(nh / nkv);
+        d->split_smem = (size_t)split_plan(G, (int)hd).total * 4;
+        int occ = 0;
+        if (allow_smem(attn_split_kernel, d->split_smem) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attn_split_kernel, 256, d->split_smem) ==
+                cudaSuccess &&
+            occ > 0) {
+            d->split_npm = (int)((max_len + kSplitPB - 1) / kSplitPB);
+            const int units = std::max((int)nkv * d->split_npm, (int)(nkv * hd / kSplitD));
+            d->split_grid = std::min(ctx->sm_count * occ, units);
+            d->split = true;
+            if ((r = dec_alloc(ctx, d, (size_t)nh * ((max_len + 3) & ~3u) * 4, reinterpret_cast<void**>(&d->split_sc))) ||
+                (r = dec_alloc(ctx, d, (size_t)nh * d->split_npm * 4, reinterpret_cast<void**>(&d->split_pm))) ||
+                (r = dec_alloc(ctx, d, 16, reinterpret_cast<void**>(&d->split_bar))))
+                return bail(r);
+        } else {
+            cudaGetLastError();
         }
     }
     const size_t score_floats = max_len > min_cap ? B * nh * max_len : 4;
@@ -2599,6 +2639,17 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
     *out = d;
     return HALE_OK;
 }
+
+// L2 prefetch descriptor of up to two device ranges (a range that is not
+// 16-byte aligned is skipped; lengths round down to 16 bytes).
+static L2Prefetch l2_ranges(const void* a, size_t an, const void* b, size_t bn) {
+    L2Prefetch pf{};
+    if (a && aligned16(a)) { pf.p[0] = static_cast<const uint8_t*>(a); pf.bytes[0] = an & ~(size_t)15; }
+    if (b && aligned16(b)) { pf.p[1] = static_cast<const uint8_t*>(b); pf.bytes[1] = bn & ~(size_t)15; }
+    return pf;
+}
+// CTAs an RMSNorm launch adds for the L2 prefetch.
+static constexpr uint32_t kNormPrefetchCtas = 32;
 
 // One step of n rows on stream st: the row descriptors' copy from the pinned
 // slot, then every kernel of the step. logits: [n, V], or [1, V] for the last
@@ -2624,11 +2675,13 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         const auto& ly = d->layers[l];
         float* kc = d->kcache + (size_t)l * lstride;
         float* vc = d->vcache + (size_t)l * lstride;
-        // the previous layer's FFN residual folds into this norm
+        // the previous layer's FFN residual folds into this norm; its spare
+        // CTAs pull this layer's attention weights into L2 for the GEMVs
         {
             ProfScope ps_(ctx, "rmsnorm", st);
-            rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H,
-                                                         d->normed);
+            const L2Prefetch pf = l2_ranges(ly.qkv->data, ly.qkv->bytes, ly.o->data, ly.o->bytes);
+            rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(
+                d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed, (int)n, pf);
         }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
@@ -2641,7 +2694,26 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         if ((r = check_launch(ctx, "qk_rope"))) return r;
         {
             ProfScope ps_(ctx, "attention", st);
-            if (d->gqa) {
+            if (n == 1 && d->split) {
+                SplitArgs sa{};
+                sa.qkv = d->qkv;
+                sa.nh = (int)d->nh;
+                sa.nkv = (int)d->nkv;
+                sa.hd = (int)d->hd;
+                sa.kcache = kc;
+                sa.vcache = vc;
+                sa.rows = d->d_rows;
+                sa.seq_stride = d->seq_stride;
+                sa.scale = d->scale;
+                sa.sc = d->split_sc;
+                sa.pm = d->split_pm;
+                sa.sc_stride = (int)((d->max_len + 3) & ~3u);
+                sa.npm = d->split_npm;
+                sa.ctx = d->attn;
+                sa.bar = d->split_bar;
+                sa.err = ctx->d_err;
+                attn_split_kernel<<<d->split_grid, 256, d->split_smem, st>>>(sa);
+            } else if (d->gqa) {
                 // the most heads per CTA (each K/V element read once per group)
                 // that still gives about two thirds of the SMs a CTA
                 int gc = d->gc_one;
@@ -2671,7 +2743,12 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
         if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
         {
             ProfScope ps_(ctx, "rmsnorm", st);
-            rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, ly.post_norm, d->eps, H, d->normed);
+            // spare CTAs: the router (MoE) or the dense FFN's gate and up rows
+            const L2Prefetch pf =
+                ly.is_moe ? l2_ranges(ly.router, (size_t)d->E * H * (ly.router_dtype == HALE_F32 ? 4 : 2), nullptr, 0)
+                          : l2_ranges(ly.gate->data, ly.gate->bytes, ly.up->data, ly.up->bytes);
+            rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(d->x, d->delta, ly.post_norm, d->eps,
+                                                                              H, d->normed, (int)n, pf);
         }
         if ((r = check_launch(ctx, "rmsnorm"))) return r;
         if (ly.is_moe) {
@@ -2698,7 +2775,8 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
     }
     {
         ProfScope ps_(ctx, "rmsnorm", st);
-        rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed);
+        rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed, (int)n,
+                                                     l2_ranges(nullptr, 0, nullptr, 0));
     }
     if ((r = check_launch(ctx, "rmsnorm"))) return r;
     if (hidden) CUDA_TRY(ctx, cudaMemcpyAsync(hidden, d->normed, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, st));
@@ -2771,7 +2849,25 @@ extern "C" hale_status hale_decoder_step(hale_ctx* ctx, hale_decoder* d, const u
                                          const uint32_t* positions, const uint32_t* seqs, uint32_t n, float* logits,
                                          int32_t last_logits_only, float* hidden, void* stream) {
     if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_step: bad handle");
-    if (n == 0) return HALE_OK;
+    if (n == 0) {
+        // an expert-parallel rank with no rows still takes part in every
+        // layer's exchange (the other ranks' tokens may route to its experts)
+        if (!d->comm) return HALE_OK;
+        CUDA_TRY(ctx, cudaSetDevice(d->device));
+        for (const auto& ly : d->layers) {
+            if (!ly.is_moe) continue;
+            hale_moe_layer m{};
+            m.layer = ly.pool_layer;
+            m.router = ly.router;
+            m.router_dtype = ly.router_dtype;
+            m.n_experts = d->E;
+            m.top_k = d->k;
+            m.normalize_topk = d->normalize;
+            hale_status r = hale_moe_forward_ep(ctx, d->comm, d->pool, &m, nullptr, 0, nullptr, nullptr, nullptr, stream);
+            if (r) return r;
+        }
+        return HALE_OK;
+    }
     if (!tokens || !positions) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_step: NULL tokens or positions");
     if (n > d->max_batch)
         return fail(ctx, HALE_E_INVALID_ARGUMENT, "step of %u rows exceeds the decoder's %u", n, d->max_batch);

@@ -42,8 +42,36 @@ __global__ void embed_kernel(const void* __restrict__ embed, int H, const uint32
 // with every global load issued up front, so the one sequential chain is
 // FADDs alone over 16-byte shared loads issued ahead of it and the output
 // pass reads no global memory. Dynamic shared memory: 3 n floats.
+// Up to two byte ranges to pull into L2 while a latency-bound kernel runs
+// (the next kernels' weights). Each range: 16-byte aligned, a multiple of 16
+// bytes (or null / 0).
+struct L2Prefetch {
+    const uint8_t* p[2];
+    size_t bytes[2];
+};
+constexpr uint32_t kL2Piece = 16384;
+
+// CTA `slot` of `slots` prefetch CTAs issues its share of the ranges' pieces
+// (cp.async.bulk.prefetch.L2: no destination, nothing to wait for).
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int slot, int slots) {
+    for (int r = 0; r < 2; r++) {
+        if (!pf.p[r]) continue;
+        const size_t n = (pf.bytes[r] + kL2Piece - 1) / kL2Piece;
+        for (size_t i = (size_t)slot + (size_t)slots * threadIdx.x; i < n; i += (size_t)slots * blockDim.x) {
+            const size_t off = i * kL2Piece;
+            const uint32_t len = (uint32_t)(pf.bytes[r] - off < kL2Piece ? pf.bytes[r] - off : kL2Piece);
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.p[r] + off), "r"(len) : "memory");
+        }
+    }
+}
+
+// Rows past the first n of the grid only prefetch (pf) and leave.
 __global__ void rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w,
-                               float eps, int n, float* __restrict__ out) {
+                               float eps, int n, float* __restrict__ out, int rows, L2Prefetch pf) {
+    if ((int)blockIdx.x >= rows) {
+        l2_prefetch_share(pf, blockIdx.x - rows, gridDim.x - rows);
+        return;
+    }
     extern __shared__ __align__(16) float s_v[];  // [n] v, [n] v*v, [n] w
     float* s_sq = s_v + n;
     float* s_w = s_sq + n;

@@ -466,8 +466,9 @@ HALE_API hale_status hale_decoder_step(hale_ctx* ctx, hale_decoder* dec, const u
  * rank's n_experts / n_ranks experts of every MoE layer (HBM-resident);
  * attention and the dense layers stay on this rank for its own sequences
  * (data-parallel). Every rank must then make the same sequence of decoder
- * calls (collective per MoE layer; its own rows each time), which run
- * eagerly (no graph replay). comm NULL returns to single-GPU layers.
+ * calls (collective per MoE layer; its own rows each time; a rank with no
+ * rows calls hale_decoder_step with n = 0, which still joins every MoE
+ * layer's exchange), which run eagerly (no graph replay). comm NULL returns to single-GPU layers.
  * comm's max_tokens must cover the decoder's max_batch. Such a decoder is
  * created with the rank's pool (n_experts / n_ranks experts per layer);
  * until its comm is set, its MoE calls fail with HALE_E_INVALID_ARGUMENT. */

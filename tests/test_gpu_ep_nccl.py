@@ -86,8 +86,9 @@ def _rank_main(rank, world, port, uid, uid2, uid3, results):
             om = OM.OracleModel(expert_dtype=qt, hf_config=hf, tensors=tt, expert_encoded=enc)
             e_r = E2 // world
             toks = np.random.default_rng(40 + rank).integers(0, V2, 9).tolist()
-            full_dec = build_decoder(ctx, om, qt, len(toks), max_batch=4)
-            ep_dec = build_decoder(ctx, om, qt, len(toks), max_batch=4, experts=range(rank * e_r, (rank + 1) * e_r))
+            full_dec = build_decoder(ctx, om, qt, len(toks) + 1, max_batch=4)
+            ep_dec = build_decoder(ctx, om, qt, len(toks) + 1, max_batch=4,
+                                   experts=range(rank * e_r, (rank + 1) * e_r))
             dcomm = hale.Comm(ctx, world, rank, duid, Hh, E2, k2, 4)
             try:
                 ep_dec.set_comm(dcomm)
@@ -101,6 +102,15 @@ def _rank_main(rank, world, port, uid, uid2, uid3, results):
                 for i in range(4, len(toks)):
                     ep_dec.step([toks[i]], [i], logits=lg[:1])
                     full_dec.step([toks[i]], [i], logits=lw[:1])
+                    got.append(lg[:1].cpu().numpy().copy())
+                    want.append(lw[:1].cpu().numpy().copy())
+                # a step in which rank 0 has no rows: it still joins every
+                # MoE layer's exchange, so the others' tokens reach its experts
+                if rank == 0:
+                    ep_dec.step([], [])
+                else:
+                    ep_dec.step([toks[0]], [len(toks)], logits=lg[:1])
+                    full_dec.step([toks[0]], [len(toks)], logits=lw[:1])
                     got.append(lg[:1].cpu().numpy().copy())
                     want.append(lw[:1].cpu().numpy().copy())
                 ctx.check()
