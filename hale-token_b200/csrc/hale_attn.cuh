@@ -85,6 +85,7 @@ struct SplitArgs {
     int sc_stride, npm;
     float* ctx;               // [nh * hd]
     unsigned* bar;            // [3] grid barrier counters, 0 at entry and exit
+    L2Prefetch pf;            // the next kernels' weights, pulled into L2 at the start
     uint32_t* err;
 };
 
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
     if (tid < 32) s_tab[tid] = kExp2TabDev[tid];
     const float* qrow = a.qkv;
     const int npb = (seq + kSplitPB - 1) / kSplitPB;
+    l2_prefetch_share(a.pf, blockIdx.x, gridDim.x);
     HALE_SPLIT_MARK(0);
 
     // ---- S: score chains ------------------------------------------------------

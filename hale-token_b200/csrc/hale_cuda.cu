@@ -22,6 +22,7 @@
 #include <mutex>
 #include <set>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/hale_cuda.h"
@@ -615,6 +616,62 @@ static void fgemv_dispatch(const hale_matrix* m, const float* x, uint32_t M, flo
         fgemv_kernel<DT, 8><<<grid, 128, 0, st>>>(m->data, (int)m->rows, (int)m->cols, (int)m->nb, x, (int)M, out, vec);
 }
 
+// Blocks a kernel keeps resident per SM at `smem` bytes and `threads`
+// threads (cached per device, kernel and configuration).
+template <class F>
+static int kernel_occupancy(F* kern, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, const void*, int, size_t>, int> memo;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kern), threads, smem);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+    int n = 0;
+    if (allow_smem(kern, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    memo[key] = n;
+    return n;
+}
+
+// Warps per CTA of the single-row lane-major kernels: 8 (32 rows) when that
+// still gives every SM two CTAs, else 4 so a decode-size matrix spreads over
+// more SMs.
+static unsigned lanes_warps(const hale_ctx* ctx, const hale_matrix* m) {
+    return m->rows_pad / 32 >= 2u * (unsigned)ctx->sm_count ? 8u : 4u;
+}
+
+// Weight-ring depth of a single-row lane-major launch: the deepest (up to 4
+// stages, no more than a warp's region has) that keeps the whole grid in one
+// wave; grids of several waves take 2 (more CTAs per SM). 0: nothing fits.
+template <class F>
+static int lanes_pick_ns(const hale_ctx* ctx, F* kern, int act_bytes, uint32_t cols, int stage_bytes, unsigned wpc,
+                         unsigned grid, size_t* smem_out) {
+    const int nst = (int)((cols / 64 + kLanesSB - 1) / kLanesSB);
+    int fallback = 0;
+    size_t fb_smem = 0;
+    for (int ns = std::min(4, std::max(nst, 1)); ns >= 1; ns--) {
+        const size_t smem = lanes_smem(act_bytes, (int)wpc, ns * stage_bytes, ns);
+        if (smem > kMaxDynSmem) continue;
+        const int occ = kernel_occupancy(kern, (int)(32 * wpc), smem);
+        if (occ <= 0) continue;
+        if ((long long)occ * ctx->sm_count >= (long long)grid) {
+            *smem_out = smem;
+            return ns;
+        }
+        if (fallback == 0 || ns == 2) {
+            fallback = ns;
+            fb_smem = smem;
+        }
+    }
+    *smem_out = fb_smem;
+    return fallback;
+}
+
 static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float* x, uint32_t M, float* out,
                                 cudaStream_t st) {
     ProfScope ps_(ctx, "fgemv", st);
@@ -649,20 +706,22 @@ static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float
         return check_launch(ctx, "fgemv_lanes_batch");
     }
     if (m->lanes) {
-        // 8 warps (32 rows) per CTA when that still gives every SM two CTAs;
-        // otherwise 4 warps, so a decode-size matrix spreads over more SMs
-        const unsigned wpc = m->rows_pad / 32 >= 2u * (unsigned)ctx->sm_count ? 8u : 4u;
-        const unsigned grid = (m->rows_pad / 4 + wpc - 1) / wpc, threads = 32 * wpc;
-        const size_t smem = (size_t)m->cols * 4;
-        for (uint32_t t = 0; t < M; t++) {
-            const float* xt = x + (size_t)t * m->cols;
-            float* ot = out + (size_t)t * m->rows;
-            switch (m->dtype) {
-            case HALE_F32: fgemv_lanes_kernel<0><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
-            case HALE_F16: fgemv_lanes_kernel<1><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
-            default: fgemv_lanes_kernel<2><<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, xt, ot); break;
-            }
-        }
+        const unsigned wpc = lanes_warps(ctx, m), grid = (m->rows_pad / 4 + wpc - 1) / wpc, threads = 32 * wpc;
+        auto go = [&](auto kern, int ring_stage) -> cudaError_t {
+            size_t smem = 0;
+            const int ns = lanes_pick_ns(ctx, kern, (int)m->cols * 4, m->cols, ring_stage, wpc, grid, &smem);
+            if (ns == 0) return cudaErrorInvalidConfiguration;
+            cudaError_t e = allow_smem(kern, smem);
+            if (e != cudaSuccess) return e;
+            for (uint32_t t = 0; t < M; t++)
+                kern<<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, x + (size_t)t * m->cols,
+                                                  out + (size_t)t * m->rows, ns, ctx->d_err);
+            return cudaSuccess;
+        };
+        cudaError_t e = m->dtype == HALE_F32 ? go(fgemv_lanes_kernel<0>, lanes_stage_bytes<0>())
+                        : m->dtype == HALE_F16 ? go(fgemv_lanes_kernel<1>, lanes_stage_bytes<1>())
+                                               : go(fgemv_lanes_kernel<2>, lanes_stage_bytes<2>());
+        if (e != cudaSuccess) return fail(ctx, HALE_E_CUDA, "fgemv_lanes: %s", cudaGetErrorString(e));
         return check_launch(ctx, "fgemv_lanes");
     }
     int vec = (m->cols % 4 == 0) && (((uintptr_t)x & 15) == 0);
@@ -672,6 +731,42 @@ static hale_status fgemv_launch(hale_ctx* ctx, const hale_matrix* m, const float
     default: fgemv_dispatch<2>(m, x, M, out, vec, st); break;
     }
     return check_launch(ctx, "fgemv");
+}
+
+// One activation row through a lane-major float matrix with the RMSNorm in
+// front folded in (fgemv_lanes_norm_kernel); false in *done when the matrix
+// or buffers do not fit that kernel (nothing launched).
+static hale_status fgemv_norm_launch(hale_ctx* ctx, const hale_matrix* m, const float* x, const float* delta,
+                                     const float* nw, float eps, float* x_out, float* out, cudaStream_t st,
+                                     bool* done) {
+    *done = false;
+    if (!m->lanes || m->cols % 64 || !aligned16(x) || (delta && (!aligned16(delta) || !aligned16(x_out))))
+        return HALE_OK;
+    const unsigned wpc = lanes_warps(ctx, m), grid = (m->rows_pad / 4 + wpc - 1) / wpc, threads = 32 * wpc;
+    if (m->cols > 4u * kLanesNormVec * threads) return HALE_OK;
+    ProfScope ps_(ctx, "fgemv", st);
+    bool skip = false;
+    auto go = [&](auto kern, int ring_stage) -> cudaError_t {
+        size_t smem = 0;
+        const int ns = lanes_pick_ns(ctx, kern, (int)m->cols * 8, m->cols, ring_stage, wpc, grid, &smem);
+        if (ns == 0) {
+            skip = true;
+            return cudaSuccess;
+        }
+        cudaError_t e = allow_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, threads, smem, st>>>(m->data, (int)m->rows, (int)m->cols, x, delta, nw, eps, x_out, out, ns,
+                                          ctx->d_err);
+        return cudaSuccess;
+    };
+    cudaError_t e = m->dtype == HALE_F32 ? go(fgemv_lanes_norm_kernel<0>, lanes_stage_bytes<0>())
+                    : m->dtype == HALE_F16 ? go(fgemv_lanes_norm_kernel<1>, lanes_stage_bytes<1>())
+                                           : go(fgemv_lanes_norm_kernel<2>, lanes_stage_bytes<2>());
+    if (e != cudaSuccess) return fail(ctx, HALE_E_CUDA, "fgemv_lanes_norm: %s", cudaGetErrorString(e));
+    if (skip) return HALE_OK;
+    hale_status r = check_launch(ctx, "fgemv_lanes_norm");
+    if (!r) *done = true;
+    return r;
 }
 
 extern "C" hale_status hale_quantize_q8(hale_ctx* ctx, const float* x, uint32_t m_rows, uint32_t cols,
@@ -1539,9 +1634,18 @@ static hale_status token_go(hale_ctx* ctx, TokenArgs a, cudaStream_t st, bool* d
     return r;
 }
 
+// RMSNorm folded in front of a one-token layer (the decoder's post-attention
+// norm): input = rmsnorm(x + delta) * w; x + delta goes to x_out.
+struct TokNorm {
+    const float* delta;
+    const float* w;
+    float eps;
+    float* x_out;
+};
+
 static hale_status launch_token(hale_ctx* ctx, const hale_pool* p, const hale_moe_layer* ly, const float* x,
                                 const MoeLayout& L, float* out, int32_t* topk_idx, float* topk_w, cudaStream_t st,
-                                bool* done) {
+                                bool* done, const TokNorm* norm = nullptr) {
     uint8_t* ws = static_cast<uint8_t*>(ctx->ws);
     TokenArgs a{};
     a.router = ly->router;
@@ -1564,6 +1668,12 @@ static hale_status launch_token(hale_ctx* ctx, const hale_pool* p, const hale_mo
     a.out = out;
     a.bar = reinterpret_cast<unsigned*>(ws + L.tok_bar);
     a.err = ctx->d_err;
+    if (norm) {
+        a.delta = norm->delta;
+        a.norm_w = norm->w;
+        a.eps = norm->eps;
+        a.x_out = norm->x_out;
+    }
     const int dt = float_code(ly->router_dtype);
     if (p->dtype == HALE_Q4_0)
         return dt == 0 ? token_go<0, 0>(ctx, a, st, done)
@@ -1637,6 +1747,22 @@ extern "C" hale_status hale_moe_forward(hale_ctx* ctx, hale_pool* p, const hale_
         p->done_recorded = true;
     }
     return r;
+}
+
+// The decoder's post-attention RMSNorm and a one-token MoE layer in one
+// launch when the token kernel serves the layer (*done), else nothing is
+// launched and the caller runs the two separately.
+static hale_status moe_token_norm(hale_ctx* ctx, hale_pool* p, const hale_moe_layer* ly, const float* x,
+                                  const TokNorm& norm, float* out, cudaStream_t st, bool* done) {
+    *done = false;
+    if (!use_token(ctx, p, ly, 1) || p->H > 4u * kTokNormVec * kTokThreads || ly->layer >= p->L ||
+        ly->n_experts != p->E ||
+        p->layer_resident[ly->layer] != p->E || !aligned16(x) || !aligned16(norm.delta) || !aligned16(norm.x_out))
+        return HALE_OK;
+    MoeLayout L;
+    hale_status r = ensure_moe_ws(ctx, 1, (int)p->E, (int)ly->top_k, (int)p->H, (int)p->I, st, &L);
+    if (r) return r;
+    return launch_token(ctx, p, ly, x, L, out, nullptr, nullptr, st, done, &norm);
 }
 
 // The expert kernels over the routes in a (expert lists built, activations
@@ -2341,6 +2467,8 @@ struct hale_decoder {
     float* final_norm = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr, *kcache = nullptr, *vcache = nullptr;
     float *x = nullptr, *normed = nullptr, *delta = nullptr, *qkv = nullptr, *attn = nullptr;
+    float* x2 = nullptr;  // second residual buffer: norms folded into their consumers write x + delta here
+    float* moe_out = nullptr;  // a fused norm + MoE layer writes its output here (it reads delta)
     float *g = nullptr, *u = nullptr, *h = nullptr, *scores = nullptr;
     std::vector<void*> allocs;
     // step rows (token, position, sequence) through device memory from a
@@ -2624,7 +2752,8 @@ extern "C" hale_status hale_decoder_create_batched(hale_ctx* ctx, const hale_dec
         }
     }
     const size_t score_floats = max_len > min_cap ? B * nh * max_len : 4;
-    struct { float** p; size_t n; } bufs[] = {{&d->x, B * H}, {&d->normed, B * H}, {&d->delta, B * H},
+    struct { float** p; size_t n; } bufs[] = {{&d->x, B * H}, {&d->x2, B * H}, {&d->moe_out, B * H},
+                                               {&d->normed, B * H}, {&d->delta, B * H},
                                                {&d->qkv, B * qkv_rows}, {&d->attn, B * nh * hd},
                                                {&d->g, B * max_inter}, {&d->u, B * max_inter},
                                                {&d->h, B * max_inter}, {&d->scores, score_floats}};
@@ -2671,20 +2800,37 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
     }
     }
     if ((r = check_launch(ctx, "embed"))) return r;
+    // the residual stream: norms folded into their consumer read xr and write
+    // xr + delta to the other buffer (other CTAs of the launch still read xr)
+    float* xr = d->x;
+    float* xo = d->x2;
+    // the layer output buffer (dl) and its spare: a fused norm + MoE layer
+    // reads dl and writes dspare, which then becomes dl
+    float* dl = d->delta;
+    float* dspare = d->moe_out;
     for (uint32_t l = 0; l < d->L; l++) {
         const auto& ly = d->layers[l];
         float* kc = d->kcache + (size_t)l * lstride;
         float* vc = d->vcache + (size_t)l * lstride;
-        // the previous layer's FFN residual folds into this norm; its spare
-        // CTAs pull this layer's attention weights into L2 for the GEMVs
-        {
-            ProfScope ps_(ctx, "rmsnorm", st);
-            const L2Prefetch pf = l2_ranges(ly.qkv->data, ly.qkv->bytes, ly.o->data, ly.o->bytes);
-            rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(
-                d->x, l ? d->delta : nullptr, ly.in_norm, d->eps, H, d->normed, (int)n, pf);
+        // the previous layer's FFN residual folds into this norm; one row: the
+        // norm runs inside the q/k/v matvec
+        bool fused = false;
+        if (n == 1 && (r = fgemv_norm_launch(ctx, ly.qkv, xr, l ? dl : nullptr, ly.in_norm, d->eps,
+                                             l ? xo : nullptr, d->qkv, st, &fused)))
+            return r;
+        if (fused) {
+            if (l) std::swap(xr, xo);
+        } else {
+            {
+                // spare CTAs pull this layer's attention weights into L2
+                ProfScope ps_(ctx, "rmsnorm", st);
+                const L2Prefetch pf = l2_ranges(ly.qkv->data, ly.qkv->bytes, ly.o->data, ly.o->bytes);
+                rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(
+                    xr, l ? dl : nullptr, ly.in_norm, d->eps, H, d->normed, (int)n, pf);
+            }
+            if ((r = check_launch(ctx, "rmsnorm"))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
         }
-        if ((r = check_launch(ctx, "rmsnorm"))) return r;
-        if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
         {
             ProfScope ps_(ctx, "qk_rope", st);
             qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
@@ -2711,6 +2857,7 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
                 sa.npm = d->split_npm;
                 sa.ctx = d->attn;
                 sa.bar = d->split_bar;
+                sa.pf = l2_ranges(ly.o->data, ly.o->bytes, nullptr, 0);
                 sa.err = ctx->d_err;
                 attn_split_kernel<<<d->split_grid, 256, d->split_smem, st>>>(sa);
             } else if (d->gqa) {
@@ -2740,29 +2887,44 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             }
         }
         if ((r = check_launch(ctx, "attn_decode"))) return r;
-        if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, d->delta, nullptr, stream))) return r;
-        {
-            ProfScope ps_(ctx, "rmsnorm", st);
-            // spare CTAs: the router (MoE) or the dense FFN's gate and up rows
-            const L2Prefetch pf =
-                ly.is_moe ? l2_ranges(ly.router, (size_t)d->E * H * (ly.router_dtype == HALE_F32 ? 4 : 2), nullptr, 0)
-                          : l2_ranges(ly.gate->data, ly.gate->bytes, ly.up->data, ly.up->bytes);
-            rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(d->x, d->delta, ly.post_norm, d->eps,
-                                                                              H, d->normed, (int)n, pf);
-        }
-        if ((r = check_launch(ctx, "rmsnorm"))) return r;
+        if ((r = hale_matrix_matvec(ctx, ly.o, d->attn, n, dl, nullptr, stream))) return r;
+        hale_moe_layer m{};
         if (ly.is_moe) {
-            hale_moe_layer m{};
             m.layer = ly.pool_layer;
             m.router = ly.router;
             m.router_dtype = ly.router_dtype;
             m.n_experts = d->E;
             m.top_k = d->k;
             m.normalize_topk = d->normalize;
+        }
+        // one row through a resident pool: the post-attention norm runs inside
+        // the one-launch MoE layer (its output, the layer's delta, replaces
+        // the attention delta it read)
+        fused = false;
+        if (ly.is_moe && n == 1 && !d->comm && !d->pool->tiered) {
+            const TokNorm tn{dl, ly.post_norm, d->eps, xo};
+            if ((r = moe_token_norm(ctx, d->pool, &m, xr, tn, dspare, st, &fused))) return r;
+            if (fused) {
+                std::swap(xr, xo);
+                std::swap(dl, dspare);
+                continue;
+            }
+        }
+        {
+            ProfScope ps_(ctx, "rmsnorm", st);
+            // spare CTAs: the router (MoE) or the dense FFN's gate and up rows
+            const L2Prefetch pf =
+                ly.is_moe ? l2_ranges(ly.router, (size_t)d->E * H * (ly.router_dtype == HALE_F32 ? 4 : 2), nullptr, 0)
+                          : l2_ranges(ly.gate->data, ly.gate->bytes, ly.up->data, ly.up->bytes);
+            rmsnorm_kernel<<<n + kNormPrefetchCtas, 256, (size_t)H * 12, st>>>(xr, dl, ly.post_norm, d->eps,
+                                                                              H, d->normed, (int)n, pf);
+        }
+        if ((r = check_launch(ctx, "rmsnorm"))) return r;
+        if (ly.is_moe) {
             if (d->comm)
-                r = hale_moe_forward_ep(ctx, d->comm, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream);
+                r = hale_moe_forward_ep(ctx, d->comm, d->pool, &m, d->normed, n, dl, nullptr, nullptr, stream);
             else
-                r = hale_moe_forward(ctx, d->pool, &m, d->normed, n, d->delta, nullptr, nullptr, stream);
+                r = hale_moe_forward(ctx, d->pool, &m, d->normed, n, dl, nullptr, nullptr, stream);
             if (r) return r;
         } else {
             if ((r = hale_matrix_matvec(ctx, ly.gate, d->normed, n, d->g, nullptr, stream))) return r;
@@ -2770,12 +2932,12 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             const int cnt = (int)(n * ly.inter);
             silu_mul_kernel<<<(cnt + 255) / 256, 256, 0, st>>>(d->g, d->u, cnt, d->h);
             if ((r = check_launch(ctx, "silu_mul"))) return r;
-            if ((r = hale_matrix_matvec(ctx, ly.down, d->h, n, d->delta, nullptr, stream))) return r;
+            if ((r = hale_matrix_matvec(ctx, ly.down, d->h, n, dl, nullptr, stream))) return r;
         }
     }
     {
         ProfScope ps_(ctx, "rmsnorm", st);
-        rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(d->x, d->delta, d->final_norm, d->eps, H, d->normed, (int)n,
+        rmsnorm_kernel<<<n, 256, (size_t)H * 12, st>>>(xr, dl, d->final_norm, d->eps, H, d->normed, (int)n,
                                                      l2_ranges(nullptr, 0, nullptr, 0));
     }
     if ((r = check_launch(ctx, "rmsnorm"))) return r;

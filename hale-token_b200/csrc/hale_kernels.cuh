@@ -1203,11 +1203,134 @@ __device__ __forceinline__ int lanes_x_slot(int c) {
 // ((a0+a4)+(a1+a5))+((a2+a6)+(a3+a7)) (quant.rs:37-41) combines the 8
 // threads; the (empty) tail adds -0. 8x the row parallelism of
 // fgemv_kernel, with 512-byte warp loads.
+// Single-row lane-major matvec: each warp's 4 rows are one contiguous
+// region (S8 groups of [4 rows][64 columns]); the warp streams it through a
+// ring of `ns` shared-memory stages of kLanesSB groups by bulk copies (lane 0
+// issues every stage it can at once, then refills), so the whole region is
+// in flight from the kernel's start -- under the RMSNorm chain when the norm
+// is folded in. Shared memory after the staged activations:
+// lanes_ring_bytes<DT>(ns) per warp, then ns mbarriers per warp.
+constexpr int kLanesSB = 8;  // 64-column groups per stage
+
+// Phase marks for timing probes built from this header; empty in the library.
+#ifndef HALE_LANES_MARK
+#define HALE_LANES_MARK(i)
+#endif
+
+template <int DT>
+__host__ __device__ constexpr int lanes_stage_bytes() { return kLanesSB * 4 * 64 * (DT == 0 ? 4 : 2); }
+template <int DT>
+__host__ __device__ inline int lanes_ring_bytes(int ns) { return ns * lanes_stage_bytes<DT>(); }
+
+// Issue stages [st0, st1) of this warp's region (lane 0 only).
+template <int DT>
+__device__ __forceinline__ void lanes_issue(const uint8_t* wq, int S8, uint8_t* ring, uint64_t* bars, int ns,
+                                            int st0, int st1) {
+    constexpr int ES = DT == 0 ? 4 : 2, STB = lanes_stage_bytes<DT>();
+    for (int st = st0; st < st1; st++) {
+        const int slot = st % ns, groups = min(kLanesSB, S8 - st * kLanesSB);
+        const uint32_t bytes = (uint32_t)(groups * 4 * 64 * ES);
+        mbar_arrive_expect_tx(&bars[slot], bytes);
+        bulk_g2s(ring + (size_t)slot * STB, wq + (size_t)st * STB, bytes, &bars[slot]);
+    }
+}
+
+// Starts this warp's weight stream (barrier init + the first ns stages).
+// Returns false for warps past the last row (nothing issued).
+template <int DT>
+__device__ __forceinline__ bool lanes_start(const uint8_t* __restrict__ W, int rows, int cols, uint8_t* ring,
+                                            uint64_t* bars, int ns) {
+    constexpr int ES = DT == 0 ? 4 : 2;
+    const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (q * 4 >= rows) return false;
+    const int S8 = cols / 64, nst = (S8 + kLanesSB - 1) / kLanesSB;
+    if (lane == 0) {
+        for (int i = 0; i < ns; i++) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+        const uint8_t* wq = W + (size_t)q * 4 * cols * ES;
+        lanes_issue<DT>(wq, S8, ring, bars, ns, 0, min(ns, nst));
+        if (nst > ns) {
+            // the stages the ring cannot hold yet: into L2, for the refills
+            const size_t done = (size_t)ns * lanes_stage_bytes<DT>(), total = (size_t)4 * cols * ES;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wq + done), "r"((uint32_t)(total - done))
+                         : "memory");
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+// The matvec proper over activations already staged in s_x (lanes order),
+// consuming the stream lanes_start began.
+template <int DT>
+__device__ __forceinline__ void lanes_gemv(const uint8_t* __restrict__ W, int rows, int cols, const float* s_x,
+                                           float* __restrict__ out, uint8_t* ring, uint64_t* bars, int ns,
+                                           uint32_t* err) {
+    constexpr int ES = DT == 0 ? 4 : 2, STB = lanes_stage_bytes<DT>();
+    const float4* s_x4 = reinterpret_cast<const float4*>(s_x);
+    const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int rr = lane >> 3, l = lane & 7, S8 = cols / 64, nst = (S8 + kLanesSB - 1) / kLanesSB;
+    const uint8_t* wq = W + (size_t)q * 4 * cols * ES;
+    float acc = 0.0f;
+    uint32_t ph = 0;
+    for (int st = 0; st < nst; st++) {
+        const int slot = st % ns;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[slot], (ph >> slot) & 1u, err))) {
+            // copies still in flight get a bounded chance to land
+            for (int s2 = st; s2 < min(st + ns, nst); s2++)
+                mbar_wait(&bars[s2 % ns], (ph >> (s2 % ns)) & 1u, nullptr, 400000000LL);
+            return;
+        }
+        ph ^= 1u << slot;
+        if (st == 0) HALE_LANES_MARK(5);
+        const uint8_t* sb = ring + (size_t)slot * STB;
+        const int groups = min(kLanesSB, S8 - st * kLanesSB);
+#pragma unroll
+        for (int u = 0; u < kLanesSB; u++) {
+            if (u < groups) {
+                const int s = st * kLanesSB + u;
+                Raw8<DT> rw;
+                const uint4* src = reinterpret_cast<const uint4*>(sb + ((u * 4 + rr) * 64 + l * 8) * ES);
+                rw.a = src[0];
+                if (DT == 0) rw.b = src[1];
+                float w[8];
+                raw8_decode<DT>(rw, w);
+                const float4 xa = s_x4[(s << 4) + l], xb = s_x4[(s << 4) + 8 + l];
+                acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
+                acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
+                acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
+                acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && st + ns < nst) {
+            fence_proxy_async_smem();
+            lanes_issue<DT>(wq, S8, ring, bars, ns, st + ns, st + ns + 1);
+        }
+    }
+    const float s1 = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
+    const float p = fadd(s1, __shfl_down_sync(0xffffffffu, s1, 1, 8));
+    const float r = fadd(p, __shfl_down_sync(0xffffffffu, p, 2, 8));
+    const int row = q * 4 + rr;
+    if (l == 0 && row < rows) out[row] = fadd(r, -0.0f);
+}
+
+// Shared memory of the single-row kernels: `act` bytes of staged
+// activations (and norm scratch), then each warp's ring, then its barriers.
+__host__ __device__ inline size_t lanes_smem(int act_bytes, int warps, int ring_bytes, int ns) {
+    return (size_t)act_bytes + (size_t)warps * ring_bytes + (size_t)warps * ns * 8;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restrict__ W, int rows, int cols,
-                                                          const float* __restrict__ x, float* __restrict__ out) {
-    extern __shared__ __align__(16) float s_x[];  // [cols]
-    constexpr int ES = DT == 0 ? 4 : 2;
+                                                          const float* __restrict__ x, float* __restrict__ out,
+                                                          int ns, uint32_t* err) {
+    extern __shared__ __align__(128) float s_x[];  // [cols], rings, barriers
+    const int warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    uint8_t* rings = reinterpret_cast<uint8_t*>(s_x) + (size_t)cols * 4;
+    uint8_t* ring = rings + (size_t)warp * lanes_ring_bytes<DT>(ns);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rings + (size_t)warps * lanes_ring_bytes<DT>(ns)) + warp * ns;
+    const bool live = lanes_start<DT>(W, rows, cols, ring, bars, ns);
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const float4* x4 = reinterpret_cast<const float4*>(x);
 #pragma unroll 4
@@ -1222,54 +1345,99 @@ __global__ void __launch_bounds__(256) fgemv_lanes_kernel(const uint8_t* __restr
         for (int i = threadIdx.x; i < cols; i += blockDim.x) s_x[lanes_x_slot(i)] = x[i];
     }
     __syncthreads();
-    const float4* s_x4 = reinterpret_cast<const float4*>(s_x);
-    const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (q * 4 >= rows) return;
-    const int rr = lane >> 3, l = lane & 7, S8 = cols / 64;
-    const uint8_t* base = W + (((size_t)q * S8 * 4 + rr) * 64 + l * 8) * ES;
-    const size_t sstep = (size_t)4 * 64 * ES;
-    float acc = 0.0f;
-    // blocks of 8 steps: the next block's weights are in flight while this
-    // block's chain runs (the chain alone is ~6 cycles a step)
-    constexpr int BS = 8;
-    int s = 0;
-    if (S8 >= BS) {
-        Raw8<DT> cur[BS];
+    if (live) lanes_gemv<DT>(W, rows, cols, s_x, out, ring, bars, ns, err);
+}
+
+// RMSNorm folded into the matvec that consumes it (one activation row):
+// every CTA forms v = x (+ delta), runs the norm's sum of squares (the
+// reference's left-to-right chain, as rmsnorm_kernel) on one thread, and
+// stages v * scale * w in lanes order; CTA 0 also writes the new residual v
+// to x_out (x_out != x: other CTAs read x meanwhile). The warps' weight
+// streams start before the chain. cols % 64 == 0, x / delta 16-byte aligned.
+// float4 of x (and delta, norm weights) a thread of the norm kernel holds:
+// cols <= 4 * kLanesNormVec * blockDim.x (4096 at 128 threads).
+constexpr int kLanesNormVec = 8;
+
+template <int DT>
+__global__ void __launch_bounds__(256) fgemv_lanes_norm_kernel(const uint8_t* __restrict__ W, int rows, int cols,
+                                                               const float* __restrict__ x,
+                                                               const float* __restrict__ delta,
+                                                               const float* __restrict__ nw, float eps,
+                                                               float* __restrict__ x_out, float* __restrict__ out,
+                                                               int ns, uint32_t* err) {
+    extern __shared__ __align__(128) float s_x[];  // [cols] staged, [cols] v, rings, barriers
+    float* s_v = s_x + cols;
+    __shared__ float s_scale;
+    const int warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    uint8_t* rings = reinterpret_cast<uint8_t*>(s_x) + (size_t)cols * 8;
+    uint8_t* ring = rings + (size_t)warp * lanes_ring_bytes<DT>(ns);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rings + (size_t)warps * lanes_ring_bytes<DT>(ns)) + warp * ns;
+    HALE_LANES_MARK(0);
+    // x, delta and the norm weights are requested before the weight streams,
+    // so they are not queued behind them (cols / 4 <= kLanesNormVec * blockDim.x)
+    float4 xv[kLanesNormVec], dv[kLanesNormVec], wv[kLanesNormVec];
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const float4* d4 = reinterpret_cast<const float4*>(delta);
+    const float4* w4 = reinterpret_cast<const float4*>(nw);
 #pragma unroll
-        for (int u = 0; u < BS; u++) raw8_load<DT>(base + (size_t)u * sstep, cur[u]);
-        for (; s + BS <= S8; s += BS) {
-            Raw8<DT> nxt[BS];
-            const int ns = s + BS + BS <= S8 ? s + BS : s;  // the last block reloads itself (unused)
-#pragma unroll
-            for (int u = 0; u < BS; u++) raw8_load<DT>(base + (size_t)(ns + u) * sstep, nxt[u]);
-#pragma unroll
-            for (int u = 0; u < BS; u++) {
-                float w[8];
-                raw8_decode<DT>(cur[u], w);
-                const float4 xa = s_x4[((s + u) << 4) + l], xb = s_x4[((s + u) << 4) + 8 + l];
-                acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
-                acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
-                acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
-                acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
-            }
-#pragma unroll
-            for (int u = 0; u < BS; u++) cur[u] = nxt[u];
+    for (int j = 0; j < kLanesNormVec; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols / 4) {
+            xv[j] = x4[i];
+            if (delta) dv[j] = d4[i];
+            wv[j] = w4[i];
         }
     }
-    for (; s < S8; s++) {
-        float w[8];
-        load8<DT>(base + (size_t)s * sstep, w);
-        const float4 xa = s_x4[(s << 4) + l], xb = s_x4[(s << 4) + 8 + l];
-        acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
-        acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
-        acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
-        acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
+    const bool live = lanes_start<DT>(W, rows, cols, ring, bars, ns);
+    float* s_w = s_x;  // the norm weights wait in s_x until the staging reads them
+#pragma unroll
+    for (int j = 0; j < kLanesNormVec; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols / 4) {
+            float4 v = xv[j];
+            if (delta) {
+                v = make_float4(fadd(v.x, dv[j].x), fadd(v.y, dv[j].y), fadd(v.z, dv[j].z), fadd(v.w, dv[j].w));
+                if (blockIdx.x == 0) reinterpret_cast<float4*>(x_out)[i] = v;
+            }
+            reinterpret_cast<float4*>(s_v)[i] = v;
+            reinterpret_cast<float4*>(s_w)[i] = wv[j];
+        }
     }
-    const float s1 = fadd(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
-    const float p = fadd(s1, __shfl_down_sync(0xffffffffu, s1, 1, 8));
-    const float r = fadd(p, __shfl_down_sync(0xffffffffu, p, 2, 8));
-    const int row = q * 4 + rr;
-    if (l == 0 && row < rows) out[row] = fadd(r, -0.0f);
+    __syncthreads();
+    HALE_LANES_MARK(1);
+    if (threadIdx.x == 0) {
+        // RmsNorm::forward (norm.rs): sum of squares left to right from -0
+        // (the squares are independent of the chain)
+        float s = -0.0f;
+        const float4* v4 = reinterpret_cast<const float4*>(s_v);
+#pragma unroll 8
+        for (int i = 0; i < cols / 4; i++) {
+            const float4 v = v4[i];
+            s = fadd(fadd(fadd(fadd(s, fmul(v.x, v.x)), fmul(v.y, v.y)), fmul(v.z, v.z)), fmul(v.w, v.w));
+        }
+        s_scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)cols), eps)));
+    }
+    __syncthreads();
+    HALE_LANES_MARK(2);
+    const float scale = s_scale;
+    // normed values into registers first: s_x holds the norm weights until
+    // every thread has read its own
+    float nv[4 * kLanesNormVec];
+#pragma unroll
+    for (int j = 0; j < 4 * kLanesNormVec; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols) nv[j] = fmul(fmul(s_v[i], scale), s_w[i]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 4 * kLanesNormVec; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols) s_x[lanes_x_slot(i)] = nv[j];
+    }
+    __syncthreads();
+    HALE_LANES_MARK(3);
+    if (live) lanes_gemv<DT>(W, rows, cols, s_x, out, ring, bars, ns, err);
+    HALE_LANES_MARK(4);
 }
 
 // The same matvec for n activation rows, NB per CTA (blockIdx.y = chunk):

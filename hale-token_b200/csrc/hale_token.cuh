@@ -47,6 +47,7 @@ constexpr int kTokDownRows = 8;            // output rows per down unit
 constexpr int kTokChunk = 8;               // blocks per gate/up bulk copy
 constexpr uint32_t kTokPrefetch = 16384;   // bytes per L2 prefetch
 constexpr int kTokDownLoads = 8;           // down products per thread with loads in flight
+constexpr int kTokNormVec = 4;             // float4 of x per thread with the norm folded in (H <= 4096)
 
 struct TokenArgs {
     const void* router;        // [E, H] f32 / f16 / bf16, row-major
@@ -66,6 +67,13 @@ struct TokenArgs {
     unsigned* bar;             // [3] grid barrier counters: 0 at entry, 0 again at exit
     int rpc;                   // router rows per CTA: ceil(E / gridDim.x), <= 32
     int prefetch_all;          // prefetch whole expert records (CTAs take several gate/up units)
+    // optional RMSNorm in front of the layer (norm_w non-null): the layer's
+    // input is rmsnorm(x + delta) with weights norm_w, and CTA 0 writes the
+    // new residual x + delta to x_out (not x: every CTA reads x)
+    const float* delta;
+    const float* norm_w;
+    float eps;
+    float* x_out;
     uint32_t* err;
 };
 
@@ -207,9 +215,38 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(TokenArgs a) 
 
     HALE_TOK_MARK(0);
     // ---- A: x, router rows, q8 of x, logits ---------------------------------
+    float4 nwv[kTokNormVec];  // this thread's norm weights (norm_w only)
     {
         const float4* x4 = reinterpret_cast<const float4*>(a.x);
-        for (int i = tid; i < H / 4; i += kTokThreads) reinterpret_cast<float4*>(xf)[i] = __ldg(x4 + i);
+        if (a.norm_w) {
+            // v = x + delta (the residual add folded into RmsNorm's caller);
+            // x, delta and the norm weights requested together, before the
+            // router rows (H / 4 <= kTokNormVec * kTokThreads)
+            const float4* d4 = reinterpret_cast<const float4*>(a.delta);
+            const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+            float4 xv[kTokNormVec], dv[kTokNormVec];
+#pragma unroll
+            for (int j = 0; j < kTokNormVec; j++) {
+                const int i = tid + j * kTokThreads;
+                if (i < H / 4) {
+                    xv[j] = __ldg(x4 + i);
+                    dv[j] = __ldg(d4 + i);
+                    nwv[j] = __ldg(w4 + i);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kTokNormVec; j++) {
+                const int i = tid + j * kTokThreads;
+                if (i < H / 4) {
+                    const float4 v = make_float4(fadd(xv[j].x, dv[j].x), fadd(xv[j].y, dv[j].y),
+                                                 fadd(xv[j].z, dv[j].z), fadd(xv[j].w, dv[j].w));
+                    reinterpret_cast<float4*>(xf)[i] = v;
+                    if (c == 0) reinterpret_cast<float4*>(a.x_out)[i] = v;
+                }
+            }
+        } else {
+            for (int i = tid; i < H / 4; i += kTokThreads) reinterpret_cast<float4*>(xf)[i] = __ldg(x4 + i);
+        }
         const int rowv = H * wb / 16;
         for (int r = 0; r < a.rpc; r++) {
             const int e = c + G * r;
@@ -221,6 +258,35 @@ __global__ void __launch_bounds__(kTokThreads, 2) moe_token_kernel(TokenArgs a) 
         }
     }
     __syncthreads();
+    if (a.norm_w) {
+        // RmsNorm::forward (norm.rs): the sum of squares left to right from
+        // -0 on one thread (each square formed as the chain reaches it), then
+        // x = v * (1 / sqrt(ss / H + eps)) * w
+        __shared__ float s_scale;
+        if (tid == 0) {
+            float ss = -0.0f;
+            const float4* v4 = reinterpret_cast<const float4*>(xf);
+#pragma unroll 8
+            for (int i = 0; i < H / 4; i++) {
+                const float4 v = v4[i];
+                ss = fadd(fadd(fadd(fadd(ss, fmul(v.x, v.x)), fmul(v.y, v.y)), fmul(v.z, v.z)), fmul(v.w, v.w));
+            }
+            s_scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)H), a.eps)));
+        }
+        __syncthreads();
+        const float scale = s_scale;
+#pragma unroll
+        for (int j = 0; j < kTokNormVec; j++) {
+            const int i = tid + j * kTokThreads;
+            if (i < H / 4) {
+                float4* p4 = reinterpret_cast<float4*>(xf) + i;
+                const float4 v = *p4;
+                *p4 = make_float4(fmul(fmul(v.x, scale), nwv[j].x), fmul(fmul(v.y, scale), nwv[j].y),
+                                  fmul(fmul(v.z, scale), nwv[j].z), fmul(fmul(v.w, scale), nwv[j].w));
+            }
+        }
+        __syncthreads();
+    }
     HALE_TOK_MARK(1);
     // Q8Activations::quantize (quant.rs:77-93), each CTA for its own use, on
     // warps 2.. first so that warp 0 starts the logit chains at once
