@@ -57,7 +57,7 @@ __host__ __device__ inline int split_ps(int G, int ch) {
 }
 
 struct SplitPlan {
-    int q, k, e, v, pr, total;  // float offsets in dynamic shared memory
+    int q, k, e, v, pr, rt, total;  // float offsets in dynamic shared memory
 };
 
 __host__ __device__ inline SplitPlan split_plan(int G, int hd) {
@@ -68,15 +68,16 @@ __host__ __device__ inline SplitPlan split_plan(int G, int hd) {
     p.e = p.k + kSplitPB * (hd + 4);
     p.v = p.e + (G * split_es(G) > kSplitPC ? G * split_es(G) : kSplitPC);
     p.pr = p.v + ch * kSplitD;
-    p.total = p.pr + G * kSplitD * (split_ps(G, ch) + 4);
+    p.rt = p.pr + G * kSplitD * (split_ps(G, ch) + 4);  // q / k norm weights, cos, sin at the position
+    p.total = p.rt + 3 * hd;
     return p;
 }
 
 struct SplitArgs {
     const float* qkv;         // row: [nh | nkv | nkv] heads of hd (q after RoPE)
     int nh, nkv, hd;
-    const float* kcache;      // this layer's caches: [sequence][position][nkv * hd]
-    const float* vcache;
+    float* kcache;            // this layer's caches: [sequence][position][nkv * hd]
+    float* vcache;
     const uint32_t* rows;     // [3]: token, position, sequence
     size_t seq_stride;
     float scale;
@@ -86,8 +87,49 @@ struct SplitArgs {
     float* ctx;               // [nh * hd]
     unsigned* bar;            // [3] grid barrier counters, 0 at entry and exit
     L2Prefetch pf;            // the next kernels' weights, pulled into L2 at the start
+    // the row's q/k head RMSNorm + RoPE and the K/V cache append folded in
+    // (qk_rope_kernel's work; rope non-zero): q heads are normed and rotated in
+    // shared memory by every score unit of their group, the new position's k
+    // and v rows by the unit that holds that position
+    int rope;
+    const float* q_norm;      // nullable: no q/k head norm
+    const float* k_norm;
+    float eps;
+    const float* rope_cos;    // [max_len][hd / 2]
+    const float* rope_sin;
     uint32_t* err;
 };
+
+// In-place head RMSNorm (when w) and RoPE of one head in shared memory, by one
+// warp, as qk_rope_kernel: s = sum x_i^2 left to right from -0 (lane 0),
+// x_i *= scale * w_i; then a' = a c - b s, b' = b c + a s on (i, i + hd/2).
+__device__ __forceinline__ void split_head_rope(float* x, int hd, const float* w, float eps, const float* c,
+                                                const float* sn, int lane) {
+    const int half = hd / 2;
+    if (w) {
+        float scale = 0.0f;
+        if (lane == 0) {
+            float s = -0.0f;
+            const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 8
+            for (int i = 0; i < hd / 4; i++) {
+                const float4 v = x4[i];
+                s = fadd(fadd(fadd(fadd(s, fmul(v.x, v.x)), fmul(v.y, v.y)), fmul(v.z, v.z)), fmul(v.w, v.w));
+            }
+            scale = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(s, (float)hd), eps)));
+        }
+        scale = __shfl_sync(0xffffffffu, scale, 0);
+        __syncwarp();
+        for (int i = lane; i < hd; i += 32) x[i] = fmul(x[i], fmul(scale, w[i]));
+        __syncwarp();
+    }
+    for (int i = lane; i < half; i += 32) {
+        const float av = x[i], bv = x[half + i];
+        x[i] = fsub(fmul(av, c[i]), fmul(bv, sn[i]));
+        x[half + i] = fadd(fmul(bv, c[i]), fmul(av, sn[i]));
+    }
+    __syncwarp();
+}
 
 #ifdef __CUDACC__
 __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
@@ -105,11 +147,28 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
     float* se = s_split + P.e;
     float* sv = s_split + P.v;
     float* spr = s_split + P.pr;
+    float* s_qn = s_split + P.rt;     // [hd]
+    float* s_kn = s_qn + hd;          // [hd]
+    float* s_rc = s_kn + hd;          // [hd / 2]
+    float* s_rs = s_rc + hd / 2;      // [hd / 2]
     const int CH = split_chunk(G), ES = split_es(G), kp = hd + 4;
     if (tid < 32) s_tab[tid] = kExp2TabDev[tid];
     const float* qrow = a.qkv;
     const int npb = (seq + kSplitPB - 1) / kSplitPB;
     l2_prefetch_share(a.pf, blockIdx.x, gridDim.x);
+    if (a.rope) {
+        // the head norms' weights and the position's rotation, for every unit
+        // (visible after the first unit's CTA barrier)
+        const int half = hd / 2, pos = seq - 1;
+        for (int i = tid; i < hd; i += 256) {
+            s_qn[i] = a.q_norm ? a.q_norm[i] : 0.0f;
+            s_kn[i] = a.k_norm ? a.k_norm[i] : 0.0f;
+        }
+        for (int i = tid; i < half; i += 256) {
+            s_rc[i] = a.rope_cos[(size_t)pos * half + i];
+            s_rs[i] = a.rope_sin[(size_t)pos * half + i];
+        }
+    }
     HALE_SPLIT_MARK(0);
 
     // ---- S: score chains ------------------------------------------------------
@@ -117,13 +176,39 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
         const int h = u / npb, pb = u - h * npb;
         const int t0 = pb * kSplitPB, here = min(kSplitPB, seq - t0);
         const float* kb = a.kcache + sbase + (size_t)h * hd;
-        for (int j = tid; j < here * q4n; j += 256) {
+        // with the rope folded in, the row's own position (seq - 1, in the
+        // last unit) is not in the cache yet: it is formed below
+        const int cached = (a.rope && pb == npb - 1) ? here - 1 : here;
+        for (int j = tid; j < cached * q4n; j += 256) {
             const int tt = j / q4n, c4 = j - tt * q4n;
             cp_async16(sk + tt * kp + 4 * c4, kb + (size_t)(t0 + tt) * kvd + 4 * c4);
         }
         cp_async_commit();
         for (int j = tid; j < G * q4n; j += 256)
             reinterpret_cast<float4*>(sq)[j] = reinterpret_cast<const float4*>(qrow + (size_t)h * G * hd)[j];
+        if (a.rope) {
+            // this kv head's new k row goes to the stage (and the cache), its v
+            // row to the cache, on a warp with no q head if there is one
+            const int pos = seq - 1, kw = G < 8 ? G : 7;
+            float* kr = sk + (here - 1) * kp;
+            if (cached < here && warp == kw) {
+                const float* kraw = qrow + (size_t)(nh + h) * hd;
+                const float* vraw = qrow + (size_t)(nh + nkv + h) * hd;
+                float* vdst = a.vcache + sbase + (size_t)h * hd + (size_t)pos * kvd;
+                for (int i = lane; i < hd; i += 32) {
+                    kr[i] = kraw[i];
+                    vdst[i] = vraw[i];
+                }
+            }
+            __syncthreads();  // q, the k row and the tables staged
+            for (int g = warp; g < G; g += 8)
+                split_head_rope(sq + g * hd, hd, a.q_norm ? s_qn : nullptr, a.eps, s_rc, s_rs, lane);
+            if (cached < here && warp == kw) {
+                split_head_rope(kr, hd, a.k_norm ? s_kn : nullptr, a.eps, s_rc, s_rs, lane);
+                float* kdst = a.kcache + sbase + (size_t)h * hd + (size_t)pos * kvd;
+                for (int i = lane; i < hd; i += 32) kdst[i] = kr[i];
+            }
+        }
         cp_async_wait<0>();
         __syncthreads();
         for (int g = warp; g < G; g += 8) {

@@ -2831,13 +2831,16 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
             if ((r = check_launch(ctx, "rmsnorm"))) return r;
             if ((r = hale_matrix_matvec(ctx, ly.qkv, d->normed, n, d->qkv, nullptr, stream))) return r;
         }
-        {
-            ProfScope ps_(ctx, "qk_rope", st);
-            qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
-                d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos, d->rope_sin,
-                d->d_rows, kc, vc, d->seq_stride);
+        // one row: attn_split_kernel does this itself
+        if (!(n == 1 && d->split)) {
+            {
+                ProfScope ps_(ctx, "qk_rope", st);
+                qk_rope_kernel<<<dim3(d->nh + 2 * d->nkv, n), 32, (size_t)d->hd * 4, st>>>(
+                    d->qkv, (int)d->nh, (int)d->nkv, (int)d->hd, ly.q_norm, ly.k_norm, d->eps, d->rope_cos,
+                    d->rope_sin, d->d_rows, kc, vc, d->seq_stride);
+            }
+            if ((r = check_launch(ctx, "qk_rope"))) return r;
         }
-        if ((r = check_launch(ctx, "qk_rope"))) return r;
         {
             ProfScope ps_(ctx, "attention", st);
             if (n == 1 && d->split) {
@@ -2858,6 +2861,12 @@ static hale_status decoder_enqueue(hale_ctx* ctx, hale_decoder* d, uint32_t n, f
                 sa.ctx = d->attn;
                 sa.bar = d->split_bar;
                 sa.pf = l2_ranges(ly.o->data, ly.o->bytes, nullptr, 0);
+                sa.rope = 1;
+                sa.q_norm = ly.q_norm;
+                sa.k_norm = ly.k_norm;
+                sa.eps = d->eps;
+                sa.rope_cos = d->rope_cos;
+                sa.rope_sin = d->rope_sin;
                 sa.err = ctx->d_err;
                 attn_split_kernel<<<d->split_grid, 256, d->split_smem, st>>>(sa);
             } else if (d->gqa) {
