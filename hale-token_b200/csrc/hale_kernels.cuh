@@ -631,6 +631,11 @@ __host__ __device__ inline int router_slot_bytes(int wbytes) {
     return kRouterET * (kRouterCH + kRouterPad) * wbytes + kRouterTT * (kRouterCH + kRouterPad) * 4;
 }
 
+// Phase marks for timing probes built from this header; empty in the library.
+#ifndef HALE_ROUTER_MARK
+#define HALE_ROUTER_MARK(i)
+#endif
+
 template <int DT>
 __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -647,6 +652,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const int full = a.H / 8;
     constexpr int wb = DT == 0 ? 4 : 2;
     if (tid < 32) s_tab[tid] = kExp2TabDev[tid];  // exp table for the tail (read after barriers)
+    HALE_ROUTER_MARK(0);
     float acc = 0.0f;
     if (a.staged) {
         // ring of column chunks [8 router rows][4 token rows]; with up to
@@ -720,12 +726,14 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             tail = fadd(tail, fmul(load_w<DT>(a.w, (size_t)e * a.H + c), xt[c]));
         a.logits[(size_t)t * a.E + e] = fadd(r, tail);
     }
+    HALE_ROUTER_MARK(1);
     __threadfence();
     __syncthreads();
     if (tid == 0) s_flag = (atomicAdd(&a.tile_cnt[blockIdx.x], 1u) == gridDim.y - 1) ? 1u : 0u;
     __syncthreads();
     if (!s_flag) return;
     __threadfence();
+    HALE_ROUTER_MARK(2);
 
     // ---- last CTA of this token tile: softmax, top-k, quantize ----------
     // warps 0 .. kRouterTT-1: softmax and top-k of one token each; the other
@@ -821,6 +829,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         }
         __syncwarp();
     }
+    HALE_ROUTER_MARK(3);
     if (gridDim.x == 1) {
         // one token tile: this CTA is also the last of the grid, and its own
         // writes are visible to all its threads after the barrier
@@ -843,6 +852,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     }
 
     // ---- last CTA of the grid: group routes by expert ----------------------
+    HALE_ROUTER_MARK(4);
     const int R = a.M * a.k;
     for (int i = tid; i < a.E; i += blockDim.x) s_cnt[i] = 0;
     __syncthreads();
@@ -892,6 +902,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         a.elist[pos] = i;
     }
     if (tid == 0) *a.grid_cnt = 0u;
+    HALE_ROUTER_MARK(5);
 }
 
 // ---------------------------------------------------------------------------
