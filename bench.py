@@ -449,11 +449,22 @@ def decode_block(hale, fmt, ctx, steps, warmup):
     try:
         b1 = decode_measure(hale, ctx, dec, shape, bpt, 1, prompt, steps, warmup)
         b16 = decode_measure(hale, ctx, dec, shape, bpt, 16, prompt, steps, warmup, seq0=1)
+        # generate() through the public call: a fresh 512-token prompt, the
+        # reference's default SamplingParams (0.7 / 0.9 / 40, seed 42)
+        n_new = 16
+        ptoks = np.random.default_rng(SEED + 99).integers(0, shape["vocab"], prompt).tolist()
+        toks, pre_ms, dec_ms = dec.generate(ptoks, hale.SamplingParams(0.7, 0.9, 40, 1.0), 42, n_new)
+        ctx.check()
+        gen = {"prompt_tokens": prompt, "generated_tokens": len(toks), "prefill_ms": pre_ms, "decode_ms": dec_ms,
+               "prefill_tok_s": prompt / (pre_ms / 1e3) if pre_ms > 0 else None,
+               "decode_tok_s": (len(toks) - 1) / (dec_ms / 1e3) if dec_ms > 0 and len(toks) > 1 else None,
+               "timing": "hale_decoder_generate's CUDA events (GenerationStats: decode rate excludes the first "
+                         "token); each round samples on the device and reads the token back for the stop check"}
     finally:
         dec.close()
         del pool
     return {"metric": "decode_tok_s_full_model", "unit": "tok/s",
-            "config": dict(workload="qwen3_30b_a3b_decode", **shape), "b1": b1, "b16": b16}
+            "config": dict(workload="qwen3_30b_a3b_decode", **shape), "b1": b1, "b16": b16, "generate": gen}
 
 
 def decode_ep_block(hale, fmt, ctx, world, rank, uid, barrier, max_over_ranks, layers=4, global_batch=32,

@@ -128,6 +128,7 @@ SIGNATURES = {
     "hale_decoder_create_batched": (I32, [P, C.POINTER(DecoderDesc), C.POINTER(DecoderLayer), P, U32, U32, U32,
                                          C.POINTER(P)]),
     "hale_decoder_step": (I32, [P, P, P, P, P, U32, P, I32, P, P]),
+    "hale_decoder_generate": (I32, [P, P, P, U32, P, U64, U32, P, U32, P, P, P, P, P]),
     "hale_lm_head": (I32, [P, P, P, U32, P, P]),
     "hale_sample": (I32, [P, P, U32, U32, C.POINTER(SamplingParams), P, P, U32, P, P]),
     "hale_expf_host": (None, [P, P, U64]),
@@ -474,6 +475,20 @@ class Decoder:
         self.ctx.call("hale_decoder_step", self.ctx.h, self.h, t.ctypes.data, p.ctypes.data,
                       None if sq is None else sq.ctypes.data, int(t.size), ptr(logits), int(bool(last_logits_only)),
                       ptr(hidden), _stream(stream))
+
+    def generate(self, prompt, params, seed, max_new_tokens, stop_tokens=(), stream=None):
+        """hale_decoder_generate (generate(), generator.rs:55-94): prompt ->
+        (new token ids, prefill ms, decode ms)."""
+        import numpy as np
+        pr = np.ascontiguousarray(prompt, dtype=np.uint32)
+        stops = np.ascontiguousarray(stop_tokens, dtype=np.uint32)
+        out = np.zeros(max(int(max_new_tokens), 1), dtype=np.uint32)
+        n = C.c_uint32()
+        pms, dms = C.c_float(), C.c_float()
+        self.ctx.call("hale_decoder_generate", self.ctx.h, self.h, pr.ctypes.data, int(pr.size), C.byref(params),
+                      int(seed), int(max_new_tokens), stops.ctypes.data if stops.size else None, int(stops.size),
+                      out.ctypes.data, C.byref(n), C.byref(pms), C.byref(dms), _stream(stream))
+        return out[: n.value].tolist(), pms.value, dms.value
 
     def set_comm(self, comm):
         """hale_decoder_set_comm: MoE layers expert-parallel over `comm` (this

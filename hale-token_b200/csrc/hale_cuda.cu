@@ -2490,6 +2490,15 @@ struct hale_decoder {
     int gc_one = 1, gc_batch = 1;
     int gqa_cap[9] = {0};
     size_t gqa_smem[9] = {0};
+    // hale_decoder_generate's buffers, made on its first call: logits [V],
+    // sampler state, sampled token, seen ids [max_len]; the token's pinned
+    // host copy; events around prefill and decode
+    float* gen_logits = nullptr;
+    uint64_t* gen_rng = nullptr;
+    int32_t* gen_tok = nullptr;
+    int32_t* gen_seen = nullptr;
+    int32_t* h_tok = nullptr;
+    cudaEvent_t gen_ev[3] = {nullptr, nullptr, nullptr};
     // single-row attention over the whole GPU (attn_split_kernel)
     bool split = false;
     int split_grid = 0, split_npm = 0;
@@ -2507,6 +2516,9 @@ extern "C" void hale_decoder_destroy(hale_decoder* d) {
     if (d->cap) cudaStreamDestroy(d->cap);
     if (d->ev_copied) cudaEventDestroy(d->ev_copied);
     if (d->h_rows) cudaFreeHost(d->h_rows);
+    if (d->h_tok) cudaFreeHost(d->h_tok);
+    for (cudaEvent_t e : d->gen_ev)
+        if (e) cudaEventDestroy(e);
     for (auto& ly : d->layers)
         for (hale_matrix* m : {ly.qkv, ly.o, ly.gate, ly.up, ly.down})
             if (m) hale_matrix_destroy(m);
@@ -3193,6 +3205,88 @@ static hale_status noalloc_scratch(int device, uint8_t** out) {
                     device, cudaGetErrorString(e));
     addr[device] = static_cast<uint8_t*>(p);
     *out = static_cast<uint8_t*>(p);
+    return HALE_OK;
+}
+
+
+// generate() (src/generate/generator.rs:55-94): the prompt prefilled as
+// steps of up to max_batch rows (the last one computing only its last row's
+// logits), then Sampler::sample on the device logits and a one-row step per
+// token. Each round reads the sampled token back for the stop check, as the
+// reference's loop checks it on the host.
+extern "C" hale_status hale_decoder_generate(hale_ctx* ctx, hale_decoder* d, const uint32_t* prompt,
+                                             uint32_t n_prompt, const hale_sampling_params* params, uint64_t seed,
+                                             uint32_t max_new_tokens, const uint32_t* stop_tokens, uint32_t n_stop,
+                                             uint32_t* out_tokens, uint32_t* n_out, float* prefill_ms,
+                                             float* decode_ms, void* stream) {
+    if (!ctx || !d || d->ctx != ctx) return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_generate: bad handle");
+    if (!prompt || n_prompt == 0 || !params || !out_tokens || !n_out || (n_stop && !stop_tokens))
+        return fail(ctx, HALE_E_INVALID_ARGUMENT, "hale_decoder_generate: NULL argument or empty prompt");
+    *n_out = 0;
+    if (d->comm)
+        return fail(ctx, HALE_E_UNSUPPORTED,
+                    "hale_decoder_generate: an expert-parallel decoder steps in lockstep with its peers; drive it "
+                    "with hale_decoder_step");
+    const uint64_t needed = (uint64_t)n_prompt + max_new_tokens;
+    if (needed > d->max_len)
+        return fail(ctx, HALE_E_CONTEXT_OVERFLOW, "prompt + new tokens (%llu) exceed the KV cache (%u positions)",
+                    (unsigned long long)needed, d->max_len);
+    if (max_new_tokens == 0) return HALE_OK;
+    CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+    cudaStream_t st = S(stream);
+    hale_status r;
+    if (!d->gen_logits) {
+        if ((r = dec_alloc(ctx, d, (size_t)d->V * 4, reinterpret_cast<void**>(&d->gen_logits))) ||
+            (r = dec_alloc(ctx, d, 8, reinterpret_cast<void**>(&d->gen_rng))) ||
+            (r = dec_alloc(ctx, d, 4, reinterpret_cast<void**>(&d->gen_tok))) ||
+            (r = dec_alloc(ctx, d, (size_t)d->max_len * 4, reinterpret_cast<void**>(&d->gen_seen))))
+            return r;
+        if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_tok), 4, cudaHostAllocDefault) != cudaSuccess)
+            return fail(ctx, HALE_E_OUT_OF_MEMORY, "hale_decoder_generate: cannot allocate a pinned token slot");
+        for (cudaEvent_t& e : d->gen_ev) CUDA_TRY(ctx, cudaEventCreate(&e));
+    }
+    // XorShift64 state seed.max(1) (sampler.rs:131-133); seen ids = the
+    // sequence so far (only the repetition penalty reads them)
+    const uint64_t s0 = seed > 1 ? seed : 1;
+    CUDA_TRY(ctx, cudaMemcpyAsync(d->gen_rng, &s0, 8, cudaMemcpyHostToDevice, st));
+    const bool penalty = params->repetition_penalty != 1.0f;
+    if (penalty) {
+        std::vector<int32_t> ids(prompt, prompt + n_prompt);
+        CUDA_TRY(ctx, cudaMemcpyAsync(d->gen_seen, ids.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st));
+        CUDA_TRY(ctx, cudaStreamSynchronize(st));  // ids leaves scope
+    }
+    CUDA_TRY(ctx, cudaEventRecord(d->gen_ev[0], st));
+    std::vector<uint32_t> pos(d->max_batch);
+    for (uint32_t b = 0; b < n_prompt; b += d->max_batch) {
+        const uint32_t n = std::min(d->max_batch, n_prompt - b);
+        for (uint32_t i = 0; i < n; i++) pos[i] = b + i;
+        const bool last = b + n == n_prompt;
+        if ((r = hale_decoder_step(ctx, d, prompt + b, pos.data(), nullptr, n, last ? d->gen_logits : nullptr, 1,
+                                   nullptr, stream)))
+            return r;
+    }
+    CUDA_TRY(ctx, cudaEventRecord(d->gen_ev[1], st));
+    uint32_t count = 0;
+    for (uint32_t step = 0; step < max_new_tokens; step++) {
+        if ((r = hale_sample(ctx, d->gen_logits, 1, d->V, params, d->gen_rng, penalty ? d->gen_seen : nullptr,
+                             penalty ? n_prompt + step : 0, d->gen_tok, stream)))
+            return r;
+        CUDA_TRY(ctx, cudaMemcpyAsync(d->h_tok, d->gen_tok, 4, cudaMemcpyDeviceToHost, st));
+        CUDA_TRY(ctx, cudaStreamSynchronize(st));
+        const uint32_t tok = (uint32_t)*d->h_tok;
+        out_tokens[count++] = tok;
+        bool stop = step + 1 == max_new_tokens;
+        for (uint32_t i = 0; i < n_stop && !stop; i++) stop = stop_tokens[i] == tok;
+        if (stop) break;
+        if (penalty)
+            CUDA_TRY(ctx, cudaMemcpyAsync(d->gen_seen + n_prompt + step, d->gen_tok, 4, cudaMemcpyDeviceToDevice, st));
+        if ((r = hale_decoder_forward(ctx, d, tok, n_prompt + step, d->gen_logits, nullptr, stream))) return r;
+    }
+    CUDA_TRY(ctx, cudaEventRecord(d->gen_ev[2], st));
+    CUDA_TRY(ctx, cudaEventSynchronize(d->gen_ev[2]));
+    *n_out = count;
+    if (prefill_ms) CUDA_TRY(ctx, cudaEventElapsedTime(prefill_ms, d->gen_ev[0], d->gen_ev[1]));
+    if (decode_ms) CUDA_TRY(ctx, cudaEventElapsedTime(decode_ms, d->gen_ev[1], d->gen_ev[2]));
     return HALE_OK;
 }
 

@@ -506,6 +506,26 @@ HALE_API hale_status hale_sample(hale_ctx* ctx, const float* logits, uint32_t ba
                         const int32_t* seen_ids, uint32_t n_seen, int32_t* out_tokens,
                         void* stream);
 
+/* generate() (src/generate/generator.rs:55-94) on a decoder: the prompt is
+ * prefilled into sequence 0 from position 0 (steps of up to max_batch rows,
+ * only the last row's logits computed), then each round samples the next
+ * token from the device logits (hale_sample with `params`; the XorShift64
+ * state starts at seed.max(1), sampler.rs:131-133; a repetition penalty
+ * other than 1 sees the prompt and the tokens generated so far), appends it
+ * to out_tokens and, unless it is in stop_tokens or the round is the last,
+ * runs the one-row step for it at the next position. *n_out = tokens
+ * written (<= max_new_tokens). Each round reads the token back to the host
+ * for the stop check, as the reference's loop does. prefill_ms / decode_ms
+ * (nullable): CUDA-event times of the prefill and of the rounds, the split
+ * GenerationStats reports. n_prompt + max_new_tokens beyond the decoder's
+ * positions: HALE_E_CONTEXT_OVERFLOW (HaleError::ContextOverflow). Not for an
+ * expert-parallel decoder (HALE_E_UNSUPPORTED). No reference counterpart for
+ * the timing outputs. */
+HALE_API hale_status hale_decoder_generate(hale_ctx* ctx, hale_decoder* dec, const uint32_t* prompt, uint32_t n_prompt,
+                                           const hale_sampling_params* params, uint64_t seed, uint32_t max_new_tokens,
+                                           const uint32_t* stop_tokens, uint32_t n_stop, uint32_t* out_tokens,
+                                           uint32_t* n_out, float* prefill_ms, float* decode_ms, void* stream);
+
 /* ---- self-checks ----------------------------------------------------------- */
 
 /* The exp used by the device kernels, evaluated on the host from the same

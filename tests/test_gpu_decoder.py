@@ -134,6 +134,62 @@ def test_decoder_greedy_generation_matches_the_oracle(ctx, name):
     dec.close()
 
 
+@pytest.mark.parametrize("name", ["tiny-qwen3-moe", "tiny-mixtral"])
+@pytest.mark.parametrize("max_batch", [1, 4])
+def test_generate_greedy_matches_the_oracle(ctx, name, max_batch):
+    """hale_decoder_generate (generate(), generator.rs:55-94) with greedy
+    sampling: the fixture's prompt prefilled in steps of max_batch rows, then
+    sample -> step on the device; the tokens equal the oracle's greedy run.
+    A stop token ends the output right after it; asking for more positions
+    than the cache holds is ContextOverflow."""
+    d = os.path.join(GOLDEN, name)
+    with open(os.path.join(d, "expected.json")) as f:
+        exp = json.load(f)
+    prompt, n = exp["prompt"], len(exp["greedy_continuation"])
+    om = OM.OracleModel(d, expert_dtype=fmt.Q8_0)
+    want = list(om.greedy(prompt, n))
+    dec = build_decoder(ctx, om, fmt.Q8_0, len(prompt) + n, max_batch=max_batch)
+    greedy = hale.SamplingParams(0.0, 1.0, 0, 1.0)
+    got, prefill_ms, decode_ms = dec.generate(prompt, greedy, 42, n)
+    assert got == want
+    assert prefill_ms > 0 and decode_ms > 0
+    stop = want[2]
+    got_s, _, _ = dec.generate(prompt, greedy, 42, n, stop_tokens=[stop])
+    assert got_s == want[: want.index(stop) + 1]
+    with pytest.raises(hale.HaleError) as ei:
+        dec.generate(prompt, greedy, 42, n + 1)
+    assert ei.value.status == hale.E_CONTEXT_OVERFLOW
+    ctx.check()
+    dec.close()
+
+
+def test_generate_seeded_top_p_matches_the_oracle_loop(ctx):
+    """A seeded temperature / top-k / top-p generation: the device loop's
+    tokens equal the oracle's generate() loop (prefill, then TopPSampler with
+    the same seed -> forward) token for token."""
+    d = os.path.join(GOLDEN, "tiny-qwen3-moe")
+    with open(os.path.join(d, "expected.json")) as f:
+        exp = json.load(f)
+    prompt, n = exp["prompt"], 10
+    om = OM.OracleModel(d, expert_dtype=fmt.Q8_0)
+    cache = om.new_cache(len(prompt) + n)
+    for i, t in enumerate(prompt):
+        logits = om.forward(t, i, cache, want_logits=(i == len(prompt) - 1))
+    sampler = O.Sampler(temperature=0.8, top_p=0.9, top_k=20, seed=7)
+    want = []
+    for step in range(n):
+        tok = sampler.sample(logits)
+        want.append(tok)
+        if step + 1 == n:
+            break
+        logits = om.forward(tok, len(prompt) + step, cache)
+    dec = build_decoder(ctx, om, fmt.Q8_0, len(prompt) + n, max_batch=4)
+    got, _, _ = dec.generate(prompt, hale.SamplingParams(0.8, 0.9, 20, 1.0), 7, n)
+    assert got == want
+    ctx.check()
+    dec.close()
+
+
 def test_decoder_rejects_positions_beyond_its_cache(ctx):
     d = os.path.join(GOLDEN, "tiny-mixtral")
     om = OM.OracleModel(d, expert_dtype=fmt.Q8_0)
