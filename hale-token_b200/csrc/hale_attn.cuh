@@ -357,11 +357,27 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
             // adds its row of them in order (4 per 16-byte load)
             for (int s0 = 0; s0 < here; s0 += PS) {
                 const int n = min(PS, here - s0);
-                if (pc < G * kSplitD)
-                    for (int t = pq; t < n; t += TPC)
-                        spr[pc * PR + t] =
-                            fmul(se[(pc / kSplitD) * ES + s0 + t], sv[(s0 + t) * kSplitD + pc % kSplitD]);
+                if (pc < G * kSplitD) {
+                    // 8 products' operands loaded before any is formed (one
+                    // shared-memory round trip per 8, not per product)
+                    const float* pe = se + (pc / kSplitD) * ES + s0;
+                    const float* pv = sv + s0 * kSplitD + pc % kSplitD;
+                    float* po = spr + pc * PR;
+                    int t = pq;
+                    for (; t + 7 * TPC < n; t += 8 * TPC) {
+                        float ea[8], va[8];
+#pragma unroll
+                        for (int w = 0; w < 8; w++) {
+                            ea[w] = pe[t + w * TPC];
+                            va[w] = pv[(t + w * TPC) * kSplitD];
+                        }
+#pragma unroll
+                        for (int w = 0; w < 8; w++) po[t + w * TPC] = fmul(ea[w], va[w]);
+                    }
+                    for (; t < n; t += TPC) po[t] = fmul(pe[t], pv[t * kSplitD]);
+                }
                 __syncthreads();
+                if (s0 == 0) HALE_SPLIT_MARK(9);
                 if (busy) {
                     const float* row = spr + tid * PR;
                     int t = 0;
@@ -378,6 +394,7 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
                     for (; t < n; t++) c = fadd(c, row[t]);
                 }
                 __syncthreads();
+                if (s0 == 0) HALE_SPLIT_MARK(10);
             }
             __syncthreads();  // se / sv are restaged by the next chunk or unit
             HALE_SPLIT_MARK(8);
