@@ -10,18 +10,20 @@
 // head per CTA at one row, so 32 SMs hold the whole step and each pulls a KV
 // head's cache through one SM. Here every chain keeps its order but the
 // independent ones run on different SMs, in one grid of co-resident CTAs:
-//   S  units (kv head, 32 positions): K rows staged in shared memory, one
-//      thread per (query head of the group, position) runs the score chain;
-//      scores and each unit's per-head maximum go to global scratch
+//   S  units (kv head, 32 positions): K rows staged in shared memory (with
+//      `rope`, the q heads' norms and RoPE done here and the row's new k / v
+//      appended to the cache by the unit holding its position), one thread
+//      per (query head of the group, position) runs the score chain; scores
+//      and each unit's per-head maximum go to global scratch
 //   -- grid barrier --
-//   C  units (kv head, 8 head dims): the maximum of the partial maxima, the
-//      exps, the denominator chains (one thread per head) and p, recomputed by
-//      every unit of the head group (same inputs, same result), then one
-//      thread per (head, dim) runs the context chain over V columns staged in
-//      shared memory.
-// Positions come in chunks of split_chunk(G) (the exps of a chunk in shared
-// memory); with more than one chunk the exps are recomputed for the context
-// pass.
+//   P  one unit per query head: the maximum of the partial maxima, the exps,
+//      the denominator chain on one thread, p_t = e_t / sum written over the
+//      head's scores (positions in chunks of kSplitPC)
+//   -- grid barrier --
+//   C  units (kv head, 8 head dims): p of the group's heads and the V
+//      columns staged in shared memory (chunks of split_chunk(G) positions);
+//      all threads form the products p_t v_td, then one thread per (head,
+//      dim) adds them in position order.
 #pragma once
 
 #include "hale_decoder.cuh"

@@ -13,8 +13,10 @@
 // requested once the previous launch has finished. Here one grid, never
 // larger than the number of CTAs the GPU holds at once (the host sizes it
 // from the occupancy), runs all phases with two grid-wide barriers:
-//   A  every CTA stages x and its router rows in shared memory and
-//      quantizes x for itself; 8-lane groups chain the router logits
+//   A  every CTA stages x and its router rows in shared memory (with
+//      norm_w, x = rmsnorm(x + delta): the residual add and RMSNorm in front
+//      of the layer, the sum of squares on one thread) and quantizes x for
+//      itself; 8-lane groups chain the router logits
 //   -- barrier 1 --
 //   B  every CTA repeats softmax + top-k over the E logits (the same inputs
 //      and operations give the same result everywhere), then issues L2
