@@ -260,6 +260,15 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
     // p_t overwrites s_t in the head's score row (only this unit reads it)
     for (int u = blockIdx.x; u < nh; u += gridDim.x) {
         float* row = a.sc + (size_t)u * a.sc_stride;
+        // the first chunk's scores are requested together with the partial
+        // maxima (one L2 round trip, not two)
+        float v0[8];
+        const int here0 = min(kSplitPC, seq);
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            const int j = w * 256 + tid;
+            if (j < here0) v0[w] = __ldcg(row + j);
+        }
         if (warp == 0) {
             float m = -__int_as_float(0x7f800000);
             for (int i = lane; i < npb; i += 32) m = fmaxf(m, __ldcg(a.pm + (size_t)u * a.npm + i));
@@ -269,22 +278,28 @@ __global__ void __launch_bounds__(256, 1) attn_split_kernel(SplitArgs a) {
         }
         __syncthreads();
         const float m = s_max[0];
-        // exps of positions [t0, t0 + here) into se (scores requested 8 per
-        // thread before any is used)
-        auto exps = [&](int t0, int here) {
-            for (int base = 0; base < here; base += 8 * 256) {
-                float v[8];
+        // exps of positions [t0, t0 + here) into se (a chunk's scores are 8
+        // per thread, all requested before any is used)
+        static_assert(kSplitPC == 8 * 256, "a softmax chunk is 8 scores per thread");
+        auto exps_of = [&](const float (&v)[8], int here) {
 #pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    const int j = base + w * 256 + tid;
-                    if (j < here) v[w] = __ldcg(row + t0 + j);
-                }
-#pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    const int j = base + w * 256 + tid;
-                    if (j < here) se[j] = hale_expf_tab(fsub(v[w], m), s_tab);
-                }
+            for (int w = 0; w < 8; w++) {
+                const int j = w * 256 + tid;
+                if (j < here) se[j] = hale_expf_tab(fsub(v[w], m), s_tab);
             }
+        };
+        auto exps = [&](int t0, int here) {
+            if (t0 == 0) {
+                exps_of(v0, here);
+                return;
+            }
+            float v[8];
+#pragma unroll
+            for (int w = 0; w < 8; w++) {
+                const int j = w * 256 + tid;
+                if (j < here) v[w] = __ldcg(row + t0 + j);
+            }
+            exps_of(v, here);
         };
         const int nch = (seq + kSplitPC - 1) / kSplitPC;
         float sum = 0.0f;  // thread 0: the denominator, t ascending

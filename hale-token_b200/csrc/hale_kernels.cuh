@@ -1259,7 +1259,11 @@ __device__ __forceinline__ bool lanes_start(const uint8_t* __restrict__ W, int r
         for (int i = 0; i < ns; i++) mbar_init(&bars[i], 1);
         fence_mbar_init();
         const uint8_t* wq = W + (size_t)q * 4 * cols * ES;
-        lanes_issue<DT>(wq, S8, ring, bars, ns, 0, min(ns, nst));
+        // the first min(ns, nst) stages are contiguous in the region and in
+        // the ring: one copy on the first stage's barrier
+        const uint32_t first = (uint32_t)(min(ns * kLanesSB, S8) * 4 * 64 * ES);
+        mbar_arrive_expect_tx(&bars[0], first);
+        bulk_g2s(ring, wq, first, &bars[0]);
         if (nst > ns) {
             // the stages the ring cannot hold yet: into L2, for the refills
             const size_t done = (size_t)ns * lanes_stage_bytes<DT>(), total = (size_t)4 * cols * ES;
@@ -1284,18 +1288,47 @@ __device__ __forceinline__ void lanes_gemv(const uint8_t* __restrict__ W, int ro
     const uint8_t* wq = W + (size_t)q * 4 * cols * ES;
     float acc = 0.0f;
     uint32_t ph = 0;
+    const int first = min(ns, nst);  // stages of the first copy (all on bars[0])
     for (int st = 0; st < nst; st++) {
         const int slot = st % ns;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars[slot], (ph >> slot) & 1u, err))) {
-            // copies still in flight get a bounded chance to land
-            for (int s2 = st; s2 < min(st + ns, nst); s2++)
-                mbar_wait(&bars[s2 % ns], (ph >> (s2 % ns)) & 1u, nullptr, 400000000LL);
-            return;
+        if (st == 0 || st >= first) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars[slot], (ph >> slot) & 1u, err))) {
+                // copies still in flight get a bounded chance to land: the
+                // first copy (st 0), else the refills of stages st ..
+                if (st == 0) mbar_wait(&bars[0], 0u, nullptr, 400000000LL);
+                for (int s2 = max(st, first); s2 < min(st + ns, nst); s2++)
+                    mbar_wait(&bars[s2 % ns], (ph >> (s2 % ns)) & 1u, nullptr, 400000000LL);
+                return;
+            }
+            ph ^= 1u << slot;
         }
-        ph ^= 1u << slot;
         if (st == 0) HALE_LANES_MARK(5);
+        if (st == 1) HALE_LANES_MARK(6);
+        if (st == 3) HALE_LANES_MARK(7);
         const uint8_t* sb = ring + (size_t)slot * STB;
         const int groups = min(kLanesSB, S8 - st * kLanesSB);
+        if (groups == kLanesSB) {
+            // a full stage: every group's weights into registers first, so no
+            // add waits on a shared-memory load
+            Raw8<DT> rw[kLanesSB];
+#pragma unroll
+            for (int u = 0; u < kLanesSB; u++) {
+                const uint4* src = reinterpret_cast<const uint4*>(sb + ((u * 4 + rr) * 64 + l * 8) * ES);
+                rw[u].a = src[0];
+                if (DT == 0) rw[u].b = src[1];
+            }
+#pragma unroll
+            for (int u = 0; u < kLanesSB; u++) {
+                const int s = st * kLanesSB + u;
+                float w[8];
+                raw8_decode<DT>(rw[u], w);
+                const float4 xa = s_x4[(s << 4) + l], xb = s_x4[(s << 4) + 8 + l];
+                acc = fadd(acc, fmul(w[0], xa.x)); acc = fadd(acc, fmul(w[1], xa.y));
+                acc = fadd(acc, fmul(w[2], xa.z)); acc = fadd(acc, fmul(w[3], xa.w));
+                acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
+                acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
+            }
+        } else {
 #pragma unroll
         for (int u = 0; u < kLanesSB; u++) {
             if (u < groups) {
@@ -1312,6 +1345,7 @@ __device__ __forceinline__ void lanes_gemv(const uint8_t* __restrict__ W, int ro
                 acc = fadd(acc, fmul(w[4], xb.x)); acc = fadd(acc, fmul(w[5], xb.y));
                 acc = fadd(acc, fmul(w[6], xb.z)); acc = fadd(acc, fmul(w[7], xb.w));
             }
+        }
         }
         __syncwarp();
         if (lane == 0 && st + ns < nst) {
