@@ -96,3 +96,20 @@ def test_device_exp_is_glibc_expf_for_every_float():
             t.join()
         threads.extend(ts)
     assert not bad, bad[:4]
+
+
+def test_null_handles_are_rejected_without_a_device():
+    """Entry points given NULL handles answer HALE_E_INVALID_ARGUMENT (the
+    reference's validation errors) before touching any device."""
+    hale = hale_pkg()
+    lib = hale.lib()
+    n = C.c_uint32()
+    params = hale.SamplingParams(0.0, 1.0, 0, 1.0)
+    prompt = (C.c_uint32 * 2)(1, 2)
+    out = (C.c_uint32 * 4)()
+    st = lib.hale_decoder_generate(None, None, prompt, 2, C.byref(params), 42, 4, None, 0, out, C.byref(n),
+                                   None, None, None)
+    assert st == hale.E_INVALID_ARGUMENT
+    assert lib.hale_decoder_set_comm(None, None) == hale.E_INVALID_ARGUMENT
+    assert lib.hale_pool_set_source(None, None, None) == hale.E_INVALID_ARGUMENT
+    assert lib.hale_moe_forward_ep(None, None, None, None, None, 0, None, None, None, None) == hale.E_INVALID_ARGUMENT
